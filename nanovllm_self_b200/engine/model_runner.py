@@ -1,0 +1,357 @@
+"""Model runner: owns the model, the paged KV pool, input packing, CUDA graphs, sampling.
+
+Reference counterpart: ``nanovllm/engine/model_runner.py:14-579``.  Same contract:
+``run(seqs) -> (token_ids, seq_need_compute_logits)`` where the second list holds the
+batch indices of the sequences that sampled this step.
+
+B200-first differences:
+
+* KV pool layout ``[2, L, num_blocks, kv_heads, block_size, head_dim]`` (one block of
+  one head is a contiguous ``block_size x head_dim`` tile that a kernel can stream);
+  ``num_blocks`` is sized from free HBM when the config says ``-1``;
+* the whole step's integer metadata is packed on the host (numpy, no per-token Python
+  loops) into one pinned buffer and moved with ONE host-to-device copy;
+* decode-only steps replay a CUDA graph captured per batch-size bucket
+  (``[1, 2, 4, 8] + 16k`` up to ``cuda_graph_max_bs``, reference :80) that contains the
+  whole forward *and* the sampler; mixed prefill steps run eagerly;
+* sampled ids come back through one pinned device-to-host copy.
+"""
+from __future__ import annotations
+
+import math
+import os
+
+import numpy as np
+import torch
+
+from ..models.configs import resolve_arch
+from ..models.loader import has_checkpoint, load_safetensors, random_init
+from ..models.qwen3 import Qwen3ForCausalLM
+from ..ops import get_ops
+from ..parallel.state import TPState
+from ..utils.context import Context
+from .block_manager import BlockManager
+from .sequence import Sequence
+
+
+def graph_buckets(max_bs: int) -> list[int]:
+    b = [x for x in (1, 2, 4, 8) if x <= max_bs]
+    b += list(range(16, max_bs + 1, 16))
+    if b[-1] != max_bs:
+        b.append(max_bs)
+    return b
+
+
+class _Packed:
+    """Host-side packed step inputs (int32 segments in one pinned buffer)."""
+    __slots__ = ("T", "B", "W", "S", "n_decode", "offsets", "host", "temps", "top_p", "q_lens", "k_lens",
+                 "need", "max_q", "max_k")
+
+
+class ModelRunner:
+    def __init__(self, config, tp: TPState | None = None, comm=None):
+        self.config = config
+        self.tp = tp or TPState()
+        self.device = torch.device(config.device) if not config.is_cuda else (
+            self.tp.device if self.tp.device.type == "cuda" else torch.device("cuda", torch.cuda.current_device()))
+        self.is_cuda = self.device.type == "cuda"
+        self.arch = resolve_arch(config.model, config.model_path)
+        dtype = config.dtype
+        self.model = Qwen3ForCausalLM(self.arch, self.tp.rank, self.tp.size, dtype=dtype, device=self.device)
+        with torch.inference_mode():
+            if has_checkpoint(config.model_path):
+                load_safetensors(self.model, config.model_path)
+            else:
+                random_init(self.model, seed=config.seed, std=config.init_std)
+        self.ops = get_ops(self.device, config.use_custom_kernels)
+        self.comm = comm
+        max_pos = max(config.max_model_len + 1, 16)
+        self.model.finalize(self.ops, comm, max_position=max(max_pos, self.arch.max_position_embeddings))
+        self.block_size = config.block_size
+        self.max_blocks_per_seq = (config.max_model_len + self.block_size - 1) // self.block_size
+        self.num_blocks = self._decide_num_blocks()
+        self._allocate_kv_cache()
+        self.block_manager = BlockManager(self.num_blocks, self.block_size, config.enable_prefix_cache)
+        self.sample_step = 0
+        self._gen = torch.Generator(device=self.device)
+        self._gen.manual_seed(config.seed)
+        self.graphs: dict = {}
+        self.graph_pool = None
+        self.enable_cuda_graph = bool(self.is_cuda and config.enable_cuda_graph and not config.enforce_eager)
+        self._staging_dev = None
+        self._pinned = None
+        self._out_pinned = None
+        if self.is_cuda:
+            self._alloc_staging()
+        if self.enable_cuda_graph:
+            self.capture_cuda_graphs()
+
+    # ---------------------------------------------------------------- memory
+    def kv_block_bytes(self) -> int:
+        m = self.model
+        elem = torch.empty(0, dtype=self.config.kv_cache_dtype).element_size()
+        per = 2 * m.num_layers * m.num_kv_heads * self.block_size * m.head_dim * elem
+        if self.config.kv_cache_quant_mode == "fp8":
+            per += 2 * m.num_layers * m.num_kv_heads * 4
+        elif self.config.kv_cache_quant_mode == "int8_mock":
+            per += 2 * m.num_layers * m.num_kv_heads * self.block_size * 4
+        return per
+
+    def _activation_reserve(self) -> int:
+        m, c = self.model, self.config
+        t = c.max_num_batched_tokens
+        per_tok = (m.q_size + 2 * m.kv_size) + 2 * m.intermediate + m.intermediate + 4 * m.hidden_size + m.q_size
+        acts = t * per_tok * 2 * 2
+        logits = max(c.max_num_seqs, c.cuda_graph_max_bs) * (m.vocab_end - m.vocab_start) * 4 * 2
+        return acts + logits + (2 << 30)
+
+    def _decide_num_blocks(self) -> int:
+        c = self.config
+        if c.num_blocks > 0:
+            return c.num_blocks
+        if not self.is_cuda:
+            need = c.max_num_seqs * self.max_blocks_per_seq
+            return max(8, min(need, 4096))
+        free, total = torch.cuda.mem_get_info(self.device)
+        used = total - free
+        budget = int(total * c.gpu_memory_utilization) - used - self._activation_reserve()
+        n = max(budget // self.kv_block_bytes(), 0)
+        if self.tp.size > 1:
+            t = torch.tensor([n], dtype=torch.int64, device=self.device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+            n = int(t.item())
+        if n < 2:
+            raise RuntimeError("not enough device memory for the KV cache")
+        return int(n)
+
+    def _allocate_kv_cache(self):
+        m, c = self.model, self.config
+        shape = (2, m.num_layers, self.num_blocks, m.num_kv_heads, self.block_size, m.head_dim)
+        self.kv_cache = torch.zeros(shape, dtype=c.kv_cache_dtype, device=self.device)
+        self.kv_scale_cache = None
+        if c.kv_cache_quant_mode == "fp8":
+            self.kv_scale_cache = torch.ones(2, m.num_layers, self.num_blocks, m.num_kv_heads,
+                                             dtype=torch.float32, device=self.device)
+        elif c.kv_cache_quant_mode == "int8_mock":
+            self.kv_scale_cache = torch.ones(2, m.num_layers, self.num_blocks, m.num_kv_heads, self.block_size,
+                                             dtype=torch.float32, device=self.device)
+        self.kv_layers = [(self.kv_cache[0, i], self.kv_cache[1, i]) for i in range(m.num_layers)]
+        self.kv_scale_layers = None
+        if self.kv_scale_cache is not None:
+            self.kv_scale_layers = [(self.kv_scale_cache[0, i], self.kv_scale_cache[1, i])
+                                    for i in range(m.num_layers)]
+
+    def _alloc_staging(self):
+        c = self.config
+        maxT = c.max_num_batched_tokens + max(c.max_num_seqs, c.cuda_graph_max_bs)
+        maxB = max(c.max_num_seqs, c.cuda_graph_max_bs)
+        n = 3 * maxT + 2 * (maxB + 1) + maxB + maxB * self.max_blocks_per_seq + 2 * maxB + 64
+        self._staging_n = n
+        self._staging_dev = torch.zeros(n, dtype=torch.int32, device=self.device)
+        self._pinned = torch.zeros(n, dtype=torch.int32, pin_memory=True)
+        self._out_pinned = torch.zeros(maxB, dtype=torch.int32, pin_memory=True)
+        self._out_event = torch.cuda.Event()
+
+    # --------------------------------------------------------------- packing
+    def _pack(self, seqs: list[Sequence], pad_to: int | None = None) -> _Packed:
+        """Pack the step: ids, positions, slots, cu_q, ctx_lens, logits idx, block tables, temps."""
+        bs = self.block_size
+        B = len(seqs)
+        Bp = pad_to or B
+        W = self.max_blocks_per_seq if pad_to else max(1, max(len(s.block_table) for s in seqs))
+        q_lens = [s.num_new_tokens for s in seqs]
+        starts = [s.num_cached_tokens for s in seqs]
+        k_lens = [a + b for a, b in zip(starts, q_lens)]
+        T = sum(q_lens)
+        Tp = T + (Bp - B)
+        need = [i for i, s in enumerate(seqs) if s.is_need_logits]
+        S = len(need) if pad_to is None else Bp
+        n_decode = 0
+        for s in seqs:
+            if s.num_new_tokens == 1 and s.is_prefill_done:
+                n_decode += 1
+            else:
+                break
+        # segments
+        offs = {}
+        o = 0
+        for name, n in (("ids", Tp), ("pos", Tp), ("slot", Tp), ("cuq", Bp + 1), ("ctx", Bp), ("lidx", S),
+                        ("bt", Bp * W), ("temp", S), ("topp", S)):
+            offs[name] = (o, n)
+            o += n
+        host = self._pinned.numpy()[:o] if self._pinned is not None else np.zeros(o, dtype=np.int32)
+        ids = host[offs["ids"][0]:offs["ids"][0] + Tp]
+        pos = host[offs["pos"][0]:offs["pos"][0] + Tp]
+        slot = host[offs["slot"][0]:offs["slot"][0] + Tp]
+        if n_decode == B:
+            ids[:B] = [s.token_ids[-1] for s in seqs]
+            p = np.asarray(starts, dtype=np.int64)
+            pos[:B] = p
+            tbl_last = np.asarray([s.block_table[st // bs] for s, st in zip(seqs, starts)], dtype=np.int64)
+            slot[:B] = tbl_last * bs + (p % bs)
+        else:
+            t0 = 0
+            for s, st, ql in zip(seqs, starts, q_lens):
+                ids[t0:t0 + ql] = s.token_ids[st:st + ql]
+                pp = np.arange(st, st + ql, dtype=np.int64)
+                pos[t0:t0 + ql] = pp
+                tbl = np.asarray(s.block_table, dtype=np.int64)
+                slot[t0:t0 + ql] = tbl[pp // bs] * bs + (pp % bs)
+                t0 += ql
+        if Tp > T:
+            ids[T:Tp] = 0
+            pos[T:Tp] = 0
+            slot[T:Tp] = -1
+        cuq = host[offs["cuq"][0]:offs["cuq"][0] + Bp + 1]
+        cuq[0] = 0
+        cuq[1:B + 1] = np.cumsum(q_lens)
+        if Bp > B:
+            cuq[B + 1:] = T + np.arange(1, Bp - B + 1)
+        ctx = host[offs["ctx"][0]:offs["ctx"][0] + Bp]
+        ctx[:B] = k_lens
+        ctx[B:] = 0
+        lidx = host[offs["lidx"][0]:offs["lidx"][0] + S]
+        if pad_to is None:
+            lidx[:] = [int(cuq[i + 1]) - 1 for i in need]
+        else:
+            lidx[:] = np.arange(Bp)
+        bt = host[offs["bt"][0]:offs["bt"][0] + Bp * W].reshape(Bp, W)
+        bt.fill(0)
+        for i, s in enumerate(seqs):
+            bt[i, :len(s.block_table)] = s.block_table
+        tview = host[offs["temp"][0]:offs["temp"][0] + S].view(np.float32)
+        pview = host[offs["topp"][0]:offs["topp"][0] + S].view(np.float32)
+        if pad_to is None:
+            tview[:] = [seqs[i].temperature for i in need]
+            pview[:] = [seqs[i].top_p for i in need]
+        else:
+            tview[:B] = [s.temperature for s in seqs]
+            tview[B:] = 0.0
+            pview[:B] = [s.top_p for s in seqs]
+            pview[B:] = 1.0
+        pk = _Packed()
+        pk.T, pk.B, pk.W, pk.S, pk.n_decode = Tp, Bp, W, S, n_decode if n_decode < B else Bp
+        pk.offsets, pk.host, pk.need = offs, host, need
+        pk.q_lens, pk.k_lens = q_lens + [1] * (Bp - B), k_lens + [0] * (Bp - B)
+        pk.max_q, pk.max_k = max(q_lens), max(k_lens)
+        return pk
+
+    def _to_device(self, pk: _Packed, dev_buf: torch.Tensor | None = None):
+        total = sum(n for _, n in pk.offsets.values())
+        if self.is_cuda:
+            dst = dev_buf if dev_buf is not None else self._staging_dev
+            dst[:total].copy_(self._pinned[:total], non_blocking=True)
+        else:
+            dst = torch.from_numpy(pk.host[:total].copy())
+        v = {k: dst[o:o + n] for k, (o, n) in pk.offsets.items()}
+        ctx = Context(
+            cu_seqlens_q=v["cuq"], context_lens=v["ctx"], slot_mapping=v["slot"],
+            block_tables=v["bt"].view(pk.B, pk.W), logits_indices=v["lidx"],
+            seq_need_compute_logits=None, max_seqlen_q=pk.max_q, max_seqlen_k=pk.max_k,
+            num_decode_seqs=pk.n_decode, num_seqs=pk.B, num_tokens=pk.T,
+            host_q_lens=pk.q_lens, host_k_lens=pk.k_lens)
+        temps = v["temp"].view(torch.float32)
+        topp = v["topp"].view(torch.float32)
+        return v["ids"], v["pos"], ctx, temps, topp
+
+    # ------------------------------------------------------------- execution
+    def _forward_and_sample(self, ids, pos, ctx, temps, topp):
+        logits = self.model.forward(ids, pos, ctx, self.kv_layers, self.kv_scale_layers)
+        if logits.shape[0] == 0:
+            return torch.empty(0, dtype=torch.int32, device=ids.device)
+        return self.sample(logits, temps, topp)
+
+    def sample(self, logits, temps, topp):
+        if self.tp.size > 1 and self.comm is not None:
+            return self.comm.vocab_parallel_sample(logits, temps, topp, self.model, self)
+        return self.ops.sample(logits, temps, topp, seeds=None, step=self._step_tensor(),
+                               batch_greedy_compat=self.config.batch_greedy_compat, generator=self._gen)
+
+    def _step_tensor(self):
+        if not self.is_cuda:
+            return self.sample_step
+        if not hasattr(self, "_step_dev"):
+            self._step_dev = torch.zeros(2, dtype=torch.int64, device=self.device)
+            self._step_dev[0] = self.config.seed
+        return self._step_dev
+
+    @torch.inference_mode()
+    def run(self, seqs: list[Sequence]):
+        if not seqs:
+            return [], []
+        need = [i for i, s in enumerate(seqs) if s.is_need_logits]
+        all_decode = all(s.num_new_tokens == 1 and s.is_prefill_done for s in seqs)
+        graph_bs = None
+        if self.enable_cuda_graph and all_decode and len(seqs) <= self.graph_max_bs:
+            graph_bs = next(b for b in self.graph_bs_list if b >= len(seqs))
+        if graph_bs is not None:
+            toks = self._run_graph(seqs, graph_bs)
+        else:
+            pk = self._pack(seqs)
+            ids, pos, ctx, temps, topp = self._to_device(pk)
+            toks = self._forward_and_sample(ids, pos, ctx, temps, topp)
+            toks = self._fetch(toks, len(need))
+        self.sample_step += 1
+        if self.is_cuda:
+            self._step_dev[1] += 1
+        return toks[:len(need)], need
+
+    def _fetch(self, toks: torch.Tensor, n: int) -> list[int]:
+        if n == 0:
+            return []
+        if not self.is_cuda:
+            return [int(x) for x in toks.tolist()]
+        self._out_pinned[:n].copy_(toks[:n], non_blocking=True)
+        self._out_event.record()
+        self._out_event.synchronize()
+        return self._out_pinned[:n].tolist()
+
+    # ----------------------------------------------------------- cuda graphs
+    @property
+    def graph_max_bs(self) -> int:
+        return min(self.config.cuda_graph_max_bs, self.config.max_num_seqs)
+
+    @torch.inference_mode()
+    def capture_cuda_graphs(self):
+        self.graph_bs_list = graph_buckets(self.graph_max_bs)
+        self._step_tensor()
+        self._graph_buf = torch.zeros(self._staging_n, dtype=torch.int32, device=self.device)
+        dummy_block = 0
+        for bs in reversed(self.graph_bs_list):
+            fake = []
+            for i in range(bs):
+                s = Sequence(-1, [0], None, self.block_size)
+                s.block_table = [dummy_block]
+                s.num_cached_tokens = 0
+                s.num_new_tokens = 1
+                fake.append(s)
+            pk = self._pack(fake, pad_to=bs)
+            # Padding-style dummy rows: write nowhere, attend to nothing.
+            o, n = pk.offsets["slot"]
+            pk.host[o:o + n] = -1
+            o, n = pk.offsets["ctx"]
+            pk.host[o:o + n] = 0
+            ids, pos, ctx, temps, topp = self._to_device(pk, self._graph_buf)
+            for _ in range(2):
+                self._forward_and_sample(ids, pos, ctx, temps, topp)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=self.graph_pool):
+                out = self._forward_and_sample(ids, pos, ctx, temps, topp)
+            if self.graph_pool is None:
+                self.graph_pool = g.pool()
+            self.graphs[bs] = (g, out, pk.offsets)
+            torch.cuda.synchronize(self.device)
+
+    def _run_graph(self, seqs, bs) -> list[int]:
+        g, out, offsets = self.graphs[bs]
+        pk = self._pack(seqs, pad_to=bs)
+        assert pk.offsets == offsets
+        total = sum(n for _, n in offsets.values())
+        self._graph_buf[:total].copy_(self._pinned[:total], non_blocking=True)
+        g.replay()
+        return self._fetch(out, len(seqs))
+
+    def release_graphs(self):
+        self.graphs.clear()
+        self.graph_pool = None
