@@ -1,0 +1,605 @@
+// Paged attention over the KV pool: split-KV flash-decode and prefix-aware flash-prefill.
+//
+// Reference: nanovllm/layers/attention.py:303-375 calls flash_attn_varlen_func, reading
+// the paged cache through block_table for prefix-hit prefill, chunked prefill and
+// decode (q_len = 1); the torch fallback (:378-498) defines the semantics: causal mask
+// offset by k_len - q_len, softmax scale 1/sqrt(D), GQA by repeating KV heads.
+//
+// Both kernels here read K/V straight from the paged pool [num_blocks, nkv, BS, 128]
+// (bf16, or fp8 e4m3 with one scale per block per head), any power-of-two block size,
+// and use bf16 mma.sync m16n8k16 tiles with fp32 accumulation; the tile loads are
+// cp.async into XOR-swizzled shared memory (conflict-free ldmatrix).
+//
+// decode:  grid (splits, nkv, B).  Each CTA takes all G = nq/nkv query heads of one KV
+//          head (packed as the 16 rows of one MMA tile) over one slice of the context,
+//          4 warps splitting each 64-key tile.  With splits > 1 the CTA writes a
+//          normalised partial output and its log2-sum-exp to scratch, and
+//          attn_combine merges the slices.
+// prefill: grid (q tiles of 64, prefill seqs, nq).  4 warps x 16 query rows.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace nvb {
+
+constexpr int AD = 128;        // head dim
+constexpr int KTILE = 64;      // keys per tile
+constexpr int ROWB = AD * 2;   // bytes per bf16 row
+constexpr float LOG2E = 1.4426950408889634f;
+
+__device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * ROWB + ((c ^ (r & 7)) << 4)); }
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+struct AttnArgs {
+  const __nv_bfloat16* q;   // [T, nq, 128]
+  const void* k_cache;      // [NB, nkv, BS, 128]
+  const void* v_cache;
+  const float* k_scale;     // [NB, nkv] (fp8) or null
+  const float* v_scale;
+  const int* block_tables;  // [B, W]
+  int W;
+  const int* cu_q;          // [B + 1]
+  const int* ctx_lens;      // [B]
+  __nv_bfloat16* out;       // [T, nq, 128]
+  float* part_o;            // [B, nq, splits, 128]
+  float* part_lse;          // [B, nq, splits]
+  int nq, nkv, block_size, num_blocks;
+  int splits;
+  int seq_offset;           // first sequence handled by this launch
+  float scale_log2;
+};
+
+// Issue cp.async for one 64-key tile of K or V (head h of seq b) into `dst` (bf16:
+// swizzled 64 x 256 B; fp8: plain 64 x 128 B staging).  Rows beyond k_len, or whose
+// block id is out of range, are zero-filled.
+template <bool FP8>
+__device__ __forceinline__ void load_tile(const AttnArgs& a, const void* cache, int b, int h, int tile, int k_len,
+                                          uint32_t dst) {
+  const int* bt = a.block_tables + (int64_t)b * a.W;
+  constexpr int CHUNKS = FP8 ? 8 : 16;  // 16-byte chunks per row
+  constexpr int RB = FP8 ? AD : ROWB;
+#pragma unroll
+  for (int i = 0; i < KTILE * CHUNKS / 128; ++i) {
+    int idx = threadIdx.x + i * 128;
+    int r = idx / CHUNKS, c = idx % CHUNKS;
+    int tok = tile * KTILE + r;
+    bool valid = tok < k_len;
+    const uint8_t* src = static_cast<const uint8_t*>(cache);
+    if (valid) {
+      int bi = tok / a.block_size;
+      int blk = bi < a.W ? bt[bi] : -1;
+      valid = blk >= 0 && blk < a.num_blocks;
+      if (valid) src += ((((int64_t)blk * a.nkv + h) * a.block_size + (tok % a.block_size)) * RB) + c * 16;
+    }
+    uint32_t d = FP8 ? dst + r * RB + c * 16 : dst + swz(r, c);
+    cp_async16(d, src, valid);
+  }
+}
+
+// fp8 staging tile -> scaled bf16 swizzled tile.
+__device__ __forceinline__ void convert_fp8_tile(const AttnArgs& a, const float* scales, int b, int h, int tile,
+                                                 int k_len, const uint8_t* stage, uint8_t* dst) {
+  const int* bt = a.block_tables + (int64_t)b * a.W;
+#pragma unroll
+  for (int i = 0; i < KTILE * 16 / 128; ++i) {
+    int idx = threadIdx.x + i * 128;
+    int r = idx >> 4, c = idx & 15;
+    int tok = tile * KTILE + r;
+    float s = 0.f;
+    if (tok < k_len) {
+      int bi = tok / a.block_size;
+      int blk = bi < a.W ? bt[bi] : -1;
+      if (blk >= 0 && blk < a.num_blocks) s = scales[(int64_t)blk * a.nkv + h];
+    }
+    uint2 raw = *reinterpret_cast<const uint2*>(stage + r * AD + c * 8);
+    float f[8];
+    e4m3x4_to_f32(raw.x, f);
+    e4m3x4_to_f32(raw.y, f + 4);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] *= s;
+    *reinterpret_cast<uint4*>(dst + swz(r, c)) = f32_to_bf16x8(f);
+  }
+}
+
+// ------------------------------------------------------------------------- decode
+template <bool FP8>
+__global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sq = smem;                                  // 16 x 256 B
+  uint8_t* sk = smem + 16 * ROWB;                      // 2 stages x 64 x 256 B
+  uint8_t* sv = sk + 2 * KTILE * ROWB;                 // 2 stages
+  uint8_t* stg = sv + 2 * KTILE * ROWB;                // fp8 staging: K,V x 2 stages x 64 x 128 B
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z + a.seq_offset;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = a.nq / a.nkv;
+  const int k_len = a.ctx_lens[b];
+  const int qrow = a.cu_q[b];
+  const int n_tiles = (k_len + KTILE - 1) / KTILE;
+  const int per = (n_tiles + a.splits - 1) / a.splits;
+  const int t0 = split * per;
+  const int t1 = min(n_tiles, t0 + per);
+  const int qh0 = h * G;
+
+  if (t0 >= t1) {  // empty slice
+    if (a.splits > 1) {
+      for (int r = threadIdx.x; r < G; r += 128) a.part_lse[((int64_t)b * a.nq + qh0 + r) * a.splits + split] = -INFINITY;
+    } else {
+      for (int i = threadIdx.x; i < G * AD; i += 128)
+        a.out[((int64_t)qrow * a.nq + qh0) * AD + i] = __float2bfloat16(0.f);
+    }
+    return;
+  }
+
+  // Q rows (G heads, zero padded to 16)
+  for (int idx = threadIdx.x; idx < 16 * 16; idx += 128) {
+    int r = idx >> 4, c = idx & 15;
+    bool v = r < G;
+    const __nv_bfloat16* src = a.q + ((int64_t)qrow * a.nq + qh0 + (v ? r : 0)) * AD + c * 8;
+    cp_async16(smem_u32(sq) + swz(r, c), src, v);
+  }
+  const void* kc = a.k_cache;
+  const void* vc = a.v_cache;
+  auto issue = [&](int tile, int st) {
+    if (FP8) {
+      load_tile<true>(a, kc, b, h, tile, k_len, smem_u32(stg) + st * KTILE * AD);
+      load_tile<true>(a, vc, b, h, tile, k_len, smem_u32(stg) + (2 + st) * KTILE * AD);
+    } else {
+      load_tile<false>(a, kc, b, h, tile, k_len, smem_u32(sk) + st * KTILE * ROWB);
+      load_tile<false>(a, vc, b, h, tile, k_len, smem_u32(sv) + st * KTILE * ROWB);
+    }
+  };
+  issue(t0, 0);
+  cp_commit();
+
+  uint32_t qf[8][4];
+  float acc[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  bool q_loaded = false;
+
+  for (int t = t0; t < t1; ++t) {
+    const int st = (t - t0) & 1;
+    if (t + 1 < t1) {
+      issue(t + 1, st ^ 1);
+      cp_commit();
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    int cs = st;
+    if (FP8) {
+      convert_fp8_tile(a, a.k_scale, b, h, t, k_len, stg + st * KTILE * AD, sk);
+      convert_fp8_tile(a, a.v_scale, b, h, t, k_len, stg + (2 + st) * KTILE * AD, sv);
+      __syncthreads();
+      cs = 0;
+    }
+    if (!q_loaded) {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        int r = (lane & 7) + ((lane >> 3) & 1) * 8, c = kk * 2 + (lane >> 4);
+        ldsm_x4(smem_u32(sq) + swz(r, c), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      }
+      q_loaded = true;
+    }
+    const uint32_t kb = smem_u32(sk) + cs * KTILE * ROWB;
+    const uint32_t vb = smem_u32(sv) + cs * KTILE * ROWB;
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      uint32_t b0, b1, b2, b3;
+      int r = warp * 16 + (lane & 7) + ((lane >> 4) << 3), c = kk * 2 + ((lane >> 3) & 1);
+      ldsm_x4(kb + swz(r, c), b0, b1, b2, b3);
+      mma_bf16(s[0], qf[kk], b0, b1);
+      mma_bf16(s[1], qf[kk], b2, b3);
+    }
+    // scale, mask, online softmax (rows lane/4 and lane/4 + 8)
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        int key = t * KTILE + warp * 16 + nt * 8 + (lane & 3) * 2 + e;
+        bool ok = key < k_len;
+        s[nt][e] = ok ? s[nt][e] * a.scale_log2 : -INFINITY;
+        s[nt][2 + e] = ok ? s[nt][2 + e] * a.scale_log2 : -INFINITY;
+        mx0 = fmaxf(mx0, s[nt][e]);
+        mx1 = fmaxf(mx1, s[nt][2 + e]);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(FULL_MASK, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(FULL_MASK, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(FULL_MASK, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(FULL_MASK, mx1, 2));
+    const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
+    const float base0 = nm0 == -INFINITY ? 0.f : nm0, base1 = nm1 == -INFINITY ? 0.f : nm1;
+    const float al0 = exp2f(m0 - base0), al1 = exp2f(m1 - base1);
+    m0 = nm0;
+    m1 = nm1;
+    float p[2][4];
+    float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      p[nt][0] = exp2f(s[nt][0] - base0);
+      p[nt][1] = exp2f(s[nt][1] - base0);
+      p[nt][2] = exp2f(s[nt][2] - base1);
+      p[nt][3] = exp2f(s[nt][3] - base1);
+      rs0 += p[nt][0] + p[nt][1];
+      rs1 += p[nt][2] + p[nt][3];
+    }
+    l0 = l0 * al0 + rs0;
+    l1 = l1 * al1 + rs1;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      acc[i][0] *= al0;
+      acc[i][1] *= al0;
+      acc[i][2] *= al1;
+      acc[i][3] *= al1;
+    }
+    uint32_t pa[4] = {pack_bf16(p[0][0], p[0][1]), pack_bf16(p[0][2], p[0][3]), pack_bf16(p[1][0], p[1][1]),
+                      pack_bf16(p[1][2], p[1][3])};
+#pragma unroll
+    for (int np = 0; np < 8; ++np) {
+      uint32_t b0, b1, b2, b3;
+      int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, c = np * 2 + (lane >> 4);
+      ldsm_x4_t(vb + swz(r, c), b0, b1, b2, b3);
+      mma_bf16(acc[2 * np], pa, b0, b1);
+      mma_bf16(acc[2 * np + 1], pa, b2, b3);
+    }
+    __syncthreads();
+  }
+
+  // quad-reduce l, then combine the 4 warps through shared memory
+  l0 += __shfl_xor_sync(FULL_MASK, l0, 1);
+  l0 += __shfl_xor_sync(FULL_MASK, l0, 2);
+  l1 += __shfl_xor_sync(FULL_MASK, l1, 1);
+  l1 += __shfl_xor_sync(FULL_MASK, l1, 2);
+  float* sm_acc = reinterpret_cast<float*>(sk);               // [4][16][128]
+  float* sm_ml = reinterpret_cast<float*>(sk + 4 * 16 * AD * 4);  // [4][16][2]
+  const int r0 = lane >> 2, r1 = r0 + 8;
+  if ((lane & 3) == 0) {
+    sm_ml[(warp * 16 + r0) * 2] = m0;
+    sm_ml[(warp * 16 + r0) * 2 + 1] = l0;
+    sm_ml[(warp * 16 + r1) * 2] = m1;
+    sm_ml[(warp * 16 + r1) * 2 + 1] = l1;
+  }
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    int c = nt * 8 + (lane & 3) * 2;
+    sm_acc[(warp * 16 + r0) * AD + c] = acc[nt][0];
+    sm_acc[(warp * 16 + r0) * AD + c + 1] = acc[nt][1];
+    sm_acc[(warp * 16 + r1) * AD + c] = acc[nt][2];
+    sm_acc[(warp * 16 + r1) * AD + c + 1] = acc[nt][3];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * AD; i += 128) {
+    int r = i / AD, c = i % AD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_ml[(w * 16 + r) * 2]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        float f = exp2f(sm_ml[(w * 16 + r) * 2] - M);
+        L += sm_ml[(w * 16 + r) * 2 + 1] * f;
+        O += sm_acc[(w * 16 + r) * AD + c] * f;
+      }
+    }
+    float o = L > 0.f ? O / L : 0.f;
+    if (a.splits == 1) {
+      a.out[((int64_t)qrow * a.nq + qh0 + r) * AD + c] = __float2bfloat16(o);
+    } else {
+      int64_t pi = ((int64_t)b * a.nq + qh0 + r) * a.splits + split;
+      a.part_o[pi * AD + c] = o;
+      if (c == 0) a.part_lse[pi] = L > 0.f ? M + log2f(L) : -INFINITY;
+    }
+  }
+}
+
+// Merge split partials: one CTA per (seq, q head), one thread per dim.
+__global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
+                                    const int* __restrict__ cu_q, __nv_bfloat16* __restrict__ out, int nq, int splits,
+                                    int seq_offset) {
+  const int bh = blockIdx.x;
+  const int b = bh / nq + seq_offset, hq = bh % nq;
+  const int64_t base = ((int64_t)b * nq + hq) * splits;
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, part_lse[base + s]);
+  float L = 0.f, O = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < splits; ++s) {
+      float w = exp2f(part_lse[base + s] - M);
+      L += w;
+      O += w * part_o[(base + s) * AD + threadIdx.x];
+    }
+  }
+  out[((int64_t)cu_q[b] * nq + hq) * AD + threadIdx.x] = __float2bfloat16(L > 0.f ? O / L : 0.f);
+}
+
+// ------------------------------------------------------------------------ prefill
+template <bool FP8>
+__global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sq = smem;                      // 64 x 256 B
+  uint8_t* sk = smem + KTILE * ROWB;       // 2 x 64 x 256
+  uint8_t* sv = sk + 2 * KTILE * ROWB;     // 2 x 64 x 256
+  uint8_t* stg = sv + 2 * KTILE * ROWB;    // fp8 staging 4 x 64 x 128
+  const int b = blockIdx.y + a.seq_offset;
+  const int hq = blockIdx.z;
+  const int G = a.nq / a.nkv;
+  const int h = hq / G;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int qs = a.cu_q[b];
+  const int q_len = a.cu_q[b + 1] - qs;
+  const int row0 = blockIdx.x * 64;
+  if (row0 >= q_len) return;
+  const int k_len = a.ctx_lens[b];
+  const int off = k_len - q_len;
+  const int kmax = min(k_len, off + row0 + 64);
+  const int n_tiles = (kmax + KTILE - 1) / KTILE;
+
+  for (int idx = threadIdx.x; idx < 64 * 16; idx += 128) {
+    int r = idx >> 4, c = idx & 15;
+    bool v = row0 + r < q_len;
+    const __nv_bfloat16* src = a.q + ((int64_t)(qs + row0 + (v ? r : 0)) * a.nq + hq) * AD + c * 8;
+    cp_async16(smem_u32(sq) + swz(r, c), src, v);
+  }
+  auto issue = [&](int tile, int st) {
+    if (FP8) {
+      load_tile<true>(a, a.k_cache, b, h, tile, k_len, smem_u32(stg) + st * KTILE * AD);
+      load_tile<true>(a, a.v_cache, b, h, tile, k_len, smem_u32(stg) + (2 + st) * KTILE * AD);
+    } else {
+      load_tile<false>(a, a.k_cache, b, h, tile, k_len, smem_u32(sk) + st * KTILE * ROWB);
+      load_tile<false>(a, a.v_cache, b, h, tile, k_len, smem_u32(sv) + st * KTILE * ROWB);
+    }
+  };
+  if (n_tiles > 0) issue(0, 0);
+  cp_commit();
+
+  const int qr0 = warp * 16 + (lane >> 2);        // local rows of this thread
+  const int qpos0 = off + row0 + qr0, qpos1 = qpos0 + 8;
+  uint32_t qf[8][4];
+  float acc[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  bool q_loaded = false;
+
+  for (int t = 0; t < n_tiles; ++t) {
+    const int st = t & 1;
+    if (t + 1 < n_tiles) {
+      issue(t + 1, st ^ 1);
+      cp_commit();
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    int cs = st;
+    if (FP8) {
+      convert_fp8_tile(a, a.k_scale, b, h, t, k_len, stg + st * KTILE * AD, sk);
+      convert_fp8_tile(a, a.v_scale, b, h, t, k_len, stg + (2 + st) * KTILE * AD, sv);
+      __syncthreads();
+      cs = 0;
+    }
+    if (!q_loaded) {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, c = kk * 2 + (lane >> 4);
+        ldsm_x4(smem_u32(sq) + swz(r, c), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      }
+      q_loaded = true;
+    }
+    const uint32_t kb = smem_u32(sk) + cs * KTILE * ROWB;
+    const uint32_t vb = smem_u32(sv) + cs * KTILE * ROWB;
+    // Skip tiles entirely above this warp's diagonal (still joins the barriers).
+    const bool warp_active = t * KTILE <= off + row0 + warp * 16 + 15;
+    if (warp_active) {
+      float s[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          uint32_t b0, b1, b2, b3;
+          int r = np * 16 + (lane & 7) + ((lane >> 4) << 3), c = kk * 2 + ((lane >> 3) & 1);
+          ldsm_x4(kb + swz(r, c), b0, b1, b2, b3);
+          mma_bf16(s[2 * np], qf[kk], b0, b1);
+          mma_bf16(s[2 * np + 1], qf[kk], b2, b3);
+        }
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          int key = t * KTILE + nt * 8 + (lane & 3) * 2 + e;
+          bool ok0 = key < k_len && key <= qpos0;
+          bool ok1 = key < k_len && key <= qpos1;
+          s[nt][e] = ok0 ? s[nt][e] * a.scale_log2 : -INFINITY;
+          s[nt][2 + e] = ok1 ? s[nt][2 + e] * a.scale_log2 : -INFINITY;
+          mx0 = fmaxf(mx0, s[nt][e]);
+          mx1 = fmaxf(mx1, s[nt][2 + e]);
+        }
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(FULL_MASK, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(FULL_MASK, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(FULL_MASK, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(FULL_MASK, mx1, 2));
+      const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
+      const float base0 = nm0 == -INFINITY ? 0.f : nm0, base1 = nm1 == -INFINITY ? 0.f : nm1;
+      const float al0 = exp2f(m0 - base0), al1 = exp2f(m1 - base1);
+      m0 = nm0;
+      m1 = nm1;
+      float rs0 = 0.f, rs1 = 0.f;
+      uint32_t pa[4][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        float p0 = exp2f(s[nt][0] - base0), p1 = exp2f(s[nt][1] - base0);
+        float p2 = exp2f(s[nt][2] - base1), p3 = exp2f(s[nt][3] - base1);
+        rs0 += p0 + p1;
+        rs1 += p2 + p3;
+        // A fragment of P for key step nt/2: regs (nt even) 0,1 / (nt odd) 2,3
+        pa[nt >> 1][(nt & 1) * 2] = pack_bf16(p0, p1);
+        pa[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(p2, p3);
+      }
+      l0 = l0 * al0 + rs0;
+      l1 = l1 * al1 + rs1;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        acc[i][0] *= al0;
+        acc[i][1] *= al0;
+        acc[i][2] *= al1;
+        acc[i][3] *= al1;
+      }
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+          uint32_t b0, b1, b2, b3;
+          int r = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, c = np * 2 + (lane >> 4);
+          ldsm_x4_t(vb + swz(r, c), b0, b1, b2, b3);
+          mma_bf16(acc[2 * np], pa[ks], b0, b1);
+          mma_bf16(acc[2 * np + 1], pa[ks], b2, b3);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  l0 += __shfl_xor_sync(FULL_MASK, l0, 1);
+  l0 += __shfl_xor_sync(FULL_MASK, l0, 2);
+  l1 += __shfl_xor_sync(FULL_MASK, l1, 1);
+  l1 += __shfl_xor_sync(FULL_MASK, l1, 2);
+  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  const int gr0 = row0 + qr0, gr1 = gr0 + 8;
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    int c = nt * 8 + (lane & 3) * 2;
+    if (gr0 < q_len)
+      *reinterpret_cast<uint32_t*>(a.out + ((int64_t)(qs + gr0) * a.nq + hq) * AD + c) =
+          pack_bf16(acc[nt][0] * inv0, acc[nt][1] * inv0);
+    if (gr1 < q_len)
+      *reinterpret_cast<uint32_t*>(a.out + ((int64_t)(qs + gr1) * a.nq + hq) * AD + c) =
+          pack_bf16(acc[nt][2] * inv1, acc[nt][3] * inv1);
+  }
+}
+
+static int decode_smem(bool fp8) { return 16 * ROWB + 4 * KTILE * ROWB + (fp8 ? 4 * KTILE * AD : 0); }
+static int prefill_smem(bool fp8) { return KTILE * ROWB + 4 * KTILE * ROWB + (fp8 ? 4 * KTILE * AD : 0); }
+
+int attn_decode_splits(int num_seqs, int nkv, int max_ctx, int num_sms) {
+  int ctas = num_seqs * nkv;
+  int want = (2 * num_sms + ctas - 1) / ctas;
+  int max_tiles = (max_ctx + KTILE - 1) / KTILE;
+  int s = want < max_tiles ? want : max_tiles;
+  if (s > 64) s = 64;
+  return s < 1 ? 1 : s;
+}
+
+cudaError_t launch_attn_decode(const AttnLaunch& L, cudaStream_t stream) {
+  if (L.num_seqs == 0) return cudaSuccess;
+  if (L.head_dim != AD || L.nq % L.nkv || L.nq / L.nkv > 16) return cudaErrorInvalidValue;
+  if (L.splits > 1 && (!L.part_o || !L.part_lse)) return cudaErrorInvalidValue;
+  AttnArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(L.q);
+  a.k_cache = L.k_cache;
+  a.v_cache = L.v_cache;
+  a.k_scale = L.k_scale;
+  a.v_scale = L.v_scale;
+  a.block_tables = L.block_tables;
+  a.W = L.W;
+  a.cu_q = L.cu_q;
+  a.ctx_lens = L.ctx_lens;
+  a.out = static_cast<__nv_bfloat16*>(L.out);
+  a.part_o = L.part_o;
+  a.part_lse = L.part_lse;
+  a.nq = L.nq;
+  a.nkv = L.nkv;
+  a.block_size = L.block_size;
+  a.num_blocks = L.num_blocks;
+  a.splits = L.splits;
+  a.seq_offset = L.seq_offset;
+  a.scale_log2 = L.softmax_scale * LOG2E;
+  dim3 grid(L.splits, L.nkv, L.num_seqs);
+  int sm = decode_smem(L.kv_fp8);
+  if (L.kv_fp8) {
+    cudaFuncSetAttribute(attn_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    attn_decode_kernel<true><<<grid, 128, sm, stream>>>(a);
+  } else {
+    cudaFuncSetAttribute(attn_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    attn_decode_kernel<false><<<grid, 128, sm, stream>>>(a);
+  }
+  NVB_LAUNCH_CHECK();
+  if (L.splits > 1) {
+    attn_combine_kernel<<<L.num_seqs * L.nq, AD, 0, stream>>>(L.part_o, L.part_lse, L.cu_q, a.out, L.nq, L.splits,
+                                                             L.seq_offset);
+    NVB_LAUNCH_CHECK();
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_attn_prefill(const AttnLaunch& L, int max_q_len, cudaStream_t stream) {
+  if (L.num_seqs == 0 || max_q_len == 0) return cudaSuccess;
+  if (L.head_dim != AD || L.nq % L.nkv) return cudaErrorInvalidValue;
+  AttnArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(L.q);
+  a.k_cache = L.k_cache;
+  a.v_cache = L.v_cache;
+  a.k_scale = L.k_scale;
+  a.v_scale = L.v_scale;
+  a.block_tables = L.block_tables;
+  a.W = L.W;
+  a.cu_q = L.cu_q;
+  a.ctx_lens = L.ctx_lens;
+  a.out = static_cast<__nv_bfloat16*>(L.out);
+  a.part_o = nullptr;
+  a.part_lse = nullptr;
+  a.nq = L.nq;
+  a.nkv = L.nkv;
+  a.block_size = L.block_size;
+  a.num_blocks = L.num_blocks;
+  a.splits = 1;
+  a.seq_offset = L.seq_offset;
+  a.scale_log2 = L.softmax_scale * LOG2E;
+  dim3 grid((max_q_len + 63) / 64, L.num_seqs, L.nq);
+  int sm = prefill_smem(L.kv_fp8);
+  if (L.kv_fp8) {
+    cudaFuncSetAttribute(attn_prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    attn_prefill_kernel<true><<<grid, 128, sm, stream>>>(a);
+  } else {
+    cudaFuncSetAttribute(attn_prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    attn_prefill_kernel<false><<<grid, 128, sm, stream>>>(a);
+  }
+  NVB_LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
+}  // namespace nvb

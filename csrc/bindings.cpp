@@ -1,0 +1,192 @@
+// Python bindings (torch tensors -> raw launches on the current CUDA stream).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "kernels.h"
+
+namespace {
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bfloat16")
+#define CHECK_I32(x) TORCH_CHECK((x).scalar_type() == at::kInt, #x " must be int32")
+
+void check(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, what, " failed: ", cudaGetErrorString(e));
+}
+
+template <typename T>
+T* ptr_or_null(const c10::optional<at::Tensor>& t) {
+  return t.has_value() && t->defined() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void add_rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual_in,
+                 const c10::optional<at::Tensor>& residual_out, const at::Tensor& w, at::Tensor& out, double eps,
+                 const c10::optional<at::Tensor>& row_index) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  CHECK_BF16(out);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be [rows, H] with unit inner stride");
+  int H = (int)x.size(1);
+  int rows = (int)out.size(0);
+  if (row_index.has_value()) CHECK_I32(*row_index);
+  if (residual_in.has_value()) CHECK_CONTIG(*residual_in);
+  at::cuda::CUDAGuard g(x.device());
+  check(nvb::launch_add_rmsnorm(x.data_ptr(), x.stride(0), ptr_or_null<void>(residual_in),
+                                ptr_or_null<void>(residual_out), w.data_ptr(), out.data_ptr(), rows, H, (float)eps,
+                                ptr_or_null<int>(row_index), stream()),
+        "add_rmsnorm");
+}
+
+void silu_mul(const at::Tensor& x, at::Tensor& out) {
+  CHECK_CONTIG(x);
+  CHECK_BF16(x);
+  CHECK_CONTIG(out);
+  at::cuda::CUDAGuard g(x.device());
+  check(nvb::launch_silu_mul(x.data_ptr(), out.data_ptr(), (int)x.size(0), (int)out.size(1), stream()), "silu_mul");
+}
+
+void embedding(const at::Tensor& ids, const at::Tensor& table, int64_t vocab_start, at::Tensor& out) {
+  CHECK_I32(ids);
+  CHECK_CONTIG(table);
+  CHECK_BF16(table);
+  at::cuda::CUDAGuard g(ids.device());
+  check(nvb::launch_embedding(ids.data_ptr<int>(), table.data_ptr(), (int)table.size(0), (int)vocab_start,
+                              out.data_ptr(), (int)ids.size(0), (int)table.size(1), stream()),
+        "embedding");
+}
+
+void qkv_post(const at::Tensor& qkv, at::Tensor& q_out, const at::Tensor& q_norm, const at::Tensor& k_norm, double eps,
+              const at::Tensor& positions, const at::Tensor& cos_sin, at::Tensor& k_cache, at::Tensor& v_cache,
+              const c10::optional<at::Tensor>& k_scale, const c10::optional<at::Tensor>& v_scale,
+              const at::Tensor& slots, int64_t nq, int64_t nkv) {
+  CHECK_BF16(qkv);
+  TORCH_CHECK(qkv.stride(1) == 1, "qkv inner stride");
+  CHECK_I32(positions);
+  CHECK_I32(slots);
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos_sin fp32 contiguous");
+  int fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
+  TORCH_CHECK(fp8 || k_cache.scalar_type() == at::kBFloat16, "KV cache must be bf16 or fp8 e4m3");
+  TORCH_CHECK(!fp8 || (k_scale.has_value() && v_scale.has_value()), "fp8 KV cache needs scales");
+  at::cuda::CUDAGuard g(qkv.device());
+  check(nvb::launch_qkv_post(qkv.data_ptr(), qkv.stride(0), q_out.data_ptr(), q_norm.data_ptr(), k_norm.data_ptr(),
+                             (float)eps, positions.data_ptr<int>(), cos_sin.data_ptr<float>(), k_cache.data_ptr(),
+                             v_cache.data_ptr(), ptr_or_null<float>(k_scale), ptr_or_null<float>(v_scale),
+                             slots.data_ptr<int>(), (int)qkv.size(0), (int)nq, (int)nkv, (int)k_cache.size(3),
+                             (int)k_cache.size(2), fp8, stream()),
+        "qkv_post");
+}
+
+nvb::AttnLaunch attn_args(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                          const c10::optional<at::Tensor>& k_scale, const c10::optional<at::Tensor>& v_scale,
+                          const at::Tensor& block_tables, const at::Tensor& cu_q, const at::Tensor& ctx_lens,
+                          at::Tensor& out, int64_t nq, int64_t nkv, int64_t seq_offset, int64_t num_seqs,
+                          double scale) {
+  CHECK_BF16(q);
+  CHECK_CONTIG(q);
+  CHECK_CONTIG(k_cache);
+  CHECK_CONTIG(v_cache);
+  CHECK_I32(block_tables);
+  CHECK_CONTIG(block_tables);
+  CHECK_I32(cu_q);
+  CHECK_I32(ctx_lens);
+  int fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
+  TORCH_CHECK(fp8 || k_cache.scalar_type() == at::kBFloat16, "KV cache must be bf16 or fp8 e4m3");
+  nvb::AttnLaunch L{};
+  L.q = q.data_ptr();
+  L.k_cache = k_cache.data_ptr();
+  L.v_cache = v_cache.data_ptr();
+  L.k_scale = ptr_or_null<float>(k_scale);
+  L.v_scale = ptr_or_null<float>(v_scale);
+  L.block_tables = block_tables.data_ptr<int>();
+  L.W = (int)block_tables.size(1);
+  L.cu_q = cu_q.data_ptr<int>();
+  L.ctx_lens = ctx_lens.data_ptr<int>();
+  L.out = out.data_ptr();
+  L.nq = (int)nq;
+  L.nkv = (int)nkv;
+  L.head_dim = (int)k_cache.size(3);
+  L.block_size = (int)k_cache.size(2);
+  L.num_blocks = (int)k_cache.size(0);
+  L.seq_offset = (int)seq_offset;
+  L.num_seqs = (int)num_seqs;
+  L.kv_fp8 = fp8;
+  L.softmax_scale = (float)scale;
+  return L;
+}
+
+void attn_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                 const c10::optional<at::Tensor>& k_scale, const c10::optional<at::Tensor>& v_scale,
+                 const at::Tensor& block_tables, const at::Tensor& cu_q, const at::Tensor& ctx_lens, at::Tensor& out,
+                 const c10::optional<at::Tensor>& part_o, const c10::optional<at::Tensor>& part_lse, int64_t nq,
+                 int64_t nkv, int64_t splits, int64_t seq_offset, int64_t num_seqs, double scale) {
+  auto L = attn_args(q, k_cache, v_cache, k_scale, v_scale, block_tables, cu_q, ctx_lens, out, nq, nkv, seq_offset,
+                     num_seqs, scale);
+  L.splits = (int)splits;
+  L.part_o = ptr_or_null<float>(part_o);
+  L.part_lse = ptr_or_null<float>(part_lse);
+  if (splits > 1) {
+    TORCH_CHECK(part_o.has_value() && part_lse.has_value(), "split decode needs scratch");
+    int64_t need = (seq_offset + num_seqs) * nq * splits;
+    TORCH_CHECK(part_lse->numel() >= need && part_o->numel() >= need * L.head_dim, "decode scratch too small");
+  }
+  at::cuda::CUDAGuard g(q.device());
+  check(nvb::launch_attn_decode(L, stream()), "attn_decode");
+}
+
+void attn_prefill(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                  const c10::optional<at::Tensor>& k_scale, const c10::optional<at::Tensor>& v_scale,
+                  const at::Tensor& block_tables, const at::Tensor& cu_q, const at::Tensor& ctx_lens, at::Tensor& out,
+                  int64_t nq, int64_t nkv, int64_t seq_offset, int64_t num_seqs, int64_t max_q_len, double scale) {
+  auto L = attn_args(q, k_cache, v_cache, k_scale, v_scale, block_tables, cu_q, ctx_lens, out, nq, nkv, seq_offset,
+                     num_seqs, scale);
+  L.splits = 1;
+  at::cuda::CUDAGuard g(q.device());
+  check(nvb::launch_attn_prefill(L, (int)max_q_len, stream()), "attn_prefill");
+}
+
+int64_t decode_splits(int64_t num_seqs, int64_t nkv, int64_t max_ctx, int64_t num_sms) {
+  return nvb::attn_decode_splits((int)num_seqs, (int)nkv, (int)max_ctx, (int)num_sms);
+}
+
+int64_t sample_chunks(int64_t rows, int64_t V) { return nvb::sample_num_chunks((int)rows, (int)V); }
+
+void sample(const at::Tensor& logits, int64_t col_offset, const at::Tensor& temps, const at::Tensor& seed_step,
+            at::Tensor& part_val, at::Tensor& part_idx, int64_t nchunk, at::Tensor& out_tok,
+            const c10::optional<at::Tensor>& out_val) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits [rows, V]");
+  TORCH_CHECK(temps.scalar_type() == at::kFloat, "temps fp32");
+  TORCH_CHECK(seed_step.scalar_type() == at::kLong && seed_step.numel() >= 2, "seed_step int64[2]");
+  TORCH_CHECK(part_val.numel() >= logits.size(0) * nchunk && part_idx.numel() >= logits.size(0) * nchunk,
+              "sample scratch too small");
+  int bf16 = logits.scalar_type() == at::kBFloat16;
+  TORCH_CHECK(bf16 || logits.scalar_type() == at::kFloat, "logits bf16 or fp32");
+  at::cuda::CUDAGuard g(logits.device());
+  check(nvb::launch_sample(logits.data_ptr(), bf16, logits.stride(0), (int)logits.size(0), (int)logits.size(1),
+                           col_offset, temps.data_ptr<float>(), seed_step.data_ptr<int64_t>(),
+                           part_val.data_ptr<float>(), part_idx.data_ptr<int>(), (int)nchunk, out_tok.data_ptr<int>(),
+                           ptr_or_null<float>(out_val), stream()),
+        "sample");
+}
+
+}  // namespace
+
+void register_gemm(pybind11::module& m);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "nanovllm_self_b200 sm_100a kernels";
+  m.def("add_rmsnorm", &add_rmsnorm);
+  m.def("silu_mul", &silu_mul);
+  m.def("embedding", &embedding);
+  m.def("qkv_post", &qkv_post);
+  m.def("attn_decode", &attn_decode);
+  m.def("attn_prefill", &attn_prefill);
+  m.def("decode_splits", &decode_splits);
+  m.def("sample_chunks", &sample_chunks);
+  m.def("sample", &sample);
+  register_gemm(m);
+}

@@ -1,0 +1,49 @@
+// Host-side launch entry points of the sm_100a kernels (raw pointers, no torch types).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace nvb {
+
+cudaError_t launch_add_rmsnorm(const void* x, int64_t x_stride, const void* residual_in, void* residual_out,
+                               const void* w, void* out, int rows, int H, float eps, const int* row_index,
+                               cudaStream_t stream);
+cudaError_t launch_silu_mul(const void* x, void* out, int T, int I, cudaStream_t stream);
+cudaError_t launch_embedding(const int* ids, const void* table, int rows, int vocab_start, void* out, int T, int H,
+                             cudaStream_t stream);
+cudaError_t launch_qkv_post(const void* qkv, int64_t qkv_stride, void* q_out, const void* q_norm, const void* k_norm,
+                            float eps, const int* positions, const float* cos_sin, void* k_cache, void* v_cache,
+                            float* k_scale, float* v_scale, const int* slots, int T, int nq, int nkv, int head_dim,
+                            int block_size, int kv_fp8, cudaStream_t stream);
+
+struct AttnLaunch {
+  const void* q;
+  const void* k_cache;
+  const void* v_cache;
+  const float* k_scale;
+  const float* v_scale;
+  const int* block_tables;
+  int W;
+  const int* cu_q;
+  const int* ctx_lens;
+  void* out;
+  float* part_o;
+  float* part_lse;
+  int nq, nkv, head_dim, block_size, num_blocks;
+  int splits;
+  int seq_offset;
+  int num_seqs;
+  int kv_fp8;
+  float softmax_scale;
+};
+
+int attn_decode_splits(int num_seqs, int nkv, int max_ctx, int num_sms);
+cudaError_t launch_attn_decode(const AttnLaunch& L, cudaStream_t stream);
+cudaError_t launch_attn_prefill(const AttnLaunch& L, int max_q_len, cudaStream_t stream);
+
+int sample_num_chunks(int rows, int V);
+cudaError_t launch_sample(const void* logits, int logits_is_bf16, int64_t ld, int rows, int V, int64_t col_offset,
+                          const float* temps, const int64_t* seed_step, float* part_val, int* part_idx, int nchunk,
+                          int* out_tok, float* out_val, cudaStream_t stream);
+
+}  // namespace nvb

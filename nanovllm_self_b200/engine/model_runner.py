@@ -73,6 +73,7 @@ class ModelRunner:
         self._allocate_kv_cache()
         self.block_manager = BlockManager(self.num_blocks, self.block_size, config.enable_prefix_cache)
         self.sample_step = 0
+        self._use_top_p = False
         self._gen = torch.Generator(device=self.device)
         self._gen.manual_seed(config.seed)
         self.graphs: dict = {}
@@ -234,6 +235,9 @@ class ModelRunner:
         pk.offsets, pk.host, pk.need = offs, host, need
         pk.q_lens, pk.k_lens = q_lens + [1] * (Bp - B), k_lens + [0] * (Bp - B)
         pk.max_q, pk.max_k = max(q_lens), max(k_lens)
+        if pad_to is not None:
+            # a captured graph serves any context length up to max_model_len
+            pk.max_k = self.config.max_model_len
         return pk
 
     def _to_device(self, pk: _Packed, dev_buf: torch.Tensor | None = None):
@@ -265,7 +269,8 @@ class ModelRunner:
         if self.tp.size > 1 and self.comm is not None:
             return self.comm.vocab_parallel_sample(logits, temps, topp, self.model, self)
         return self.ops.sample(logits, temps, topp, seeds=None, step=self._step_tensor(),
-                               batch_greedy_compat=self.config.batch_greedy_compat, generator=self._gen)
+                               batch_greedy_compat=self.config.batch_greedy_compat, generator=self._gen,
+                               use_top_p=self._use_top_p)
 
     def _step_tensor(self):
         if not self.is_cuda:
@@ -281,8 +286,12 @@ class ModelRunner:
             return [], []
         need = [i for i, s in enumerate(seqs) if s.is_need_logits]
         all_decode = all(s.num_new_tokens == 1 and s.is_prefill_done for s in seqs)
+        self._use_top_p = any(seqs[i].top_p < 1.0 and seqs[i].temperature > 0 for i in need)
+        if self.config.batch_greedy_compat and any(seqs[i].temperature <= 0 for i in need):
+            for i in need:  # reference quirk: one greedy row makes the whole batch greedy
+                seqs[i].temperature = 0.0
         graph_bs = None
-        if self.enable_cuda_graph and all_decode and len(seqs) <= self.graph_max_bs:
+        if self.enable_cuda_graph and all_decode and not self._use_top_p and len(seqs) <= self.graph_max_bs:
             graph_bs = next(b for b in self.graph_bs_list if b >= len(seqs))
         if graph_bs is not None:
             toks = self._run_graph(seqs, graph_bs)

@@ -127,9 +127,12 @@ class Qwen3ForCausalLM:
         ops = self.ops
         if logits_indices.numel() == 0:
             return torch.empty(0, self.vocab_end - self.vocab_start, device=h.device, dtype=torch.float32)
-        hs = h.index_select(0, logits_indices)
-        rs = residual.index_select(0, logits_indices)
-        x, _ = self._reduce_norm(hs, rs, self.norm)
+        if self.comm is not None and self.tp_size > 1:
+            hs = h.index_select(0, logits_indices)
+            rs = residual.index_select(0, logits_indices)
+            x, _ = self.comm.allreduce_add_rmsnorm(hs, rs, self.norm, self.eps)
+        else:
+            x, _ = ops.add_rmsnorm_rows(h, residual, self.norm, self.eps, logits_indices)
         return ops.linear(x, self.lm_head)
 
     def forward(self, input_ids, positions, ctx, kv_caches, kv_scales=None):

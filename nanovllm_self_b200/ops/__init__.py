@@ -25,6 +25,10 @@ class TorchOps:
     def add_rmsnorm(self, x, residual, w, eps):
         return R.add_rmsnorm(x, residual, w, eps)
 
+    def add_rmsnorm_rows(self, h, residual, w, eps, rows):
+        idx = rows.long()
+        return R.add_rmsnorm(h.index_select(0, idx), residual.index_select(0, idx), w, eps)
+
     def rmsnorm(self, x, w, eps):
         return R.rmsnorm(x, w, eps)
 
@@ -52,7 +56,7 @@ class TorchOps:
         return R.silu_mul(x)
 
     def sample(self, logits, temperatures, top_p=None, seeds=None, step=0, batch_greedy_compat=False,
-               generator=None):
+               generator=None, use_top_p=True, col_offset=0):
         return R.sample(logits, temperatures, top_p, generator, batch_greedy_compat).to(torch.int32)
 
 

@@ -1,0 +1,204 @@
+"""Numerics of every sm_100a kernel against the plain-PyTorch fp32 reference of the same op."""
+import math
+
+import pytest
+import torch
+
+from nanovllm_self_b200.ops import torch_ref as R
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from nanovllm_self_b200.ops.cuda_ops import CudaOps
+    return CudaOps()
+
+
+def _close(a, b, atol, rtol=0.02):
+    a, b = a.float(), b.float()
+    err = (a - b).abs()
+    tol = atol + rtol * b.abs()
+    bad = (err > tol).float().mean().item()
+    assert bad < 1e-3, f"{bad*100:.3f}% elements out of tolerance, max err {err.max().item():.4g}"
+
+
+@pytest.mark.parametrize("rows,H", [(1, 1024), (7, 4096), (300, 5120), (33, 256)])
+@pytest.mark.parametrize("with_res", [False, True])
+def test_add_rmsnorm(ops, rows, H, with_res):
+    g = torch.Generator(device=DEV).manual_seed(rows + H)
+    x = torch.randn(rows, H, device=DEV, generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device=DEV, generator=g)).bfloat16()
+    res = torch.randn(rows, H, device=DEV, generator=g).bfloat16() if with_res else None
+    ref_out, ref_res = R.add_rmsnorm(x.float(), None if res is None else res.float(), w.float(), 1e-6)
+    out, r = ops.add_rmsnorm(x, None if res is None else res.clone(), w, 1e-6)
+    _close(out, ref_out, 0.02)
+    _close(r, ref_res, 0.02)
+
+
+def test_add_rmsnorm_rows(ops):
+    h = torch.randn(50, 1024, device=DEV).bfloat16()
+    res = torch.randn(50, 1024, device=DEV).bfloat16()
+    w = torch.ones(1024, device=DEV).bfloat16()
+    rows = torch.tensor([3, 49, 0, 17], device=DEV, dtype=torch.int32)
+    out, _ = ops.add_rmsnorm_rows(h, res, w, 1e-6, rows)
+    ref, _ = R.add_rmsnorm(h[rows.long()].float(), res[rows.long()].float(), w.float(), 1e-6)
+    _close(out, ref, 0.02)
+
+
+@pytest.mark.parametrize("T,I", [(1, 3072), (129, 12288), (5, 1536)])
+def test_silu_mul(ops, T, I):
+    x = torch.randn(T, 2 * I, device=DEV).bfloat16()
+    _close(ops.silu_mul(x), R.silu_mul(x.float()), 0.01)
+
+
+def test_embedding_shard(ops):
+    w = torch.randn(100, 256, device=DEV).bfloat16()
+    ids = torch.tensor([0, 150, 175, 249, 250, 3], device=DEV, dtype=torch.int32)
+    out = ops.embedding(ids, w, 150)
+    ref = R.embedding(ids, w, 150)
+    assert torch.equal(out, ref)
+
+
+def _kv_setup(nb, nkv, bs, dtype, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    kc = torch.zeros(nb, nkv, bs, 128, device=DEV, dtype=dtype)
+    vc = torch.zeros_like(kc)
+    ks = vs = None
+    if dtype == torch.float8_e4m3fn:
+        ks = torch.ones(nb, nkv, device=DEV)
+        vs = torch.ones(nb, nkv, device=DEV)
+    return kc, vc, ks, vs, g
+
+
+@pytest.mark.parametrize("kv_dtype", [torch.bfloat16, torch.float8_e4m3fn])
+@pytest.mark.parametrize("bs", [16, 256])
+def test_qkv_post(ops, kv_dtype, bs):
+    nq, nkv, T = 8, 2, 40
+    nb = 16
+    kc, vc, ks, vs, g = _kv_setup(nb, nkv, bs, kv_dtype)
+    qkv = torch.randn(T, (nq + 2 * nkv) * 128, device=DEV, generator=g).bfloat16()
+    qn = (1 + 0.1 * torch.randn(128, device=DEV, generator=g)).bfloat16()
+    kn = (1 + 0.1 * torch.randn(128, device=DEV, generator=g)).bfloat16()
+    pos = torch.arange(5, 5 + T, device=DEV, dtype=torch.int32)
+    cs = R.rope_cos_sin(128, 4096, 1e6, device=DEV)
+    # tokens 5.. of a sequence whose block table is [3, 7, 1, ...]; slot -1 for the last token
+    table = torch.tensor([3, 7, 1, 9, 11, 2, 4, 5], device=DEV)
+    p = pos.long()
+    slots = (table[p // bs] * bs + p % bs).to(torch.int32)
+    slots[-1] = -1
+    q = ops.qkv_post(qkv, qn, kn, 1e-6, pos, cs, kc, vc, slots, ks, vs, nq, nkv, 128)
+    kc2, vc2 = torch.zeros_like(kc, dtype=torch.float32), torch.zeros_like(vc, dtype=torch.float32)
+    ks2 = vs2 = None
+    if kv_dtype == torch.float8_e4m3fn:
+        kc2, vc2 = torch.zeros_like(kc), torch.zeros_like(vc)
+        ks2, vs2 = torch.ones_like(ks), torch.ones_like(vs)
+    qf = qkv.float()
+    qr = R.apply_rope(R.rmsnorm(qf[:, :nq * 128].reshape(T, nq, 128), qn.float(), 1e-6), pos, cs)
+    kr = R.apply_rope(R.rmsnorm(qf[:, nq * 128:(nq + nkv) * 128].reshape(T, nkv, 128), kn.float(), 1e-6), pos, cs)
+    vr = qf[:, (nq + nkv) * 128:].reshape(T, nkv, 128)
+    R.store_kv(kr, vr, kc2, vc2, slots, ks2, vs2)
+    _close(q.view(T, nq, 128), qr, 0.03)
+    if kv_dtype == torch.float8_e4m3fn:
+        _close(kc.float() * ks[:, :, None, None], kc2.float() * ks2[:, :, None, None], 0.05, 0.08)
+        _close(vc.float() * vs[:, :, None, None], vc2.float() * vs2[:, :, None, None], 0.05, 0.08)
+        _close(ks, ks2, 1e-3)
+    else:
+        _close(kc, kc2, 0.03)
+        _close(vc, vc2, 0.03)
+
+
+def _paged_case(q_lens, k_lens, nq, nkv, bs, kv_dtype, seed=1):
+    nb = sum((k + bs - 1) // bs for k in k_lens) + 4
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    kf = torch.randn(nb, nkv, bs, 128, device=DEV, generator=g)
+    vf = torch.randn(nb, nkv, bs, 128, device=DEV, generator=g)
+    ks = vs = None
+    if kv_dtype == torch.float8_e4m3fn:
+        ks = (kf.abs().amax(dim=(2, 3)) / 448.0 * 1.5).float()
+        vs = (vf.abs().amax(dim=(2, 3)) / 448.0 * 1.5).float()
+        kc = (kf / ks[:, :, None, None]).to(kv_dtype)
+        vc = (vf / vs[:, :, None, None]).to(kv_dtype)
+    else:
+        kc, vc = kf.to(kv_dtype), vf.to(kv_dtype)
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(seed)).tolist()
+    W = max((k + bs - 1) // bs for k in k_lens)
+    tables, o = [], 0
+    for k in k_lens:
+        n = (k + bs - 1) // bs
+        tables.append(perm[o:o + n] + [0] * (W - n))
+        o += n
+    T = sum(q_lens)
+    q = torch.randn(T, nq, 128, device=DEV, generator=g).bfloat16()
+    bt = torch.tensor(tables, device=DEV, dtype=torch.int32)
+    cu = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), device=DEV, dtype=torch.int32)
+    ctx_lens = torch.tensor(k_lens, device=DEV, dtype=torch.int32)
+    return q, kc, vc, ks, vs, bt, cu, ctx_lens, tables
+
+
+class _Ctx:
+    pass
+
+
+@pytest.mark.parametrize("kv_dtype", [torch.bfloat16, torch.float8_e4m3fn])
+@pytest.mark.parametrize("nq,nkv", [(16, 8), (32, 8), (4, 1), (64, 8)])
+@pytest.mark.parametrize("bs", [16, 256])
+def test_attention_decode_and_prefill(ops, kv_dtype, nq, nkv, bs):
+    # 3 decode seqs (various ctx incl. long for split-KV) then 3 prefill seqs (prefix offset, chunk)
+    q_lens = [1, 1, 1, 37, 130, 64]
+    k_lens = [1, 300, 2100, 37, 200, 1000]
+    q, kc, vc, ks, vs, bt, cu, cl, tables = _paged_case(q_lens, k_lens, nq, nkv, bs, kv_dtype)
+    ctx = _Ctx()
+    ctx.num_decode_seqs, ctx.num_seqs = 3, 6
+    ctx.block_tables, ctx.cu_seqlens_q, ctx.context_lens = bt, cu, cl
+    ctx.max_seqlen_q, ctx.max_seqlen_k = max(q_lens), max(k_lens)
+    scale = 1 / math.sqrt(128)
+    out = ops.attention(q.view(q.shape[0], -1), kc, vc, ctx, scale, ks, vs).view_as(q)
+    ref = R.paged_attention(q.float(), kc, vc, q_lens, k_lens, tables, scale, ks, vs)
+    _close(out, ref, 0.02, 0.03)
+
+
+def test_sample_greedy_and_temperature(ops):
+    torch.manual_seed(0)
+    V = 151936
+    logits = torch.randn(6, V, device=DEV)
+    logits[:, 1234] += 50
+    temps = torch.tensor([0, 0, 0.5, 1.0, 0, 2.0], device=DEV)
+    step = torch.tensor([7, 3], dtype=torch.int64, device=DEV)
+    tok = ops.sample(logits, temps, step=step)
+    assert torch.equal(tok[temps <= 0].long(), logits[temps <= 0].argmax(-1))
+    assert (tok[temps > 0] == 1234).all()
+    # temperature sampling follows softmax(l / T): check a 4-way distribution
+    small = torch.log(torch.tensor([[0.1, 0.2, 0.3, 0.4]], device=DEV)).repeat(4096, 1)
+    counts = torch.zeros(4)
+    for s in range(4):
+        step = torch.tensor([11, s], dtype=torch.int64, device=DEV)
+        t = ops.sample(small, torch.ones(4096, device=DEV), step=step)
+        counts += torch.bincount(t.long().cpu(), minlength=4).float()
+    freq = counts / counts.sum()
+    assert torch.allclose(freq, torch.tensor([0.1, 0.2, 0.3, 0.4]), atol=0.02), freq
+
+
+@pytest.mark.parametrize("m,n,k", [
+    (1, 1024, 1024), (5, 6144, 4096), (64, 4096, 4096), (130, 24576, 1024), (256, 512, 3072),
+    (300, 1024, 1024), (1000, 3072, 1024), (4096, 4096, 4096), (77, 151936, 1024), (2, 768, 4096),
+])
+def test_gemm_tcgen05(ops, m, n, k):
+    g = torch.Generator(device=DEV).manual_seed(m * 7 + n)
+    x = (torch.randn(m, k, device=DEV, generator=g) * 0.5).bfloat16()
+    w = (torch.randn(n, k, device=DEV, generator=g) * 0.02).bfloat16()
+    out = ops.linear(x, w)
+    ref = x.float() @ w.float().t()
+    _close(out, ref, 0.01 * math.sqrt(k / 1024) * 0.5, 0.02)
+    assert ops.C.gemm_error(True) == 0
+
+
+@pytest.mark.parametrize("swap,bn,splits", [(0, 256, 1), (0, 128, 3), (1, 32, 1), (1, 64, 4), (1, 256, 2), (0, 64, 1)])
+def test_gemm_forced_configs(ops, swap, bn, splits):
+    m, n, k = 200, 1280, 2048
+    x = torch.randn(m, k, device=DEV).bfloat16()
+    w = (torch.randn(n, k, device=DEV) * 0.05).bfloat16()
+    out = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+    ops.C.linear(x, w, out, ops.scratch(x.device).gemm, swap, bn, splits)
+    _close(out, x.float() @ w.float().t(), 0.05, 0.02)
