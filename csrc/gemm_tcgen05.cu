@@ -413,8 +413,12 @@ cudaError_t run(const CUtensorMap& mp, const CUtensorMap& mq, const Params& prm,
   constexpr int STAGES = stages_for<BN>();
   constexpr int SMEM = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
   auto kern = gemm_kernel<BN, STAGES>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-  if (e != cudaSuccess) return e;
+  static bool configured = false;  // per template instance; the attribute is process-wide
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
   kern<<<grid, NUM_THREADS, SMEM, stream>>>(mp, mq, prm);
   return cudaGetLastError();
 }
@@ -475,6 +479,7 @@ cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, vo
   if (k % 8 || ldx % 8 || ldw % 8) return cudaErrorInvalidValue;
   if (((uintptr_t)x & 15) || ((uintptr_t)w & 15)) return cudaErrorMisalignedAddress;
   if (pl.splits > 1 && !ws) return cudaErrorInvalidValue;
+  if (!pl.swap && (ldc % 8 || ((uintptr_t)c & 15))) return cudaErrorInvalidValue;
   const void* pbase = pl.swap ? w : x;
   const void* qbase = pl.swap ? x : w;
   const int64_t pld = pl.swap ? ldw : ldx, qld = pl.swap ? ldx : ldw;

@@ -59,8 +59,6 @@ class LLMEngine:
             except Exception:
                 self.tokenizer = None
         self.model_runner = ModelRunner(config, self.tp, self.comm)
-        if self.comm is not None:
-            self.comm.bind(self.model_runner)
         self.block_manager = self.model_runner.block_manager
         self.scheduler = Scheduler(config, self.block_manager)
         arch = self.model_runner.arch
@@ -113,16 +111,8 @@ class LLMEngine:
         seqs = self.scheduler.schedule()
         if not seqs:
             return [], [], 0.0
-        ev0 = ev1 = None
-        if self.model_runner.is_cuda:
-            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            ev0.record()
         token_ids, need = self.model_runner.run(seqs)
-        dev_ms = 0.0
-        if ev0 is not None:
-            ev1.record()
-            ev1.synchronize()
-            dev_ms = ev0.elapsed_time(ev1)
+        dev_ms = self.model_runner.last_dev_ms
         finished = self.scheduler.postprocess(seqs, token_ids, need)
         return seqs, finished, dev_ms
 

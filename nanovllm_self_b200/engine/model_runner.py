@@ -73,6 +73,10 @@ class ModelRunner:
         self._allocate_kv_cache()
         self.block_manager = BlockManager(self.num_blocks, self.block_size, config.enable_prefix_cache)
         self.sample_step = 0
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.last_dev_ms = 0.0
+        self.graph_launches: dict = {}
         self._use_top_p = False
         self._gen = torch.Generator(device=self.device)
         self._gen.manual_seed(config.seed)
@@ -82,6 +86,8 @@ class ModelRunner:
         self._staging_dev = None
         self._pinned = None
         self._out_pinned = None
+        if comm is not None:
+            comm.bind(self)
         if self.is_cuda:
             self._alloc_staging()
         if self.enable_cuda_graph:
@@ -152,6 +158,7 @@ class ModelRunner:
         self._pinned = torch.zeros(n, dtype=torch.int32, pin_memory=True)
         self._out_pinned = torch.zeros(maxB, dtype=torch.int32, pin_memory=True)
         self._out_event = torch.cuda.Event()
+        self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
 
     # --------------------------------------------------------------- packing
     def _pack(self, seqs: list[Sequence], pad_to: int | None = None) -> _Packed:
@@ -245,6 +252,7 @@ class ModelRunner:
         if self.is_cuda:
             dst = dev_buf if dev_buf is not None else self._staging_dev
             dst[:total].copy_(self._pinned[:total], non_blocking=True)
+            self.h2d_bytes += total * 4
         else:
             dst = torch.from_numpy(pk.host[:total].copy())
         v = {k: dst[o:o + n] for k, (o, n) in pk.offsets.items()}
@@ -298,12 +306,20 @@ class ModelRunner:
         else:
             pk = self._pack(seqs)
             ids, pos, ctx, temps, topp = self._to_device(pk)
+            self._mark(0)
             toks = self._forward_and_sample(ids, pos, ctx, temps, topp)
+            self._mark(1)
             toks = self._fetch(toks, len(need))
+        self.last_dev_ms = self._ev[0].elapsed_time(self._ev[1]) if self.is_cuda else 0.0
         self.sample_step += 1
         if self.is_cuda:
             self._step_dev[1] += 1
         return toks[:len(need)], need
+
+    def _mark(self, i: int) -> None:
+        """Device timestamps around the forward + sampler (excludes host packing and copies)."""
+        if self.is_cuda:
+            self._ev[i].record()
 
     def _fetch(self, toks: torch.Tensor, n: int) -> list[int]:
         if n == 0:
@@ -311,6 +327,7 @@ class ModelRunner:
         if not self.is_cuda:
             return [int(x) for x in toks.tolist()]
         self._out_pinned[:n].copy_(toks[:n], non_blocking=True)
+        self.d2h_bytes += n * 4
         self._out_event.record()
         self._out_event.synchronize()
         return self._out_pinned[:n].tolist()
@@ -345,8 +362,10 @@ class ModelRunner:
                 self._forward_and_sample(ids, pos, ctx, temps, topp)
             torch.cuda.synchronize(self.device)
             g = torch.cuda.CUDAGraph()
+            l0 = self._launch_count()
             with torch.cuda.graph(g, pool=self.graph_pool):
                 out = self._forward_and_sample(ids, pos, ctx, temps, topp)
+            self.graph_launches[bs] = self._launch_count() - l0
             if self.graph_pool is None:
                 self.graph_pool = g.pool()
             self.graphs[bs] = (g, out, pk.offsets)
@@ -358,8 +377,23 @@ class ModelRunner:
         assert pk.offsets == offsets
         total = sum(n for _, n in offsets.values())
         self._graph_buf[:total].copy_(self._pinned[:total], non_blocking=True)
+        self.h2d_bytes += total * 4
+        self._mark(0)
         g.replay()
+        self._mark(1)
+        self._add_launches(self.graph_launches.get(bs, 0))
         return self._fetch(out, len(seqs))
+
+    def _launch_count(self) -> int:
+        n = getattr(self.ops, "launches", 0)
+        if self.comm is not None:
+            n += getattr(self.comm, "launches", 0)
+        return n
+
+    def _add_launches(self, n: int) -> None:
+        # graph replays launch the captured kernels; attribute them to the op set
+        if hasattr(self.ops, "launches"):
+            self.ops.launches += n
 
     def release_graphs(self):
         self.graphs.clear()

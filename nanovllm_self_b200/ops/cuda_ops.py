@@ -32,6 +32,8 @@ class CudaOps:
         self.C = load()
         self._scratch: dict = {}
         self.num_sms = {}
+        # Number of kernels this op set has launched (graph replays are added by the runner).
+        self.launches = 0
 
     def scratch(self, device) -> _Scratch:
         key = torch.device(device).index
@@ -46,14 +48,17 @@ class CudaOps:
     def embedding(self, ids, w, vocab_start=0):
         out = torch.empty(ids.shape[0], w.shape[1], dtype=w.dtype, device=w.device)
         self.C.embedding(ids, w, int(vocab_start), out)
+        self.launches += 1
         return out
 
     def add_rmsnorm(self, x, residual, w, eps):
         out = torch.empty(x.shape[0], x.shape[1], dtype=x.dtype, device=x.device)
         if residual is None:
             self.C.add_rmsnorm(x, None, None, w, out, float(eps), None)
+            self.launches += 1
             return out, x
         self.C.add_rmsnorm(x, residual, residual, w, out, float(eps), None)
+        self.launches += 1
         return out, residual
 
     def add_rmsnorm_rows(self, h, residual, w, eps, rows):
@@ -61,6 +66,7 @@ class CudaOps:
         out = torch.empty(rows.shape[0], h.shape[1], dtype=h.dtype, device=h.device)
         res_out = torch.empty_like(out)
         self.C.add_rmsnorm(h, residual, res_out, w, out, float(eps), rows)
+        self.launches += 1
         return out, res_out
 
     def rmsnorm(self, x, w, eps):
@@ -69,6 +75,7 @@ class CudaOps:
     def silu_mul(self, x):
         out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device)
         self.C.silu_mul(x, out)
+        self.launches += 1
         return out
 
     # ----------------------------------------------------------------- GEMM
@@ -81,8 +88,10 @@ class CudaOps:
         plan = self.C.gemm_plan(x.shape[0], w.shape[0], x.shape[1])
         if plan[6] > ws.numel():
             self.C.linear(x, w, out, ws, -1, 0, 1)
+            self.launches += 1
         else:
             self.C.linear(x, w, out, ws)
+            self.launches += 1 + (1 if plan[4] > 1 else 0)
         return out
 
     # ------------------------------------------------------------ attention
@@ -91,6 +100,7 @@ class CudaOps:
         q = torch.empty(qkv.shape[0], nq * d, dtype=qkv.dtype, device=qkv.device)
         self.C.qkv_post(qkv, q, q_norm, k_norm, float(eps), positions, cos_sin, k_cache, v_cache,
                         k_scale, v_scale, slot_mapping, nq, nkv)
+        self.launches += 1
         return q
 
     def attention(self, q, k_cache, v_cache, ctx, scale, k_scale=None, v_scale=None):
@@ -107,9 +117,11 @@ class CudaOps:
                 splits //= 2
             self.C.attn_decode(q, k_cache, v_cache, k_scale, v_scale, ctx.block_tables, ctx.cu_seqlens_q,
                                ctx.context_lens, out, sc.part_o, sc.part_lse, nq, nkv, splits, 0, nd, float(scale))
+            self.launches += 2 if splits > 1 else 1
         if B > nd:
             self.C.attn_prefill(q, k_cache, v_cache, k_scale, v_scale, ctx.block_tables, ctx.cu_seqlens_q,
                                 ctx.context_lens, out, nq, nkv, nd, B - nd, max(1, ctx.max_seqlen_q), float(scale))
+            self.launches += 1
         return out
 
     # -------------------------------------------------------------- sampling
@@ -122,6 +134,7 @@ class CudaOps:
         nchunk = int(self.C.sample_chunks(rows, V))
         tok = torch.empty(rows, dtype=torch.int32, device=logits.device)
         self.C.sample(logits, int(col_offset), temperatures, step, sc.sample_val, sc.sample_idx, nchunk, tok, None)
+        self.launches += 2
         return tok
 
     def sample_partial(self, logits, temperatures, step, col_offset):
@@ -132,4 +145,5 @@ class CudaOps:
         tok = torch.empty(rows, dtype=torch.int32, device=logits.device)
         val = torch.empty(rows, dtype=torch.float32, device=logits.device)
         self.C.sample(logits, int(col_offset), temperatures, step, sc.sample_val, sc.sample_idx, nchunk, tok, val)
+        self.launches += 2
         return val, tok

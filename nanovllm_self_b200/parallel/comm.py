@@ -1,0 +1,80 @@
+"""Tensor-parallel communication for the model.
+
+The reference reduces the row-parallel o_proj/down_proj outputs with an in-place NCCL
+``all_reduce`` (``nanovllm/distributed/parallel_state.py:62-71``, called at
+``nanovllm/models/qwen3.py:124,138``) and keeps the embedding and lm_head replicated.
+
+Here every reduction is fused with what follows it:
+
+* ``allreduce_add_rmsnorm(h, residual, w)``: sum the per-rank partial ``h`` over the TP
+  group, add the residual, RMS-normalise.  Backend ``"fused"`` does all three in ONE
+  kernel that reads the peers' partials straight from their HBM over NVLink (symmetric
+  buffers, see :mod:`nanovllm_self_b200.parallel.symm`); backend ``"nccl"`` is the
+  reference's behaviour (NCCL all-reduce, then the local add+norm kernel) and is kept
+  as the measured baseline.
+* ``vocab_parallel_sample``: each rank holds ``V / tp`` logits; the sampler reduces
+  its shard to one (score, token) pair per row (greedy or Gumbel-max with a shared
+  counter-based noise stream) and only those pairs cross the link.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .state import TPState
+
+
+class TPComm:
+    def __init__(self, tp: TPState, backend: str = "fused", config=None):
+        self.tp = tp
+        self.backend = backend
+        self.config = config
+        self.runner = None
+        self.symm = None
+        self.ops = None
+        self.launches = 0
+
+    def bind(self, runner):
+        self.runner = runner
+        self.ops = runner.ops
+        if self.backend == "fused" and runner.is_cuda:
+            from .symm import SymmetricWorkspace
+            c = runner.config
+            rows = max(c.max_num_batched_tokens, c.cuda_graph_max_bs, c.max_num_seqs)
+            self.symm = SymmetricWorkspace(self.tp, rows=rows, hidden=runner.model.hidden_size)
+        elif self.backend == "fused":
+            self.backend = "nccl"  # CPU / gloo: no peer memory
+
+    # ------------------------------------------------------------ reductions
+    def allreduce_add_rmsnorm(self, h, residual, w, eps):
+        if self.symm is not None and h.shape[0] <= self.symm.rows:
+            return self.symm.allreduce_add_rmsnorm(h, residual, w, eps, self.ops)
+        dist.all_reduce(h, op=dist.ReduceOp.SUM, group=self.tp.group)
+        return self.ops.add_rmsnorm(h, residual, w, eps)
+
+    def all_reduce(self, x):
+        dist.all_reduce(x, op=dist.ReduceOp.SUM, group=self.tp.group)
+        return x
+
+    # ------------------------------------------------------------- sampling
+    def vocab_parallel_sample(self, logits, temps, topp, model, runner):
+        n = self.tp.size
+        use_top_p = getattr(runner, "_use_top_p", False)
+        if runner.is_cuda and not use_top_p:
+            val, tok = self.ops.sample_partial(logits, temps, runner._step_tensor(), model.vocab_start)
+            pair = torch.stack([val, tok.float()], dim=1)  # token ids < 2^24 are exact in fp32
+            out = torch.empty(n, *pair.shape, dtype=pair.dtype, device=pair.device)
+            dist.all_gather_into_tensor(out, pair.contiguous(), group=self.tp.group)
+            best = out[:, :, 0].argmax(dim=0)
+            return out[best, torch.arange(pair.shape[0], device=pair.device), 1].to(torch.int32)
+        # top-p (or CPU): gather the full logits; every rank samples identically
+        parts = [torch.empty_like(logits) for _ in range(n)]
+        dist.all_gather(parts, logits.contiguous(), group=self.tp.group)
+        full = torch.cat(parts, dim=1)[:, :model.vocab_size]
+        return self.ops.sample(full, temps, topp, step=runner._step_tensor(), generator=runner._gen,
+                               use_top_p=True, batch_greedy_compat=runner.config.batch_greedy_compat)
+
+    def close(self):
+        if self.symm is not None:
+            self.symm.close()
+            self.symm = None
