@@ -7,15 +7,19 @@
 //
 // Both kernels here read K/V straight from the paged pool [num_blocks, nkv, BS, 128]
 // (bf16, or fp8 e4m3 with one scale per block per head), any power-of-two block size,
-// and use bf16 mma.sync m16n8k16 tiles with fp32 accumulation; the tile loads are
-// cp.async into XOR-swizzled shared memory (conflict-free ldmatrix).
+// and use bf16 mma.sync m16n8k16 tiles with fp32 accumulation (attention is a small
+// share of the FLOPs here and decode is bandwidth-bound); tiles land in XOR-swizzled
+// shared memory (conflict-free ldmatrix), by TMA for decode and cp.async for prefill.
 //
 // decode:  grid (splits, nkv, B).  Each CTA takes all G = nq/nkv query heads of one KV
-//          head (packed as the 16 rows of one MMA tile) over one slice of the context,
-//          4 warps splitting each 64-key tile.  With splits > 1 the CTA writes a
-//          normalised partial output and its log2-sum-exp to scratch, and
-//          attn_combine merges the slices.
+//          head (packed as the 16 rows of one MMA tile) over one slice of the context.
+//          A producer warp streams K/V tiles with TMA; 4 consumer warps split each
+//          64-key tile.  With splits > 1 the CTA writes a normalised partial output and
+//          its log2-sum-exp to scratch, and attn_combine merges the slices.
 // prefill: grid (q tiles of 64, prefill seqs, nq).  4 warps x 16 query rows.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -127,16 +131,70 @@ __device__ __forceinline__ void convert_fp8_tile(const AttnArgs& a, const float*
 }
 
 // ------------------------------------------------------------------------- decode
+// Warp-specialised: warp 4 streams 64-key K/V tiles with TMA (128B swizzle) into a
+// DSTAGES-deep ring; warps 0-3 each own 16 keys of every tile and keep their own
+// online-softmax state, so consumers never wait on one another.  The last consumer
+// warp to finish merges the four partial states (found with a shared-memory counter,
+// no barrier).  Every mbarrier wait is time-bounded and reports through g_attn_error.
+constexpr int DSTAGES = 3;
+constexpr uint64_t ATT_WAIT_NS = 2000000000ull;
+
+__device__ int g_attn_error = 0;
+
+__device__ __forceinline__ uint64_t att_timer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool att_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool att_wait(uint32_t bar, uint32_t parity, int code) {
+  if (att_try(bar, parity)) return true;
+  const uint64_t t0 = att_timer();
+  while (!att_try(bar, parity)) {
+    if (att_timer() - t0 > ATT_WAIT_NS) {
+      atomicCAS(&g_attn_error, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+struct DecodeArgs {
+  AttnArgs a;
+  int rows_per_box;  // min(64, block_size)
+  int kv_fp8;
+};
+
+// Swizzled (TMA 128B pattern) bf16 tile: [2 halves of 64 dims][64 rows][128 B].
+__device__ __forceinline__ uint32_t tswz(int r, int c16) {
+  return (uint32_t)((c16 >> 3) * 8192 + r * 128 + ((((c16 & 7) ^ (r & 7))) << 4));
+}
+
 template <bool FP8>
-__global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* sq = smem;                                  // 16 x 256 B
-  uint8_t* sk = smem + 16 * ROWB;                      // 2 stages x 64 x 256 B
-  uint8_t* sv = sk + 2 * KTILE * ROWB;                 // 2 stages
-  uint8_t* stg = sv + 2 * KTILE * ROWB;                // fp8 staging: K,V x 2 stages x 64 x 128 B
+__global__ void __launch_bounds__(160, 2)
+    attn_decode_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                           DecodeArgs da) {
+  const AttnArgs& a = da.a;
+  extern __shared__ __align__(1024) uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int KV_TILE = FP8 ? KTILE * AD : KTILE * ROWB;  // bytes of one K (or V) tile
+  constexpr int STAGE = 2 * KV_TILE;
+  uint8_t* conv = dsm + DSTAGES * STAGE;                          // fp8: per-warp bf16 staging 4 x 8 KB
+  const int G = a.nq / a.nkv;
+  uint8_t* comb = conv + (FP8 ? 4 * 8192 : 0);                    // combine: [4][G][128] f32 + [4][16][2] f32
+  uint64_t* bars = reinterpret_cast<uint64_t*>(comb + 4 * G * AD * 4 + 4 * 16 * 2 * 4);
+  int* done_ctr = reinterpret_cast<int*>(bars + 2 * DSTAGES);
+  const uint32_t bar0 = smem_u32(bars);
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z + a.seq_offset;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int G = a.nq / a.nkv;
   const int k_len = a.ctx_lens[b];
   const int qrow = a.cu_q[b];
   const int n_tiles = (k_len + KTILE - 1) / KTILE;
@@ -145,92 +203,180 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
   const int t1 = min(n_tiles, t0 + per);
   const int qh0 = h * G;
 
-  if (t0 >= t1) {  // empty slice
+  if (t0 >= t1) {
     if (a.splits > 1) {
-      for (int r = threadIdx.x; r < G; r += 128) a.part_lse[((int64_t)b * a.nq + qh0 + r) * a.splits + split] = -INFINITY;
+      for (int r = threadIdx.x; r < G; r += blockDim.x)
+        a.part_lse[((int64_t)b * a.nq + qh0 + r) * a.splits + split] = -INFINITY;
     } else {
-      for (int i = threadIdx.x; i < G * AD; i += 128)
+      for (int i = threadIdx.x; i < G * AD; i += blockDim.x)
         a.out[((int64_t)qrow * a.nq + qh0) * AD + i] = __float2bfloat16(0.f);
     }
     return;
   }
-
-  // Q rows (G heads, zero padded to 16)
-  for (int idx = threadIdx.x; idx < 16 * 16; idx += 128) {
-    int r = idx >> 4, c = idx & 15;
-    bool v = r < G;
-    const __nv_bfloat16* src = a.q + ((int64_t)qrow * a.nq + qh0 + (v ? r : 0)) * AD + c * 8;
-    cp_async16(smem_u32(sq) + swz(r, c), src, v);
-  }
-  const void* kc = a.k_cache;
-  const void* vc = a.v_cache;
-  auto issue = [&](int tile, int st) {
-    if (FP8) {
-      load_tile<true>(a, kc, b, h, tile, k_len, smem_u32(stg) + st * KTILE * AD);
-      load_tile<true>(a, vc, b, h, tile, k_len, smem_u32(stg) + (2 + st) * KTILE * AD);
-    } else {
-      load_tile<false>(a, kc, b, h, tile, k_len, smem_u32(sk) + st * KTILE * ROWB);
-      load_tile<false>(a, vc, b, h, tile, k_len, smem_u32(sv) + st * KTILE * ROWB);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < DSTAGES; ++s) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8u * s));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;" ::"r"(bar0 + 8u * (DSTAGES + s)));
     }
-  };
-  issue(t0, 0);
-  cp_commit();
+    *done_ctr = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
 
+  if (warp == 4) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      const int* bt = a.block_tables + (int64_t)b * a.W;
+      const int rpb = da.rows_per_box;
+      const int nsub = KTILE / rpb;
+      bool ok = true;
+      int issued = 0;
+      for (int t = t0; t < t1; ++t, ++issued) {
+        const int i = t - t0, s = i % DSTAGES;
+        const uint32_t round = i / DSTAGES;
+        if (!att_wait(bar0 + 8u * (DSTAGES + s), (round & 1) ^ 1, 1)) {
+          ok = false;
+          break;
+        }
+        const uint32_t full = bar0 + 8u * s;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full), "r"(STAGE) : "memory");
+        const uint32_t kdst = smem_u32(dsm + s * STAGE), vdst = kdst + KV_TILE;
+        for (int j = 0; j < nsub; ++j) {
+          const int tok = t * KTILE + j * rpb;
+          const int bi = tok / a.block_size;
+          int blk = bi < a.W ? bt[bi] : 0;
+          if (blk < 0 || blk >= a.num_blocks) blk = 0;
+          const int row = (blk * a.nkv + h) * a.block_size + (tok % a.block_size);
+          if (FP8) {
+            const uint32_t off = j * rpb * AD;
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+                "[%2];" ::"r"(kdst + off), "l"(reinterpret_cast<uint64_t>(&kmap)), "r"(full), "r"(0), "r"(row)
+                : "memory");
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+                "[%2];" ::"r"(vdst + off), "l"(reinterpret_cast<uint64_t>(&vmap)), "r"(full), "r"(0), "r"(row)
+                : "memory");
+          } else {
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const uint32_t off = half * 8192 + j * rpb * 128;
+              asm volatile(
+                  "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+                  "[%2];" ::"r"(kdst + off), "l"(reinterpret_cast<uint64_t>(&kmap)), "r"(full), "r"(half * 64),
+                  "r"(row)
+                  : "memory");
+              asm volatile(
+                  "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+                  "[%2];" ::"r"(vdst + off), "l"(reinterpret_cast<uint64_t>(&vmap)), "r"(full), "r"(half * 64),
+                  "r"(row)
+                  : "memory");
+            }
+          }
+        }
+      }
+      // Do not leave while copies this thread issued may still be landing.
+      const int n = issued < DSTAGES ? issued : DSTAGES;
+      for (int i = issued - n; i < issued; ++i) {
+        const uint32_t full = bar0 + 8u * (i % DSTAGES);
+        const uint64_t tw = att_timer();
+        while (!att_try(full, (i / DSTAGES) & 1) && att_timer() - tw < ATT_WAIT_NS) {
+        }
+      }
+      (void)ok;
+    }
+    return;
+  }
+
+  // --------------------------------------------------------------- consumers
+  // Q fragments straight from global memory (rows >= G are zero)
   uint32_t qf[8][4];
+  {
+    const int r0 = lane >> 2, r1 = r0 + 8;
+    const __nv_bfloat16* q0p = a.q + ((int64_t)qrow * a.nq + qh0 + (r0 < G ? r0 : 0)) * AD;
+    const __nv_bfloat16* q1p = a.q + ((int64_t)qrow * a.nq + qh0 + (r1 < G ? r1 : 0)) * AD;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int c = kk * 16 + (lane & 3) * 2;
+      qf[kk][0] = r0 < G ? *reinterpret_cast<const uint32_t*>(q0p + c) : 0u;
+      qf[kk][1] = r1 < G ? *reinterpret_cast<const uint32_t*>(q1p + c) : 0u;
+      qf[kk][2] = r0 < G ? *reinterpret_cast<const uint32_t*>(q0p + c + 8) : 0u;
+      qf[kk][3] = r1 < G ? *reinterpret_cast<const uint32_t*>(q1p + c + 8) : 0u;
+    }
+  }
   float acc[16][4];
 #pragma unroll
   for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  bool q_loaded = false;
+  const int* bt = a.block_tables + (int64_t)b * a.W;
+  uint8_t* myconv = conv + warp * 8192;  // fp8 only: 2 x [16 rows][256 B]
 
   for (int t = t0; t < t1; ++t) {
-    const int st = (t - t0) & 1;
-    if (t + 1 < t1) {
-      issue(t + 1, st ^ 1);
-      cp_commit();
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
-    }
-    __syncthreads();
-    int cs = st;
+    const int i = t - t0, s = i % DSTAGES;
+    if (!att_wait(bar0 + 8u * s, (i / DSTAGES) & 1, 2)) break;
+    const uint8_t* kt = dsm + s * STAGE;
+    const uint8_t* vt = kt + KV_TILE;
+    uint32_t kb, vb;  // ldmatrix bases; rows are addressed as warp-local 0..15 (+ warp*16 for TMA tiles)
+    int rbase;
     if (FP8) {
-      convert_fp8_tile(a, a.k_scale, b, h, t, k_len, stg + st * KTILE * AD, sk);
-      convert_fp8_tile(a, a.v_scale, b, h, t, k_len, stg + (2 + st) * KTILE * AD, sv);
-      __syncthreads();
-      cs = 0;
-    }
-    if (!q_loaded) {
+      // dequantise this warp's 16 K rows and 16 V rows into its bf16 staging (row 256 B, xor swizzle)
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        int r = (lane & 7) + ((lane >> 3) & 1) * 8, c = kk * 2 + (lane >> 4);
-        ldsm_x4(smem_u32(sq) + swz(r, c), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      for (int it = 0; it < 4; ++it) {
+        const int idx = lane + it * 32;       // 0..127 -> (row 0..15, 16-byte fp8 chunk 0..7)
+        const int r = idx >> 3, c = idx & 7;
+        const int gr = warp * 16 + r;
+        const int tok = t * KTILE + gr;
+        const int bi = tok / a.block_size;
+        int blk = bi < a.W ? bt[bi] : 0;
+        if (blk < 0 || blk >= a.num_blocks) blk = 0;
+        const float ksc = a.k_scale[(int64_t)blk * a.nkv + h], vsc = a.v_scale[(int64_t)blk * a.nkv + h];
+        const uint32_t soff = gr * 128 + ((c ^ (gr & 7)) << 4);
+        const uint4 kr = *reinterpret_cast<const uint4*>(kt + soff);
+        const uint4 vr = *reinterpret_cast<const uint4*>(vt + soff);
+        float f[16];
+        e4m3x4_to_f32(kr.x, f); e4m3x4_to_f32(kr.y, f + 4); e4m3x4_to_f32(kr.z, f + 8); e4m3x4_to_f32(kr.w, f + 12);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) f[j] *= ksc;
+        *reinterpret_cast<uint4*>(myconv + swz(r, 2 * c)) = f32_to_bf16x8(f);
+        *reinterpret_cast<uint4*>(myconv + swz(r, 2 * c + 1)) = f32_to_bf16x8(f + 8);
+        e4m3x4_to_f32(vr.x, f); e4m3x4_to_f32(vr.y, f + 4); e4m3x4_to_f32(vr.z, f + 8); e4m3x4_to_f32(vr.w, f + 12);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) f[j] *= vsc;
+        *reinterpret_cast<uint4*>(myconv + 4096 + swz(r, 2 * c)) = f32_to_bf16x8(f);
+        *reinterpret_cast<uint4*>(myconv + 4096 + swz(r, 2 * c + 1)) = f32_to_bf16x8(f + 8);
       }
-      q_loaded = true;
+      __syncwarp();
+      // the fp8 stage is no longer needed by this warp
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar0 + 8u * (DSTAGES + s)) : "memory");
+      kb = smem_u32(myconv);
+      vb = kb + 4096;
+      rbase = 0;
+    } else {
+      kb = smem_u32(kt);
+      vb = smem_u32(vt);
+      rbase = warp * 16;
     }
-    const uint32_t kb = smem_u32(sk) + cs * KTILE * ROWB;
-    const uint32_t vb = smem_u32(sv) + cs * KTILE * ROWB;
-    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
       uint32_t b0, b1, b2, b3;
-      int r = warp * 16 + (lane & 7) + ((lane >> 4) << 3), c = kk * 2 + ((lane >> 3) & 1);
-      ldsm_x4(kb + swz(r, c), b0, b1, b2, b3);
-      mma_bf16(s[0], qf[kk], b0, b1);
-      mma_bf16(s[1], qf[kk], b2, b3);
+      const int r = rbase + (lane & 7) + ((lane >> 4) << 3), c = kk * 2 + ((lane >> 3) & 1);
+      ldsm_x4(kb + (FP8 ? swz(r, c) : tswz(r, c)), b0, b1, b2, b3);
+      mma_bf16(sc[0], qf[kk], b0, b1);
+      mma_bf16(sc[1], qf[kk], b2, b3);
     }
-    // scale, mask, online softmax (rows lane/4 and lane/4 + 8)
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        int key = t * KTILE + warp * 16 + nt * 8 + (lane & 3) * 2 + e;
-        bool ok = key < k_len;
-        s[nt][e] = ok ? s[nt][e] * a.scale_log2 : -INFINITY;
-        s[nt][2 + e] = ok ? s[nt][2 + e] * a.scale_log2 : -INFINITY;
-        mx0 = fmaxf(mx0, s[nt][e]);
-        mx1 = fmaxf(mx1, s[nt][2 + e]);
+        const int key = t * KTILE + warp * 16 + nt * 8 + (lane & 3) * 2 + e;
+        const bool ok = key < k_len;
+        sc[nt][e] = ok ? sc[nt][e] * a.scale_log2 : -INFINITY;
+        sc[nt][2 + e] = ok ? sc[nt][2 + e] * a.scale_log2 : -INFINITY;
+        mx0 = fmaxf(mx0, sc[nt][e]);
+        mx1 = fmaxf(mx1, sc[nt][2 + e]);
       }
     }
     mx0 = fmaxf(mx0, __shfl_xor_sync(FULL_MASK, mx0, 1));
@@ -246,42 +392,48 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
     float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      p[nt][0] = exp2f(s[nt][0] - base0);
-      p[nt][1] = exp2f(s[nt][1] - base0);
-      p[nt][2] = exp2f(s[nt][2] - base1);
-      p[nt][3] = exp2f(s[nt][3] - base1);
+      p[nt][0] = exp2f(sc[nt][0] - base0);
+      p[nt][1] = exp2f(sc[nt][1] - base0);
+      p[nt][2] = exp2f(sc[nt][2] - base1);
+      p[nt][3] = exp2f(sc[nt][3] - base1);
       rs0 += p[nt][0] + p[nt][1];
       rs1 += p[nt][2] + p[nt][3];
     }
     l0 = l0 * al0 + rs0;
     l1 = l1 * al1 + rs1;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      acc[i][0] *= al0;
-      acc[i][1] *= al0;
-      acc[i][2] *= al1;
-      acc[i][3] *= al1;
+    for (int j = 0; j < 16; ++j) {
+      acc[j][0] *= al0;
+      acc[j][1] *= al0;
+      acc[j][2] *= al1;
+      acc[j][3] *= al1;
     }
-    uint32_t pa[4] = {pack_bf16(p[0][0], p[0][1]), pack_bf16(p[0][2], p[0][3]), pack_bf16(p[1][0], p[1][1]),
-                      pack_bf16(p[1][2], p[1][3])};
+    const uint32_t pa[4] = {pack_bf16(p[0][0], p[0][1]), pack_bf16(p[0][2], p[0][3]), pack_bf16(p[1][0], p[1][1]),
+                            pack_bf16(p[1][2], p[1][3])};
 #pragma unroll
     for (int np = 0; np < 8; ++np) {
       uint32_t b0, b1, b2, b3;
-      int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, c = np * 2 + (lane >> 4);
-      ldsm_x4_t(vb + swz(r, c), b0, b1, b2, b3);
+      const int r = rbase + (lane & 7) + ((lane >> 3) & 1) * 8, c = np * 2 + (lane >> 4);
+      ldsm_x4_t(vb + (FP8 ? swz(r, c) : tswz(r, c)), b0, b1, b2, b3);
       mma_bf16(acc[2 * np], pa, b0, b1);
       mma_bf16(acc[2 * np + 1], pa, b2, b3);
     }
-    __syncthreads();
+    if (!FP8) {
+      __syncwarp();
+      if (lane == 0)
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar0 + 8u * (DSTAGES + s)) : "memory");
+    } else {
+      __syncwarp();  // staging is rewritten next tile
+    }
   }
 
-  // quad-reduce l, then combine the 4 warps through shared memory
+  // publish this warp's state; the last warp to arrive merges all four
   l0 += __shfl_xor_sync(FULL_MASK, l0, 1);
   l0 += __shfl_xor_sync(FULL_MASK, l0, 2);
   l1 += __shfl_xor_sync(FULL_MASK, l1, 1);
   l1 += __shfl_xor_sync(FULL_MASK, l1, 2);
-  float* sm_acc = reinterpret_cast<float*>(sk);               // [4][16][128]
-  float* sm_ml = reinterpret_cast<float*>(sk + 4 * 16 * AD * 4);  // [4][16][2]
+  float* sm_acc = reinterpret_cast<float*>(comb);
+  float* sm_ml = sm_acc + 4 * G * AD;
   const int r0 = lane >> 2, r1 = r0 + 8;
   if ((lane & 3) == 0) {
     sm_ml[(warp * 16 + r0) * 2] = m0;
@@ -291,15 +443,19 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
   }
 #pragma unroll
   for (int nt = 0; nt < 16; ++nt) {
-    int c = nt * 8 + (lane & 3) * 2;
-    sm_acc[(warp * 16 + r0) * AD + c] = acc[nt][0];
-    sm_acc[(warp * 16 + r0) * AD + c + 1] = acc[nt][1];
-    sm_acc[(warp * 16 + r1) * AD + c] = acc[nt][2];
-    sm_acc[(warp * 16 + r1) * AD + c + 1] = acc[nt][3];
+    const int c = nt * 8 + (lane & 3) * 2;
+    if (r0 < G) *reinterpret_cast<float2*>(sm_acc + (warp * G + r0) * AD + c) = make_float2(acc[nt][0], acc[nt][1]);
+    if (r1 < G) *reinterpret_cast<float2*>(sm_acc + (warp * G + r1) * AD + c) = make_float2(acc[nt][2], acc[nt][3]);
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < G * AD; i += 128) {
-    int r = i / AD, c = i % AD;
+  __threadfence_block();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = atomicAdd(done_ctr, 1) == 3;
+  last = __shfl_sync(FULL_MASK, last, 0);
+  if (!last) return;
+  __threadfence_block();
+  for (int i = lane; i < G * AD; i += 32) {
+    const int r = i / AD, c = i % AD;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_ml[(w * 16 + r) * 2]);
@@ -307,16 +463,16 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
-        float f = exp2f(sm_ml[(w * 16 + r) * 2] - M);
+        const float f = exp2f(sm_ml[(w * 16 + r) * 2] - M);
         L += sm_ml[(w * 16 + r) * 2 + 1] * f;
-        O += sm_acc[(w * 16 + r) * AD + c] * f;
+        O += sm_acc[(w * G + r) * AD + c] * f;
       }
     }
-    float o = L > 0.f ? O / L : 0.f;
+    const float o = L > 0.f ? O / L : 0.f;
     if (a.splits == 1) {
       a.out[((int64_t)qrow * a.nq + qh0 + r) * AD + c] = __float2bfloat16(o);
     } else {
-      int64_t pi = ((int64_t)b * a.nq + qh0 + r) * a.splits + split;
+      const int64_t pi = ((int64_t)b * a.nq + qh0 + r) * a.splits + split;
       a.part_o[pi * AD + c] = o;
       if (c == 0) a.part_lse[pi] = L > 0.f ? M + log2f(L) : -INFINITY;
     }
@@ -512,7 +668,6 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
   }
 }
 
-static int decode_smem(bool fp8) { return 16 * ROWB + 4 * KTILE * ROWB + (fp8 ? 4 * KTILE * AD : 0); }
 static int prefill_smem(bool fp8) { return KTILE * ROWB + 4 * KTILE * ROWB + (fp8 ? 4 * KTILE * AD : 0); }
 
 int attn_decode_splits(int num_seqs, int nkv, int max_ctx, int num_sms) {
@@ -524,11 +679,44 @@ int attn_decode_splits(int num_seqs, int nkv, int max_ctx, int num_sms) {
   return s < 1 ? 1 : s;
 }
 
+static PFN_cuTensorMapEncodeTiled_v12000 attn_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D view [num_blocks * nkv * block_size rows, 128 dims] of one layer's K or V pool.
+static bool kv_map(CUtensorMap* m, const void* base, int64_t rows, bool fp8, int box_rows) {
+  auto enc = attn_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)AD, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(fp8 ? AD : AD * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)(fp8 ? 128 : 64), (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static int decode_tma_smem(bool fp8, int G) {
+  const int stage = 2 * (fp8 ? KTILE * AD : KTILE * ROWB);
+  return 1024 + DSTAGES * stage + (fp8 ? 4 * 8192 : 0) + 4 * G * AD * 4 + 4 * 16 * 2 * 4 + 2 * DSTAGES * 8 + 16;
+}
+
 cudaError_t launch_attn_decode(const AttnLaunch& L, cudaStream_t stream) {
   if (L.num_seqs == 0) return cudaSuccess;
   if (L.head_dim != AD || L.nq % L.nkv || L.nq / L.nkv > 16) return cudaErrorInvalidValue;
   if (L.splits > 1 && (!L.part_o || !L.part_lse)) return cudaErrorInvalidValue;
-  AttnArgs a;
+  if (L.block_size & (L.block_size - 1)) return cudaErrorInvalidValue;
+  if (((uintptr_t)L.k_cache & 15) || ((uintptr_t)L.v_cache & 15)) return cudaErrorMisalignedAddress;
+  DecodeArgs da;
+  AttnArgs& a = da.a;
   a.q = static_cast<const __nv_bfloat16*>(L.q);
   a.k_cache = L.k_cache;
   a.v_cache = L.v_cache;
@@ -548,14 +736,29 @@ cudaError_t launch_attn_decode(const AttnLaunch& L, cudaStream_t stream) {
   a.splits = L.splits;
   a.seq_offset = L.seq_offset;
   a.scale_log2 = L.softmax_scale * LOG2E;
+  da.rows_per_box = L.block_size < KTILE ? L.block_size : KTILE;
+  da.kv_fp8 = L.kv_fp8;
+  const int64_t rows = (int64_t)L.num_blocks * L.nkv * L.block_size;
+  CUtensorMap km, vm;
+  if (!kv_map(&km, L.k_cache, rows, L.kv_fp8, da.rows_per_box) || !kv_map(&vm, L.v_cache, rows, L.kv_fp8, da.rows_per_box))
+    return cudaErrorInvalidValue;
   dim3 grid(L.splits, L.nkv, L.num_seqs);
-  int sm = decode_smem(L.kv_fp8);
+  const int sm = decode_tma_smem(L.kv_fp8, L.nq / L.nkv);
+  const int sm_max = decode_tma_smem(L.kv_fp8, 16);
   if (L.kv_fp8) {
-    cudaFuncSetAttribute(attn_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-    attn_decode_kernel<true><<<grid, 128, sm, stream>>>(a);
+    static bool cfg = false;
+    if (!cfg) {
+      cudaFuncSetAttribute(attn_decode_tma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_max);
+      cfg = true;
+    }
+    attn_decode_tma_kernel<true><<<grid, 160, sm, stream>>>(km, vm, da);
   } else {
-    cudaFuncSetAttribute(attn_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-    attn_decode_kernel<false><<<grid, 128, sm, stream>>>(a);
+    static bool cfg = false;
+    if (!cfg) {
+      cudaFuncSetAttribute(attn_decode_tma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_max);
+      cfg = true;
+    }
+    attn_decode_tma_kernel<false><<<grid, 160, sm, stream>>>(km, vm, da);
   }
   NVB_LAUNCH_CHECK();
   if (L.splits > 1) {
@@ -564,6 +767,16 @@ cudaError_t launch_attn_decode(const AttnLaunch& L, cudaStream_t stream) {
     NVB_LAUNCH_CHECK();
   }
   return cudaSuccess;
+}
+
+int attn_error_code(int reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_attn_error, sizeof(int));
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_attn_error, &z, sizeof(int));
+  }
+  return v;
 }
 
 cudaError_t launch_attn_prefill(const AttnLaunch& L, int max_q_len, cudaStream_t stream) {

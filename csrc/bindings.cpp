@@ -153,6 +153,8 @@ int64_t decode_splits(int64_t num_seqs, int64_t nkv, int64_t max_ctx, int64_t nu
   return nvb::attn_decode_splits((int)num_seqs, (int)nkv, (int)max_ctx, (int)num_sms);
 }
 
+int64_t attn_error(bool reset) { return nvb::attn_error_code(reset ? 1 : 0); }
+
 int64_t sample_chunks(int64_t rows, int64_t V) { return nvb::sample_num_chunks((int)rows, (int)V); }
 
 void sample(const at::Tensor& logits, int64_t col_offset, const at::Tensor& temps, const at::Tensor& seed_step,
@@ -186,6 +188,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_decode", &attn_decode);
   m.def("attn_prefill", &attn_prefill);
   m.def("decode_splits", &decode_splits);
+  m.def("attn_error", &attn_error, pybind11::arg("reset") = false);
   m.def("sample_chunks", &sample_chunks);
   m.def("sample", &sample);
   register_gemm(m);

@@ -9,7 +9,7 @@ namespace {
 
 // out[m, n] = x[m, k] @ w[n, k]^T   (bf16 in/out, fp32 accumulation)
 void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c10::optional<at::Tensor>& ws,
-            int64_t force_swap, int64_t force_bn, int64_t force_splits) {
+            const c10::optional<at::Tensor>& counters, int64_t force_swap, int64_t force_bn, int64_t force_splits) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
                   out.scalar_type() == at::kBFloat16, "bf16 required");
@@ -19,20 +19,41 @@ void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c10
   TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == n, "shape mismatch");
   auto pl = nvb::gemm_plan(m, n, k, (int)force_swap, (int)force_bn, (int)force_splits);
   float* wsp = nullptr;
+  int* ctr = nullptr;
   if (pl.ws_elems > 0) {
     TORCH_CHECK(ws.has_value() && ws->scalar_type() == at::kFloat && ws->numel() >= pl.ws_elems,
                 "split-K scratch too small: need ", pl.ws_elems, " fp32 elements");
+    TORCH_CHECK(counters.has_value() && counters->scalar_type() == at::kInt && counters->numel() >= 4 * pl.tiles,
+                "split-K counters too small: need ", 4 * pl.tiles);
     wsp = ws->data_ptr<float>();
+    ctr = counters->data_ptr<int>();
   }
   at::cuda::CUDAGuard g(x.device());
   cudaError_t e = nvb::gemm_bf16(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0),
-                                 m, n, k, pl, wsp, at::cuda::getCurrentCUDAStream().stream());
+                                 m, n, k, pl, wsp, ctr, at::cuda::getCurrentCUDAStream().stream());
   TORCH_CHECK(e == cudaSuccess, "gemm_bf16 failed: ", cudaGetErrorString(e));
+}
+
+// Autotuned entry point used by the model (see gemm_bf16_tuned).
+std::vector<int64_t> linear_tuned(const at::Tensor& x, const at::Tensor& w, at::Tensor& out) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16, "bf16 required");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "2-D tensors required");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "unit inner stride required");
+  const int m = (int)x.size(0), k = (int)x.size(1), n = (int)w.size(0);
+  TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == n, "shape mismatch");
+  at::cuda::CUDAGuard g(x.device());
+  nvb::GemmPlan pl{};
+  cudaError_t e = nvb::gemm_bf16_tuned(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(),
+                                       out.stride(0), m, n, k, at::cuda::getCurrentCUDAStream().stream(), &pl);
+  TORCH_CHECK(e == cudaSuccess, "gemm_bf16 failed: ", cudaGetErrorString(e));
+  return {pl.swap, pl.bn, pl.tiles_p, pl.tiles_q, pl.splits, pl.grid};
 }
 
 std::vector<int64_t> plan(int64_t m, int64_t n, int64_t k) {
   auto pl = nvb::gemm_plan((int)m, (int)n, (int)k, -1, 0, 0);
-  return {pl.swap, pl.bn, pl.tiles_p, pl.tiles_q, pl.splits, pl.grid, pl.ws_elems};
+  return {pl.swap, pl.bn, pl.tiles_p, pl.tiles_q, pl.splits, pl.grid, pl.ws_elems, 4 * (int64_t)pl.tiles};
 }
 
 int64_t error_code(bool reset) { return nvb::gemm_error_code(reset ? 1 : 0); }
@@ -41,8 +62,10 @@ int64_t error_code(bool reset) { return nvb::gemm_error_code(reset ? 1 : 0); }
 
 void register_gemm(pybind11::module& m) {
   m.def("linear", &linear, "tcgen05 GEMM out = x @ w^T", pybind11::arg("x"), pybind11::arg("w"),
-        pybind11::arg("out"), pybind11::arg("ws") = c10::nullopt, pybind11::arg("force_swap") = -1,
+        pybind11::arg("out"), pybind11::arg("ws") = c10::nullopt, pybind11::arg("counters") = c10::nullopt,
+        pybind11::arg("force_swap") = -1,
         pybind11::arg("force_bn") = 0, pybind11::arg("force_splits") = 0);
   m.def("gemm_plan", &plan);
+  m.def("linear_tuned", &linear_tuned, "autotuned tcgen05 GEMM out = x @ w^T");
   m.def("gemm_error", &error_code, pybind11::arg("reset") = false);
 }

@@ -40,6 +40,8 @@ struct AttnLaunch {
 int attn_decode_splits(int num_seqs, int nkv, int max_ctx, int num_sms);
 cudaError_t launch_attn_decode(const AttnLaunch& L, cudaStream_t stream);
 cudaError_t launch_attn_prefill(const AttnLaunch& L, int max_q_len, cudaStream_t stream);
+// Error word set by an attention kernel that gave up on a bounded wait (0 = none).
+int attn_error_code(int reset);
 
 int sample_num_chunks(int rows, int V);
 cudaError_t launch_sample(const void* logits, int logits_is_bf16, int64_t ld, int rows, int V, int64_t col_offset,

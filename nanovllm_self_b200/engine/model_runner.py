@@ -175,11 +175,14 @@ class ModelRunner:
         need = [i for i, s in enumerate(seqs) if s.is_need_logits]
         S = len(need) if pad_to is None else Bp
         n_decode = 0
-        for s in seqs:
-            if s.num_new_tokens == 1 and s.is_prefill_done:
-                n_decode += 1
-            else:
-                break
+        if pad_to is not None:
+            n_decode = B  # graph buckets only ever serve pure decode steps
+        else:
+            for s in seqs:
+                if s.num_new_tokens == 1 and s.is_prefill_done:
+                    n_decode += 1
+                else:
+                    break
         # segments
         offs = {}
         o = 0
@@ -241,10 +244,10 @@ class ModelRunner:
         pk.T, pk.B, pk.W, pk.S, pk.n_decode = Tp, Bp, W, S, n_decode if n_decode < B else Bp
         pk.offsets, pk.host, pk.need = offs, host, need
         pk.q_lens, pk.k_lens = q_lens + [1] * (Bp - B), k_lens + [0] * (Bp - B)
-        pk.max_q, pk.max_k = max(q_lens), max(k_lens)
-        if pad_to is not None:
-            # a captured graph serves any context length up to max_model_len
-            pk.max_k = self.config.max_model_len
+        pk.max_q = max(q_lens)
+        # The split-KV decode partition depends only on the batch size and max_model_len,
+        # so a captured graph and an eager step of the same batch compute identically.
+        pk.max_k = self.config.max_model_len
         return pk
 
     def _to_device(self, pk: _Packed, dev_buf: torch.Tensor | None = None):

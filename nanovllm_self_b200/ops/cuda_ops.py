@@ -12,6 +12,7 @@ from . import torch_ref as R
 from ._ext import load
 
 _GEMM_WS_ELEMS = 16 << 20        # fp32 split-K scratch (64 MiB)
+_GEMM_COUNTERS = 1 << 16         # split-K arrival counters (4 per output tile)
 _ATTN_PART_ROWS = 1 << 16        # (seq, q head, split) rows of split-KV scratch
 _SAMPLE_PART = 1 << 16
 
@@ -19,6 +20,7 @@ _SAMPLE_PART = 1 << 16
 class _Scratch:
     def __init__(self, device):
         self.gemm = torch.empty(_GEMM_WS_ELEMS, dtype=torch.float32, device=device)
+        self.gemm_counters = torch.zeros(_GEMM_COUNTERS, dtype=torch.int32, device=device)
         self.part_o = torch.empty(_ATTN_PART_ROWS * 128, dtype=torch.float32, device=device)
         self.part_lse = torch.empty(_ATTN_PART_ROWS, dtype=torch.float32, device=device)
         self.sample_val = torch.empty(_SAMPLE_PART, dtype=torch.float32, device=device)
@@ -34,6 +36,7 @@ class CudaOps:
         self.num_sms = {}
         # Number of kernels this op set has launched (graph replays are added by the runner).
         self.launches = 0
+        self._plans: dict = {}
 
     def scratch(self, device) -> _Scratch:
         key = torch.device(device).index
@@ -84,15 +87,16 @@ class CudaOps:
             out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
         if x.shape[0] == 0:
             return out
-        ws = self.scratch(x.device).gemm
-        plan = self.C.gemm_plan(x.shape[0], w.shape[0], x.shape[1])
-        if plan[6] > ws.numel():
-            self.C.linear(x, w, out, ws, -1, 0, 1)
-            self.launches += 1
-        else:
-            self.C.linear(x, w, out, ws)
-            self.launches += 1 + (1 if plan[4] > 1 else 0)
+        self.C.linear_tuned(x, w, out)
+        self.launches += 1
         return out
+
+    def _plan(self, m, n, k):
+        key = (m, n, k)
+        p = self._plans.get(key)
+        if p is None:
+            p = self._plans[key] = self.C.gemm_plan(m, n, k)
+        return p
 
     # ------------------------------------------------------------ attention
     def qkv_post(self, qkv, q_norm, k_norm, eps, positions, cos_sin, k_cache, v_cache, slot_mapping,

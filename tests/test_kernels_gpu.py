@@ -200,5 +200,7 @@ def test_gemm_forced_configs(ops, swap, bn, splits):
     x = torch.randn(m, k, device=DEV).bfloat16()
     w = (torch.randn(n, k, device=DEV) * 0.05).bfloat16()
     out = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
-    ops.C.linear(x, w, out, ops.scratch(x.device).gemm, swap, bn, splits)
+    sc = ops.scratch(x.device)
+    ops.C.linear(x, w, out, sc.gemm, sc.gemm_counters, swap, bn, splits)
+    assert int(sc.gemm_counters.abs().sum()) == 0  # the fix-up leaves the counters at zero
     _close(out, x.float() @ w.float().t(), 0.05, 0.02)
