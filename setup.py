@@ -15,6 +15,7 @@ CSRC = os.path.join(ROOT, "csrc")
 SOURCES = [
     "bindings.cpp", "gemm_bind.cpp", "comm_bind.cpp",
     "norm_act.cu", "qkv_rope_kv.cu", "attention.cu", "sampling.cu", "gemm_tcgen05.cu", "comm.cu",
+    "attn_decode_noalloc.cu",
 ]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
