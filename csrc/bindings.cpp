@@ -178,6 +178,7 @@ void sample(const at::Tensor& logits, int64_t col_offset, const at::Tensor& temp
 }  // namespace
 
 void register_gemm(pybind11::module& m);
+void register_comm(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nanovllm_self_b200 sm_100a kernels";
@@ -192,4 +193,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample_chunks", &sample_chunks);
   m.def("sample", &sample);
   register_gemm(m);
+  register_comm(m);
 }

@@ -1,0 +1,202 @@
+// Tensor-parallel all-reduce fused with residual add + RMSNorm, over NVLink peer memory.
+//
+// Replaces the reference's NCCL all_reduce after o_proj / down_proj
+// (nanovllm/distributed/parallel_state.py:62-71, called at nanovllm/models/qwen3.py:124,138)
+// together with the residual add and the next RMSNorm (qwen3.py:126-129, :140 + next ln1).
+//
+// Symmetric buffers (one cudaMalloc per rank, opened by every peer through CUDA IPC):
+//   IN  [rows, H] bf16  per-rank partial sums (the row-parallel GEMM writes here)
+//   RES [rows, H] bf16  residual stream (replicated)
+//   OUT [rows, H] bf16  RMSNorm output (replicated; the next GEMM reads it)
+//   FLAGS               [2 phases][MAX_CTAS][MAX_RANKS] uint32 epoch words
+// Two-shot algorithm, one launch, grid = NCTA CTAs on every rank:
+//   1. barrier A: CTA b tells CTA b of every peer "my IN is ready" (the GEMM that wrote
+//      IN precedes this kernel on each rank's stream) and waits for the peers;
+//   2. rank r owns rows [r*T/tp, (r+1)*T/tp); CTA b takes every NCTA-th owned row,
+//      sums the row over all peers' IN (NVLink loads), adds RES, normalises, and stores
+//      the new RES row and the OUT row into every rank's buffers (NVLink stores);
+//   3. barrier B: CTA b tells CTA b of every peer "my stores are done" and waits, so on
+//      return every rank holds all rows of RES and OUT.
+// Epochs are per CTA slot in device memory, advanced by the kernel itself, so the call is
+// CUDA-graph capturable.  Every wait is bounded by a wall-clock budget; on expiry the
+// kernel records an error code (read with comm_error_code) and returns.
+#include <cuda_runtime.h>
+
+#include "comm.h"
+#include "common.cuh"
+
+namespace nvb {
+
+__device__ int g_comm_error = 0;
+
+namespace {
+
+constexpr uint64_t COMM_WAIT_NS = 10000000000ull;  // 10 s: ranks may autotune GEMMs at different speeds
+
+__device__ __forceinline__ uint64_t comm_timer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Signal slot `b` of every rank, then wait until every rank signalled slot `b` here.
+// Executed by thread 0 of the CTA.  Returns false on timeout.
+__device__ bool cta_barrier(const CommArgs& a, int phase, int b, uint32_t epoch) {
+  __threadfence_system();
+  for (int p = 0; p < a.world; ++p) {
+    uint32_t* f = a.flags[p] + ((phase * COMM_MAX_CTAS + b) * COMM_MAX_RANKS + a.rank);
+    st_release_sys(f, epoch);
+  }
+  const uint32_t* mine = a.flags[a.rank] + (phase * COMM_MAX_CTAS + b) * COMM_MAX_RANKS;
+  const uint64_t t0 = comm_timer();
+  for (int p = 0; p < a.world; ++p) {
+    while (ld_acquire_sys(mine + p) != epoch) {
+      if (comm_timer() - t0 > COMM_WAIT_NS) {
+        atomicCAS(&g_comm_error, 0, 100 + phase);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+template <int NI>
+__global__ void __launch_bounds__(256) allreduce_add_rmsnorm_kernel(CommArgs a) {
+  const int b = blockIdx.x;
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_ok;
+  __shared__ float red[32];
+  if (threadIdx.x == 0) {
+    s_epoch = a.epochs[b] + 1;
+    s_ok = cta_barrier(a, 0, b, s_epoch) ? 1 : 0;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  if (s_ok) {
+    const int H = a.hidden;
+    const int nvec = H >> 3;
+    const int per = (a.rows + a.world - 1) / a.world;
+    const int r0 = a.rank * per, r1 = min(a.rows, r0 + per);
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    for (int row = r0 + b; row < r1; row += gridDim.x) {
+      float v[NI][8];
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < nvec) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+          for (int p = 0; p < a.world; ++p) {
+            const uint4* src = reinterpret_cast<const uint4*>(a.in[p] + (int64_t)row * H);
+            float f[8];
+            bf16x8_to_f32(__ldcv(src + c), f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i][j] += f[j];
+          }
+          if (a.has_residual) {
+            float r[8];
+            bf16x8_to_f32(reinterpret_cast<const uint4*>(a.res[a.rank] + (int64_t)row * H)[c], r);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i][j] = bf16_round(v[i][j] + r[j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i][j] = bf16_round(v[i][j]);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) red[wid] = ss;
+      __syncthreads();
+      if (wid == 0) {
+        float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
+        t = warp_sum(t);
+        if (lane == 0) red[0] = rsqrtf(t / (float)H + a.eps);
+      }
+      __syncthreads();
+      const float inv = red[0];
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < nvec) {
+          float wf[8], o[8];
+          bf16x8_to_f32(reinterpret_cast<const uint4*>(a.weight)[c], wf);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = v[i][j] * inv * wf[j];
+          const uint4 ru = f32_to_bf16x8(v[i]), ou = f32_to_bf16x8(o);
+          for (int p = 0; p < a.world; ++p) {
+            reinterpret_cast<uint4*>(a.res[p] + (int64_t)row * H)[c] = ru;
+            reinterpret_cast<uint4*>(a.out[p] + (int64_t)row * H)[c] = ou;
+          }
+        }
+      }
+      __syncthreads();  // red[] is reused by the next row
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (s_ok) cta_barrier(a, 1, b, epoch);
+    a.epochs[b] = epoch;  // advance even on error so every slot stays in step locally
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_allreduce_add_rmsnorm(const CommArgs& a, cudaStream_t stream) {
+  if (a.rows == 0) return cudaSuccess;
+  if (a.hidden % 8 || a.hidden > 8 * 256 * 4 || a.world > COMM_MAX_RANKS || a.ctas > COMM_MAX_CTAS || a.ctas < 1)
+    return cudaErrorInvalidValue;
+  const int nvec = a.hidden / 8;
+  const int threads = nvec >= 256 ? 256 : ((nvec + 31) / 32) * 32;
+  const int ni = (nvec + threads - 1) / threads;
+  switch (ni) {
+    case 1: allreduce_add_rmsnorm_kernel<1><<<a.ctas, threads, 0, stream>>>(a); break;
+    case 2: allreduce_add_rmsnorm_kernel<2><<<a.ctas, threads, 0, stream>>>(a); break;
+    case 3: allreduce_add_rmsnorm_kernel<3><<<a.ctas, threads, 0, stream>>>(a); break;
+    default: allreduce_add_rmsnorm_kernel<4><<<a.ctas, threads, 0, stream>>>(a); break;
+  }
+  return cudaGetLastError();
+}
+
+int comm_error_code(int reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_comm_error, sizeof(int));
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_comm_error, &z, sizeof(int));
+  }
+  return v;
+}
+
+// ----------------------------------------------------------- symmetric memory (IPC)
+cudaError_t symm_alloc(size_t bytes, void** ptr, void* handle_out) {
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return e;
+  e = cudaMemset(*ptr, 0, bytes);
+  if (e != cudaSuccess) return e;
+  return cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle_out), *ptr);
+}
+
+cudaError_t symm_open(const void* handle, void** ptr) {
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+cudaError_t symm_close(void* peer_ptr) { return cudaIpcCloseMemHandle(peer_ptr); }
+
+cudaError_t symm_free(void* ptr) { return cudaFree(ptr); }
+
+}  // namespace nvb

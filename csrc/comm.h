@@ -1,0 +1,35 @@
+// Tensor-parallel fused all-reduce over NVLink peer memory: host interface.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_bf16.h>
+
+namespace nvb {
+
+constexpr int COMM_MAX_RANKS = 8;
+constexpr int COMM_MAX_CTAS = 64;
+// FLAGS region: [2 phases][COMM_MAX_CTAS][COMM_MAX_RANKS] uint32.
+constexpr size_t COMM_FLAG_BYTES = 2 * COMM_MAX_CTAS * COMM_MAX_RANKS * sizeof(uint32_t);
+
+struct CommArgs {
+  __nv_bfloat16* in[COMM_MAX_RANKS];   // every rank's IN buffer (peer pointers)
+  __nv_bfloat16* res[COMM_MAX_RANKS];
+  __nv_bfloat16* out[COMM_MAX_RANKS];
+  uint32_t* flags[COMM_MAX_RANKS];
+  uint32_t* epochs;                    // this rank's per-CTA epoch words (local memory)
+  const __nv_bfloat16* weight;
+  int rank, world, rows, hidden, ctas, has_residual;
+  float eps;
+};
+
+cudaError_t launch_allreduce_add_rmsnorm(const CommArgs& a, cudaStream_t stream);
+int comm_error_code(int reset);
+
+cudaError_t symm_alloc(size_t bytes, void** ptr, void* handle_out);  // handle_out: 64 bytes
+cudaError_t symm_open(const void* handle, void** ptr);
+cudaError_t symm_close(void* peer_ptr);
+cudaError_t symm_free(void* ptr);
+
+}  // namespace nvb

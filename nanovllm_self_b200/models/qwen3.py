@@ -94,6 +94,12 @@ class Qwen3ForCausalLM:
         return n
 
     # ---------------------------------------------------------------- forward
+    def _reduce_in(self, T):
+        """Output buffer for a row-parallel GEMM: the comm layer's symmetric input under TP."""
+        if self.comm is not None and self.tp_size > 1:
+            return self.comm.input_buffer(T)
+        return None
+
     def _reduce_norm(self, h, residual, w):
         """residual' = allreduce(h) + residual; return (rmsnorm(residual'), residual')."""
         if self.comm is not None and self.tp_size > 1:
@@ -115,11 +121,11 @@ class Qwen3ForCausalLM:
             q = ops.qkv_post(qkv, L.q_norm, L.k_norm, self.eps, positions, self.cos_sin, kc, vc,
                              ctx.slot_mapping, ks, vs, nq, nkv, d)
             o = ops.attention(q, kc, vc, ctx, self.scale, ks, vs)
-            h = ops.linear(o.view(T, nq * d), L.o)
+            h = ops.linear(o.view(T, nq * d), L.o, out=self._reduce_in(T))
             x, residual = self._reduce_norm(h, residual, L.ln2)
             gu = ops.linear(x, L.gate_up)
             a = ops.silu_mul(gu)
-            h = ops.linear(a, L.down)
+            h = ops.linear(a, L.down, out=self._reduce_in(T))
         return h, residual
 
     def compute_logits(self, h, residual, logits_indices: torch.Tensor) -> torch.Tensor:

@@ -32,8 +32,12 @@ class TorchOps:
     def rmsnorm(self, x, w, eps):
         return R.rmsnorm(x, w, eps)
 
-    def linear(self, x, w):
-        return R.linear(x, w)
+    def linear(self, x, w, out=None):
+        y = R.linear(x, w)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
 
     def qkv_post(self, qkv, q_norm, k_norm, eps, positions, cos_sin, k_cache, v_cache, slot_mapping,
                  k_scale, v_scale, nq, nkv, d):

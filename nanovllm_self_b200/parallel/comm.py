@@ -46,6 +46,12 @@ class TPComm:
             self.backend = "nccl"  # CPU / gloo: no peer memory
 
     # ------------------------------------------------------------ reductions
+    def input_buffer(self, T: int):
+        """Where the row-parallel GEMM should write its partial sums (None: anywhere)."""
+        if self.symm is not None and T <= self.symm.rows:
+            return self.symm.input_buffer(T)
+        return None
+
     def allreduce_add_rmsnorm(self, h, residual, w, eps):
         if self.symm is not None and h.shape[0] <= self.symm.rows:
             return self.symm.allreduce_add_rmsnorm(h, residual, w, eps, self.ops)
