@@ -170,6 +170,34 @@ cudaError_t launch_allreduce_add_rmsnorm(const CommArgs& a, cudaStream_t stream)
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------- KV block push
+// Copy whole KV blocks of every (K/V, layer) plane from this GPU's pool into another
+// GPU's pool (an IPC mapping) over NVLink: one launch per handoff, no staging buffer.
+// Pools are [planes = 2 * layers][num_blocks][block_bytes]; CTA (i, plane) moves block
+// src_ids[i] -> dst_ids[i] of that plane with 16-byte loads and stores.
+__global__ void kv_push_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, const int* __restrict__ src_ids,
+                               const int* __restrict__ dst_ids, int nb_src, int nb_dst, int64_t block_vec) {
+  const int i = blockIdx.x, plane = blockIdx.y;
+  const int s = src_ids[i], d = dst_ids[i];
+  if (s < 0 || s >= nb_src || d < 0 || d >= nb_dst) {
+    if (threadIdx.x == 0) atomicCAS(&g_comm_error, 0, 200);
+    return;
+  }
+  const uint4* sp = src + ((int64_t)plane * nb_src + s) * block_vec;
+  uint4* dp = dst + ((int64_t)plane * nb_dst + d) * block_vec;
+  for (int64_t v = threadIdx.x; v < block_vec; v += blockDim.x) dp[v] = sp[v];
+}
+
+cudaError_t launch_kv_push(const void* src_pool, void* dst_pool, const int* src_ids, const int* dst_ids, int n,
+                           int planes, int nb_src, int nb_dst, int64_t block_bytes, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  if (block_bytes % 16 || ((uintptr_t)src_pool & 15) || ((uintptr_t)dst_pool & 15)) return cudaErrorInvalidValue;
+  dim3 grid(n, planes);
+  kv_push_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4*>(src_pool), static_cast<uint4*>(dst_pool), src_ids,
+                                           dst_ids, nb_src, nb_dst, block_bytes / 16);
+  return cudaGetLastError();
+}
+
 int comm_error_code(int reset) {
   int v = 0;
   cudaMemcpyFromSymbol(&v, g_comm_error, sizeof(int));

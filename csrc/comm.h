@@ -27,6 +27,10 @@ struct CommArgs {
 cudaError_t launch_allreduce_add_rmsnorm(const CommArgs& a, cudaStream_t stream);
 int comm_error_code(int reset);
 
+// Copy blocks src_ids[i] -> dst_ids[i] of every plane of [planes][nb][block_bytes] pools.
+cudaError_t launch_kv_push(const void* src_pool, void* dst_pool, const int* src_ids, const int* dst_ids, int n,
+                           int planes, int nb_src, int nb_dst, int64_t block_bytes, cudaStream_t stream);
+
 cudaError_t symm_alloc(size_t bytes, void** ptr, void* handle_out);  // handle_out: 64 bytes
 cudaError_t symm_open(const void* handle, void** ptr);
 cudaError_t symm_close(void* peer_ptr);

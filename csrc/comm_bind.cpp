@@ -61,6 +61,22 @@ void allreduce_add_rmsnorm(std::vector<int64_t> bases, int64_t in_off, int64_t r
 
 int64_t comm_error(bool reset) { return nvb::comm_error_code(reset ? 1 : 0); }
 
+// Push blocks of a local KV pool [2, L, NB, ...] into a peer pool (raw pointer, nb_dst blocks).
+void kv_push(const at::Tensor& pool, const at::Tensor& src_ids, const at::Tensor& dst_ids, int64_t dst_ptr,
+             int64_t nb_dst) {
+  TORCH_CHECK(pool.is_cuda() && pool.is_contiguous() && pool.dim() >= 3, "pool [2, L, NB, ...] contiguous");
+  TORCH_CHECK(src_ids.scalar_type() == at::kInt && dst_ids.scalar_type() == at::kInt, "int32 ids");
+  TORCH_CHECK(src_ids.numel() == dst_ids.numel(), "id count mismatch");
+  const int planes = (int)(pool.size(0) * pool.size(1));
+  const int nb_src = (int)pool.size(2);
+  const int64_t block_bytes = pool.numel() / ((int64_t)planes * nb_src) * pool.element_size();
+  at::cuda::CUDAGuard g(pool.device());
+  check(nvb::launch_kv_push(pool.data_ptr(), reinterpret_cast<void*>(dst_ptr), src_ids.data_ptr<int>(),
+                            dst_ids.data_ptr<int>(), (int)src_ids.numel(), planes, nb_src, (int)nb_dst, block_bytes,
+                            at::cuda::getCurrentCUDAStream().stream()),
+        "kv_push");
+}
+
 }  // namespace
 
 void register_comm(pybind11::module& m) {
@@ -70,6 +86,7 @@ void register_comm(pybind11::module& m) {
   m.def("symm_free", &symm_free);
   m.def("allreduce_add_rmsnorm", &allreduce_add_rmsnorm);
   m.def("comm_error", &comm_error, pybind11::arg("reset") = false);
+  m.def("kv_push", &kv_push);
   m.attr("COMM_FLAG_BYTES") = (int64_t)nvb::COMM_FLAG_BYTES;
   m.attr("COMM_MAX_CTAS") = (int64_t)nvb::COMM_MAX_CTAS;
 }

@@ -148,6 +148,14 @@ class ModelRunner:
             self.kv_scale_layers = [(self.kv_scale_cache[0, i], self.kv_scale_cache[1, i])
                                     for i in range(m.num_layers)]
 
+    def export_kv_pool(self) -> bytes:
+        """CUDA IPC handle (64 bytes) + byte offset of the KV pool, for a peer process's push kernel."""
+        st = self.kv_cache.untyped_storage()
+        info = st._share_cuda_()
+        handle, offset = info[1], info[3]
+        self.kv_pool_ipc_offset = int(offset)
+        return bytes(handle) + int(offset).to_bytes(8, "little")
+
     def _alloc_staging(self):
         c = self.config
         maxT = c.max_num_batched_tokens + max(c.max_num_seqs, c.cuda_graph_max_bs)

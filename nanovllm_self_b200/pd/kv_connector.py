@@ -30,9 +30,11 @@ def _raw(t: torch.Tensor) -> torch.Tensor:
 
 
 class KVConnector:
-    def __init__(self, config, role: str, engine_id: str, kv_store_backend: KVStoreBackend):
+    def __init__(self, config, role: str, engine_id: str, kv_store_backend: KVStoreBackend, export: bool = True):
         if role not in ("producer", "consumer"):
             raise ValueError("role must be 'producer' or 'consumer'")
+        # export=False: metadata only (the KV is pushed straight from the pool by a kernel)
+        self.export = export
         self.config = config
         self.role = role
         self.engine_id = engine_id
@@ -75,7 +77,12 @@ class KVConnector:
     def save_kv(self, seq) -> KVTransferMeta:
         if self.role != "producer":
             raise RuntimeError("save_kv is a producer operation")
-        kv, sc, n, last, src = self._export_kv_snapshot(seq)
+        if self.export:
+            kv, sc, n, last, src = self._export_kv_snapshot(seq)
+        else:
+            bs = self.config.block_size
+            n = (seq.num_cached_tokens + bs - 1) // bs
+            kv, sc, last, src = None, None, self._last_block_num_tokens(seq.num_cached_tokens), list(seq.block_table[:n])
         hid = self._build_handoff_id(seq)
         mode = self.config.kv_cache_quant_mode
         meta = KVTransferMeta(handoff_id=hid, producer_id=self.engine_id, num_cached_tokens=seq.num_cached_tokens,

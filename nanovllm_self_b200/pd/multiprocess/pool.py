@@ -1,0 +1,217 @@
+"""P/D pool driver: N prefill workers + M decode workers, routed by the agent-aware router.
+
+Reference: ``pd_self/multiprocess/evaluation/benchmark_agent_pd_pool.py`` (N P + M D workers
+in one NCCL world, two-stage routing of P and D with session affinity, closed-loop
+concurrency, metrics and summary) and ``benchmark_agent_pd_multi_pair.py`` (fixed pairs).
+Arrivals are closed-loop (``concurrency``) or open-loop Poisson (``rate``).  Worker load
+feedback comes from each worker's ``worker_state.json``.
+
+``python -m nanovllm_self_b200.pd.multiprocess.pool --help`` runs it from the shell.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+from .agent_scheduler import Router, RouterConfig, estimate
+from .control_plane import WorkDir
+
+
+def _pct(xs, q):
+    return float(np.percentile(np.asarray(xs, dtype=np.float64), q)) if xs else 0.0
+
+
+class PDPool:
+    def __init__(self, work_root, num_prefill=1, num_decode=1, backend="shared_memory", model="tiny",
+                 prefill_devices=None, decode_devices=None, policy="load_aware", worker_args=None,
+                 handshake_timeout_s=120.0, nccl_port=29650, python=sys.executable):
+        self.root = Path(work_root)
+        self.root.mkdir(parents=True, exist_ok=True)
+        self.P, self.D = num_prefill, num_decode
+        self.backend = backend
+        self.model = model
+        self.pdev = prefill_devices or [f"cuda:{i}" for i in range(num_prefill)]
+        self.ddev = decode_devices or [f"cuda:{num_prefill + i}" for i in range(num_decode)]
+        self.p_router = Router(num_prefill, policy)
+        self.d_router = Router(num_decode, policy)
+        self.worker_args = list(worker_args or [])
+        self.timeout = handshake_timeout_s
+        self.nccl_port = nccl_port
+        self.python = python
+        self.procs = []
+        self.pwd = [WorkDir(self.root / f"prefill_{i}") for i in range(num_prefill)]
+        self.dwd = [WorkDir(self.root / f"decode_{i}") for i in range(num_decode)]
+        self.submitted = {}
+        self.results = {}
+
+    # ------------------------------------------------------------- lifecycle
+    def _launch(self, role, idx, device, wd, rank):
+        cmd = [self.python, "-m", "nanovllm_self_b200.pd.multiprocess.workers", role, "--work-dir", str(wd.path),
+               "--model", self.model, "--device", device, "--backend", self.backend,
+               "--global-rank", str(rank), "--world-size", str(self.P + self.D), "--nccl-port", str(self.nccl_port),
+               "--handshake-timeout-s", str(self.timeout)] + self.worker_args
+        log = open(wd.f(f"{role}.log"), "w")
+        env = dict(os.environ)
+        env.setdefault("NCCL_NVLS_ENABLE", "0")
+        root = str(Path(__file__).resolve().parents[3])
+        env["PYTHONPATH"] = root + os.pathsep + env.get("PYTHONPATH", "")
+        self.procs.append(subprocess.Popen(cmd, stdout=log, stderr=subprocess.STDOUT, env=env))
+
+    def start(self, ready_timeout_s: float = 600.0) -> None:
+        for wd in self.pwd + self.dwd:
+            for stale in ("shutdown", "worker_ready.json", "kv_pool.json"):
+                wd.remove(stale)
+        for i, wd in enumerate(self.pwd):
+            self._launch("prefill", i, self.pdev[i], wd, i)
+        for i, wd in enumerate(self.dwd):
+            self._launch("decode", i, self.ddev[i], wd, self.P + i)
+        deadline = time.time() + ready_timeout_s
+        for wd in self.pwd + self.dwd:
+            while not wd.exists("worker_ready.json"):
+                if time.time() > deadline or any(p.poll() not in (None, 0) for p in self.procs):
+                    self.shutdown(force=True)
+                    raise RuntimeError(f"worker in {wd.path} failed to start (see its log)")
+                time.sleep(0.05)
+
+    def shutdown(self, force: bool = False, timeout_s: float = 120.0) -> None:
+        for wd in self.pwd + self.dwd:
+            wd.touch("shutdown")
+        deadline = time.time() + timeout_s
+        for p in self.procs:
+            try:
+                p.wait(timeout=max(0.1, deadline - time.time()) if not force else 5)
+            except subprocess.TimeoutExpired:
+                p.kill()
+                p.wait(timeout=10)
+        self.procs = []
+
+    # --------------------------------------------------------------- routing
+    def _feedback(self) -> None:
+        for router, wds in ((self.p_router, self.pwd), (self.d_router, self.dwd)):
+            for i, wd in enumerate(wds):
+                try:
+                    st = wd.read_json("worker_state.json")
+                except (FileNotFoundError, json.JSONDecodeError):
+                    continue
+                load = st.get("queue_depth", 0) * 0.05 + st.get("active", 0) * 0.01 + (0.02 if st.get("busy") else 0)
+                router.update_feedback(i, load, st)
+
+    def submit(self, row: dict, index: int, now_s: float) -> str:
+        self._feedback()
+        est = estimate(row, index, int(row["max_tokens"]), RouterConfig())
+        pm = self.p_router.route(est, now_s)
+        dm = self.d_router.route(est, now_s)
+        base = f"r{index:06d}"
+        req = {"request_id": row.get("id", base), "prompt_ids": row["prompt_ids"], "max_tokens": row["max_tokens"],
+               "temperature": row.get("temperature", 0.0), "ignore_eos": row.get("ignore_eos", True),
+               "session_id": est.session_id, "decode_work_dir": str(self.dwd[dm["worker_id"]].path),
+               "dst_rank": self.P + dm["worker_id"]}
+        self.pwd[pm["worker_id"]].write_json(f"{base}.request.json", req)
+        self.submitted[base] = {"submit_time": time.time(), "p": pm, "d": dm, "row": row}
+        return base
+
+    def _collect(self) -> list:
+        done = []
+        for base, info in list(self.submitted.items()):
+            if base in self.results:
+                continue
+            dwd = self.dwd[info["d"]["worker_id"]]
+            for stage in ("prefill", "decode"):
+                if dwd.exists(f"{base}.{stage}_error.json"):
+                    self.results[base] = {"error": dwd.read_json(f"{base}.{stage}_error.json")["error"]}
+                    done.append(base)
+                    break
+            else:
+                if dwd.exists(f"{base}.decode_done"):
+                    dm = dwd.read_json(f"{base}.decode_metrics.json")
+                    pm = dwd.read_json(f"{base}.prefill_metrics.json") if dwd.exists(f"{base}.prefill_metrics.json") else {}
+                    t_sub = info["submit_time"]
+                    first = pm.get("prefill_start_time", t_sub) + pm.get("prefill_time_s", 0.0)
+                    n_out = len(dm.get("output_ids", []))
+                    end = dm.get("finish_time", time.time())
+                    self.results[base] = {"output_ids": dm.get("output_ids", []), "ttft_s": first - t_sub,
+                                          "tpot_s": (end - first) / max(1, n_out - 1), "e2e_s": end - t_sub,
+                                          "prefill": pm, "decode": dm}
+                    done.append(base)
+        return done
+
+    def run(self, rows: list, concurrency: int | None = 4, rate: float | None = None, timeout_s: float = 3600.0,
+            seed: int = 0) -> dict:
+        rng = random.Random(seed)
+        t0 = time.time()
+        next_arrival = 0.0
+        i = 0
+        inflight = set()
+        while i < len(rows) or inflight:
+            now = time.time() - t0
+            if i < len(rows):
+                if rate:
+                    if now >= next_arrival:
+                        inflight.add(self.submit(rows[i], i, now))
+                        i += 1
+                        next_arrival += rng.expovariate(rate)
+                elif len(inflight) < (concurrency or 1):
+                    inflight.add(self.submit(rows[i], i, now))
+                    i += 1
+            for b in self._collect():
+                inflight.discard(b)
+            if time.time() - t0 > timeout_s:
+                raise TimeoutError("P/D pool run timed out")
+            time.sleep(0.001)
+        wall = time.time() - t0
+        ok = [r for r in self.results.values() if "error" not in r]
+        gen = sum(len(r["output_ids"]) for r in ok)
+        return {"num_requests": len(rows), "num_errors": len(self.results) - len(ok), "wall_s": wall,
+                "output_tok_s": gen / wall if wall > 0 else 0.0,
+                "ttft_ms_p50": _pct([r["ttft_s"] * 1e3 for r in ok], 50),
+                "ttft_ms_p99": _pct([r["ttft_s"] * 1e3 for r in ok], 99),
+                "tpot_ms_p50": _pct([r["tpot_s"] * 1e3 for r in ok], 50),
+                "tpot_ms_p99": _pct([r["tpot_s"] * 1e3 for r in ok], 99),
+                "prefill_router": self.p_router.summary(), "decode_router": self.d_router.summary()}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description="P/D pool benchmark driver")
+    ap.add_argument("--work-root", required=True)
+    ap.add_argument("--num-prefill", type=int, default=1)
+    ap.add_argument("--num-decode", type=int, default=1)
+    ap.add_argument("--backend", default="ipc_push")
+    ap.add_argument("--model", default="qwen3-0.6b")
+    ap.add_argument("--policy", default="affinity_load_aware")
+    ap.add_argument("--num-requests", type=int, default=32)
+    ap.add_argument("--rate", type=float, default=None)
+    ap.add_argument("--concurrency", type=int, default=4)
+    ap.add_argument("--input-mean", type=float, default=2048)
+    ap.add_argument("--output-mean", type=float, default=256)
+    ap.add_argument("--out", default=None)
+    args, rest = ap.parse_known_args(argv)
+    rng = np.random.default_rng(0)
+    rows = []
+    for i in range(args.num_requests):
+        n_in = int(np.clip(rng.lognormal(np.log(args.input_mean), 0.5), 16, 8192))
+        n_out = int(np.clip(rng.lognormal(np.log(args.output_mean), 0.5), 4, 1024))
+        rows.append({"id": f"req-{i}", "prompt_ids": rng.integers(0, 151936, n_in).tolist(), "max_tokens": n_out,
+                     "input_tokens": n_in})
+    pool = PDPool(args.work_root, args.num_prefill, args.num_decode, args.backend, args.model, policy=args.policy,
+                  worker_args=rest)
+    pool.start()
+    try:
+        summary = pool.run(rows, concurrency=args.concurrency, rate=args.rate)
+    finally:
+        pool.shutdown()
+    print(json.dumps(summary))
+    if args.out:
+        with open(args.out, "w") as f:
+            json.dump(summary, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()
