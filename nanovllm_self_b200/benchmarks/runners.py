@@ -1,0 +1,143 @@
+"""Benchmark drivers for the BASELINE configs (reference ``scripts/benchmark_*.py``).
+
+``python -m nanovllm_self_b200.benchmarks.runners <name> [options]`` with ``name`` in:
+
+* ``runtime``      - TTFT, ITL/TPOT, prefill and decode tok/s for a batch (``benchmark_runtime.py``);
+* ``decode_sweep`` - decode tok/s at batch sizes 1/8/32/128/256 with a fixed context (config 3);
+* ``kv_dtype``     - the same workload with bf16 and fp8 KV caches (``benchmark_kv_cache_dtype.py``);
+* ``prefix``       - the multi-turn agent prefix workload (config 4): prefix-hit rate and tok/s;
+* ``pd``           - P/D pool with Poisson arrivals (config 5): p50/p99 TTFT and TPOT.
+Every driver prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import time
+
+import torch
+
+from .. import LLM, SamplingParams
+from . import datasets
+
+
+def _llm(args, **kw):
+    base = dict(device=args.device, max_model_len=args.max_model_len, max_num_seqs=args.max_num_seqs,
+                block_size=args.block_size, kv_cache_quant_mode=args.kv, tensor_parallel_size=args.tp)
+    base.update(kw)
+    return LLM(args.model, **base)
+
+
+def _sp(rows):
+    return [SamplingParams(temperature=0.0, max_tokens=r["max_tokens"], ignore_eos=True) for r in rows]
+
+
+def runtime(args) -> dict:
+    llm = _llm(args)
+    vocab = llm.model_runner.arch.vocab_size
+    rows = datasets.uniform_serving(args.batch, vocab, (args.prompt_len, args.prompt_len), (args.gen, args.gen))
+    llm.generate([r["prompt_ids"] for r in rows], _sp(rows))
+    m = llm.generate([r["prompt_ids"] for r in rows], _sp(rows), return_metrics=True)["metrics"]
+    prefill_s = m["ttft_ms_p50"] / 1e3
+    return {"bench": "runtime", "batch": args.batch, "prompt_len": args.prompt_len, "gen": args.gen,
+            "ttft_ms": m["ttft_ms_p50"], "itl_ms": m["tpot_ms_p50"],
+            "prefill_tok_s": args.batch * args.prompt_len / prefill_s if prefill_s > 0 else 0.0,
+            "decode_tok_s": args.batch / (m["tpot_ms_p50"] / 1e3) if m["tpot_ms_p50"] > 0 else 0.0,
+            "e2e_tok_s": m["e2e_throughput_tok_s"], "device_tok_s": m["throughput_tok_s"]}
+
+
+def decode_sweep(args) -> dict:
+    llm = _llm(args)
+    vocab = llm.model_runner.arch.vocab_size
+    out = {"bench": "decode_sweep", "context": args.context, "kv": args.kv, "points": []}
+    for bs in [int(b) for b in args.batches.split(",")]:
+        rows = datasets.uniform_serving(bs, vocab, (args.context, args.context), (args.gen, args.gen), seed=bs)
+        llm.generate([r["prompt_ids"] for r in rows], _sp(rows))
+        m = llm.generate([r["prompt_ids"] for r in rows], _sp(rows), return_metrics=True)["metrics"]
+        out["points"].append({"batch": bs, "tpot_ms": m["tpot_ms_p50"],
+                              "decode_tok_s": bs / (m["tpot_ms_p50"] / 1e3) if m["tpot_ms_p50"] > 0 else 0.0})
+    return out
+
+
+def kv_dtype(args) -> dict:
+    res = {"bench": "kv_dtype", "runs": []}
+    for kv in ("none", "fp8"):
+        args.kv = kv
+        llm = _llm(args)
+        vocab = llm.model_runner.arch.vocab_size
+        rows = datasets.uniform_serving(args.batch, vocab, (100, 1024), (100, 1024))
+        llm.generate([r["prompt_ids"] for r in rows], _sp(rows))
+        m = llm.generate([r["prompt_ids"] for r in rows], _sp(rows), return_metrics=True)["metrics"]
+        res["runs"].append({"kv": kv, "device_tok_s": m["throughput_tok_s"], "e2e_tok_s": m["e2e_throughput_tok_s"],
+                            "tpot_ms": m["tpot_ms_p50"], "kv_blocks": llm.model_runner.num_blocks})
+        llm.shutdown()
+        del llm
+        torch.cuda.empty_cache()
+    return res
+
+
+def prefix(args) -> dict:
+    llm = _llm(args, enable_chunked_prefill=True, prefill_chunk_size=4096)
+    vocab = llm.model_runner.arch.vocab_size
+    rows = datasets.agent_sessions(args.sessions, vocab, seed=0)
+    by_turn = {}
+    for r in rows:
+        by_turn.setdefault(r["step_id"], []).append(r)
+    t0 = time.perf_counter()
+    gen = 0
+    for t in sorted(by_turn):
+        batch = by_turn[t]
+        out = llm.generate([r["prompt_ids"] for r in batch], _sp(batch), return_metrics=True)
+        gen += out["metrics"]["generated_tokens"]
+    wall = time.perf_counter() - t0
+    snap = llm.block_manager.get_block_usage_snapshot()
+    return {"bench": "prefix", "sessions": args.sessions, "turns": len(by_turn), "wall_s": wall,
+            "output_tok_s": gen / wall, "prefix_hit_blocks": snap["prefix_hit_blocks"],
+            "prefix_query_blocks": snap["prefix_query_blocks"],
+            "prefix_hit_rate": snap["prefix_hit_blocks"] / max(1, snap["prefix_query_blocks"])}
+
+
+def pd(args) -> dict:
+    from ..pd.multiprocess.pool import PDPool
+    rows = datasets.pd_lognormal(args.num_requests)
+    pool = PDPool(args.work_root, args.num_prefill, args.num_decode, args.pd_backend, args.model,
+                  policy="affinity_load_aware",
+                  worker_args=["--max-model-len", str(args.max_model_len), "--block-size", str(args.block_size),
+                               "--kv-cache-quant-mode", args.kv])
+    pool.start()
+    try:
+        s = pool.run(rows, concurrency=None, rate=args.rate)
+    finally:
+        pool.shutdown()
+    s["bench"] = "pd"
+    return s
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("name", choices=["runtime", "decode_sweep", "kv_dtype", "prefix", "pd"])
+    ap.add_argument("--model", default="qwen3-8b")
+    ap.add_argument("--device", default="cuda")
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--kv", default="none")
+    ap.add_argument("--max-model-len", type=int, default=9216)
+    ap.add_argument("--max-num-seqs", type=int, default=256)
+    ap.add_argument("--block-size", type=int, default=256)
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--prompt-len", type=int, default=512)
+    ap.add_argument("--gen", type=int, default=64)
+    ap.add_argument("--context", type=int, default=2048)
+    ap.add_argument("--batches", default="1,8,32,128,256")
+    ap.add_argument("--sessions", type=int, default=64)
+    ap.add_argument("--num-requests", type=int, default=512)
+    ap.add_argument("--rate", type=float, default=8.0)
+    ap.add_argument("--num-prefill", type=int, default=1)
+    ap.add_argument("--num-decode", type=int, default=1)
+    ap.add_argument("--pd-backend", default="ipc_push")
+    ap.add_argument("--work-root", default="/tmp/nvb_pd")
+    args = ap.parse_args(argv)
+    print(json.dumps(globals()[args.name](args)))
+
+
+if __name__ == "__main__":
+    main()
