@@ -97,12 +97,19 @@ __global__ void __launch_bounds__(256) allreduce_add_rmsnorm_kernel(CommArgs a) 
         if (c < nvec) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
-          for (int p = 0; p < a.world; ++p) {
-            const uint4* src = reinterpret_cast<const uint4*>(a.in[p] + (int64_t)row * H);
-            float f[8];
-            bf16x8_to_f32(__ldcv(src + c), f);
+          // issue every peer's load before using any (NVLink latency overlaps)
+          uint4 raw[COMM_MAX_RANKS];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[i][j] += f[j];
+          for (int p = 0; p < COMM_MAX_RANKS; ++p)
+            if (p < a.world) raw[p] = __ldcv(reinterpret_cast<const uint4*>(a.in[p] + (int64_t)row * H) + c);
+#pragma unroll
+          for (int p = 0; p < COMM_MAX_RANKS; ++p) {
+            if (p < a.world) {
+              float f[8];
+              bf16x8_to_f32(raw[p], f);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[i][j] += f[j];
+            }
           }
           if (a.has_residual) {
             float r[8];
@@ -152,7 +159,105 @@ __global__ void __launch_bounds__(256) allreduce_add_rmsnorm_kernel(CommArgs a) 
   }
 }
 
+// One-shot variant for small batches: a single barrier ("every rank's IN is ready"),
+// then every rank reduces ALL rows itself from the peers' IN and writes RES / OUT in its
+// own memory only.  The caller rotates IN over three buffers (consecutive calls never
+// share one), which is what makes the missing second barrier safe: a rank can only
+// reach the barrier of call k+1 after every rank finished reading call k's buffer.
+template <int NI>
+__global__ void __launch_bounds__(256) allreduce_oneshot_kernel(CommArgs a) {
+  const int b = blockIdx.x;
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_ok;
+  __shared__ float red[32];
+  if (threadIdx.x == 0) {
+    s_epoch = a.epochs[b] + 1;
+    s_ok = cta_barrier(a, 0, b, s_epoch) ? 1 : 0;
+    a.epochs[b] = s_epoch;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  const int H = a.hidden;
+  const int nvec = H >> 3;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int row = b; row < a.rows; row += gridDim.x) {
+    float v[NI][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nvec) {
+        uint4 raw[COMM_MAX_RANKS];
+#pragma unroll
+        for (int p = 0; p < COMM_MAX_RANKS; ++p)
+          if (p < a.world) raw[p] = __ldcv(reinterpret_cast<const uint4*>(a.in[p] + (int64_t)row * H) + c);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+#pragma unroll
+        for (int p = 0; p < COMM_MAX_RANKS; ++p) {
+          if (p < a.world) {
+            float f[8];
+            bf16x8_to_f32(raw[p], f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i][j] += f[j];
+          }
+        }
+        if (a.has_residual) {
+          float r[8];
+          bf16x8_to_f32(reinterpret_cast<const uint4*>(a.res[a.rank] + (int64_t)row * H)[c], r);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] = bf16_round(v[i][j] + r[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] = bf16_round(v[i][j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[wid] = ss;
+    __syncthreads();
+    if (wid == 0) {
+      float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
+      t = warp_sum(t);
+      if (lane == 0) red[0] = rsqrtf(t / (float)H + a.eps);
+    }
+    __syncthreads();
+    const float inv = red[0];
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nvec) {
+        float wf[8], o[8];
+        bf16x8_to_f32(reinterpret_cast<const uint4*>(a.weight)[c], wf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = v[i][j] * inv * wf[j];
+        reinterpret_cast<uint4*>(a.res[a.rank] + (int64_t)row * H)[c] = f32_to_bf16x8(v[i]);
+        reinterpret_cast<uint4*>(a.out[a.rank] + (int64_t)row * H)[c] = f32_to_bf16x8(o);
+      }
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_allreduce_oneshot(const CommArgs& a, cudaStream_t stream) {
+  if (a.rows == 0) return cudaSuccess;
+  if (a.hidden % 8 || a.hidden > 8 * 256 * 4 || a.world > COMM_MAX_RANKS || a.ctas > COMM_MAX_CTAS || a.ctas < 1)
+    return cudaErrorInvalidValue;
+  const int nvec = a.hidden / 8;
+  const int threads = nvec >= 256 ? 256 : ((nvec + 31) / 32) * 32;
+  const int ni = (nvec + threads - 1) / threads;
+  switch (ni) {
+    case 1: allreduce_oneshot_kernel<1><<<a.ctas, threads, 0, stream>>>(a); break;
+    case 2: allreduce_oneshot_kernel<2><<<a.ctas, threads, 0, stream>>>(a); break;
+    case 3: allreduce_oneshot_kernel<3><<<a.ctas, threads, 0, stream>>>(a); break;
+    default: allreduce_oneshot_kernel<4><<<a.ctas, threads, 0, stream>>>(a); break;
+  }
+  return cudaGetLastError();
+}
 
 cudaError_t launch_allreduce_add_rmsnorm(const CommArgs& a, cudaStream_t stream) {
   if (a.rows == 0) return cudaSuccess;
@@ -211,16 +316,18 @@ int comm_error_code(int reset) {
 // ----------------------------------------------------------- symmetric memory (IPC)
 cudaError_t symm_alloc(size_t bytes, void** ptr, void* handle_out) {
   cudaError_t e = cudaMalloc(ptr, bytes);
-  if (e != cudaSuccess) return e;
-  e = cudaMemset(*ptr, 0, bytes);
-  if (e != cudaSuccess) return e;
-  return cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle_out), *ptr);
+  if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle_out), *ptr);
+  if (e != cudaSuccess) cudaGetLastError();
+  return e;
 }
 
 cudaError_t symm_open(const void* handle, void** ptr) {
   cudaIpcMemHandle_t h;
   memcpy(&h, handle, sizeof(h));
-  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) cudaGetLastError();  // do not leave the error for the next launch check
+  return e;
 }
 
 cudaError_t symm_close(void* peer_ptr) { return cudaIpcCloseMemHandle(peer_ptr); }

@@ -9,7 +9,7 @@
 namespace nvb {
 
 constexpr int COMM_MAX_RANKS = 8;
-constexpr int COMM_MAX_CTAS = 64;
+constexpr int COMM_MAX_CTAS = 256;
 // FLAGS region: [2 phases][COMM_MAX_CTAS][COMM_MAX_RANKS] uint32.
 constexpr size_t COMM_FLAG_BYTES = 2 * COMM_MAX_CTAS * COMM_MAX_RANKS * sizeof(uint32_t);
 
@@ -25,6 +25,8 @@ struct CommArgs {
 };
 
 cudaError_t launch_allreduce_add_rmsnorm(const CommArgs& a, cudaStream_t stream);
+// Single-barrier variant: every rank reduces every row (small batches; IN must rotate).
+cudaError_t launch_allreduce_oneshot(const CommArgs& a, cudaStream_t stream);
 int comm_error_code(int reset);
 
 // Copy blocks src_ids[i] -> dst_ids[i] of every plane of [planes][nb][block_bytes] pools.

@@ -104,6 +104,9 @@ class EngineConfig:
     # Use the hand-written CUDA ops (True) or the torch reference ops (False, CPU/oracle).
     use_custom_kernels: bool | None = None
     enforce_eager: bool = False
+    # Allocate the KV pool with cudaMalloc + CUDA IPC so another process can push blocks
+    # into it (the decode side of the NVLink P/D push).
+    kv_pool_ipc: bool = False
     extra: dict = field(default_factory=dict)
 
     def __post_init__(self):

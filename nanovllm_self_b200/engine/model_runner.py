@@ -134,7 +134,18 @@ class ModelRunner:
     def _allocate_kv_cache(self):
         m, c = self.model, self.config
         shape = (2, m.num_layers, self.num_blocks, m.num_kv_heads, self.block_size, m.head_dim)
-        self.kv_cache = torch.zeros(shape, dtype=c.kv_cache_dtype, device=self.device)
+        self._kv_ipc = None
+        if c.kv_pool_ipc and self.is_cuda:
+            from ..ops._ext import load
+            from ..parallel.symm import _DevPtr
+            C = load()
+            nbytes = int(np.prod(shape)) * torch.empty(0, dtype=c.kv_cache_dtype).element_size()
+            ptr, handle = C.symm_alloc(nbytes)
+            self._kv_ipc = (C, ptr, handle)
+            raw = torch.as_tensor(_DevPtr(ptr, nbytes), device=self.device)
+            self.kv_cache = raw.view(c.kv_cache_dtype).view(shape)
+        else:
+            self.kv_cache = torch.zeros(shape, dtype=c.kv_cache_dtype, device=self.device)
         self.kv_scale_cache = None
         if c.kv_cache_quant_mode == "fp8":
             self.kv_scale_cache = torch.ones(2, m.num_layers, self.num_blocks, m.num_kv_heads,
@@ -149,12 +160,12 @@ class ModelRunner:
                                     for i in range(m.num_layers)]
 
     def export_kv_pool(self) -> bytes:
-        """CUDA IPC handle (64 bytes) + byte offset of the KV pool, for a peer process's push kernel."""
-        st = self.kv_cache.untyped_storage()
-        info = st._share_cuda_()
-        handle, offset = info[1], info[3]
-        self.kv_pool_ipc_offset = int(offset)
-        return bytes(handle) + int(offset).to_bytes(8, "little")
+        """CUDA IPC handle (64 bytes) + byte offset (8 bytes) of the KV pool, for a peer's push kernel.
+
+        Needs ``kv_pool_ipc=True``: the pool is then its own cudaMalloc allocation."""
+        if self._kv_ipc is None:
+            raise RuntimeError("the KV pool was not allocated for IPC (set kv_pool_ipc=True)")
+        return bytes(self._kv_ipc[2]) + (0).to_bytes(8, "little")
 
     def _alloc_staging(self):
         c = self.config

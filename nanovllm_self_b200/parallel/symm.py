@@ -23,19 +23,24 @@ class _DevPtr:
 
 
 class SymmetricWorkspace:
-    CTAS = 32
 
-    def __init__(self, tp, rows: int, hidden: int):
+    def __init__(self, tp, rows: int, hidden: int, oneshot_rows: int = 512):
         self.C = load()
         self.tp = tp
         self.rows = rows
         self.hidden = hidden
+        # one-shot (single barrier, every rank reduces every row) while the peers' bytes
+        # each rank must read stay small; two-shot beyond
+        self.oneshot_rows = oneshot_rows
         row_bytes = rows * hidden * 2
+        small = min(rows, oneshot_rows) * hidden * 2
+        # IN (two-shot) | IN0 IN1 IN2 (one-shot rotation) | RES | OUT | FLAGS
         self.in_off = 0
-        self.res_off = row_bytes
-        self.out_off = 2 * row_bytes
-        self.flag_off = 3 * row_bytes
-        self.nbytes = 3 * row_bytes + int(self.C.COMM_FLAG_BYTES)
+        self.in1_off = [row_bytes, row_bytes + small, row_bytes + 2 * small]
+        self.res_off = row_bytes + 3 * small
+        self.out_off = 2 * row_bytes + 3 * small
+        self.flag_off = 3 * row_bytes + 3 * small
+        self.nbytes = self.flag_off + int(self.C.COMM_FLAG_BYTES)
         torch.cuda.set_device(tp.device)
         self.base, handle = self.C.symm_alloc(self.nbytes)
         handles = [None] * tp.size
@@ -51,27 +56,47 @@ class SymmetricWorkspace:
                 self.bases.append(ptr)
         raw = torch.as_tensor(_DevPtr(self.base, self.nbytes), device=tp.device)
         self._raw = raw
-        view = raw[:3 * row_bytes].view(torch.bfloat16).view(3, rows, hidden)
-        self.IN, self.RES, self.OUT = view[0], view[1], view[2]
+
+        def view(off, n):
+            return raw[off:off + n * hidden * 2].view(torch.bfloat16).view(n, hidden)
+        self.IN = view(self.in_off, rows)
+        self.IN1 = [view(o, min(rows, oneshot_rows)) for o in self.in1_off]
+        self.RES = view(self.res_off, rows)
+        self.OUT = view(self.out_off, rows)
         self.epochs = torch.zeros(self.C.COMM_MAX_CTAS, dtype=torch.int32, device=tp.device)
+        self._k = 0  # position in the one-shot IN rotation
         dist.barrier(group=tp.group)
 
+    def _oneshot(self, T: int) -> bool:
+        return T <= self.oneshot_rows
+
     def input_buffer(self, T: int) -> torch.Tensor:
+        """Where the next reduction's input should be written (the GEMM writes straight here)."""
+        if self._oneshot(T):
+            return self.IN1[self._k % 3][:T]
         return self.IN[:T]
 
     def allreduce_add_rmsnorm(self, h, residual, w, eps, ops=None):
         T = h.shape[0]
         if T > self.rows:
             raise ValueError(f"{T} rows exceed the symmetric workspace ({self.rows})")
-        inv = self.IN[:T]
+        one = self._oneshot(T)
+        inv = self.input_buffer(T)
+        in_off = self.in1_off[self._k % 3] if one else self.in_off
         if h.data_ptr() != inv.data_ptr():
             inv.copy_(h)
         res = self.RES[:T]
         has_res = residual is not None
         if has_res and residual.data_ptr() != res.data_ptr():
             res.copy_(residual)
-        self.C.allreduce_add_rmsnorm(self.bases, self.in_off, self.res_off, self.out_off, self.flag_off,
-                                     self.epochs, w, self.tp.rank, T, self.hidden, has_res, float(eps), self.CTAS)
+        if one:
+            ctas = max(1, min(148, T))
+        else:
+            ctas = max(1, min(int(self.C.COMM_MAX_CTAS), (T + self.tp.size - 1) // self.tp.size))
+        self.C.allreduce_add_rmsnorm(self.bases, in_off, self.res_off, self.out_off, self.flag_off,
+                                     self.epochs, w, self.tp.rank, T, self.hidden, has_res, float(eps), ctas, one)
+        if one:
+            self._k += 1
         if ops is not None and hasattr(ops, "launches"):
             ops.launches += 1
         return self.OUT[:T], res

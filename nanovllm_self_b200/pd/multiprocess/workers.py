@@ -68,8 +68,8 @@ def add_common_args(ap: argparse.ArgumentParser) -> None:
     ap.add_argument("--enforce-eager", action="store_true")
 
 
-def build_runner(args) -> ModelRunner:
-    cfg = EngineConfig(model=None if args.model_path else args.model, model_path=args.model_path, device=args.device,
+def build_runner(args, kv_pool_ipc: bool = False) -> ModelRunner:
+    cfg = EngineConfig(kv_pool_ipc=kv_pool_ipc, model=None if args.model_path else args.model, model_path=args.model_path, device=args.device,
                        dtype=args.dtype, block_size=args.block_size, num_blocks=args.num_blocks,
                        max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens,
                        max_model_len=args.max_model_len, kv_cache_quant_mode=args.kv_cache_quant_mode,
@@ -267,7 +267,7 @@ class DecodeWorker:
         self.args = args
         self.wd = WorkDir(args.work_dir)
         init_world(args)
-        self.runner = build_runner(args)
+        self.runner = build_runner(args, kv_pool_ipc=args.backend == "ipc_push")
         cfg = self.runner.config
         if args.backend == "shared_memory":
             store = SharedMemoryKVStoreBackend()

@@ -1,0 +1,60 @@
+"""P/D on GPUs: in-process coordinator on one GPU, and worker processes on two GPUs moving
+the KV with the NVLink IPC push kernel and with NCCL point-to-point."""
+import pytest
+import torch
+
+from nanovllm_self_b200 import LLM, SamplingParams
+
+pytestmark = pytest.mark.gpu
+
+KW = dict(max_model_len=1024, max_num_seqs=16, num_blocks=128, block_size=16, cuda_graph_max_bs=16)
+
+
+def _rows():
+    g = torch.Generator().manual_seed(31)
+    return [{"id": f"q{i}", "prompt_ids": torch.randint(0, 2048, (n,), generator=g).tolist(), "max_tokens": m,
+             "input_tokens": n, "session_id": f"s{i % 2}"} for i, (n, m) in enumerate([(40, 8), (150, 12), (9, 1),
+                                                                                         (333, 6)])]
+
+
+def _want():
+    llm = LLM("tiny-gpu", device="cuda:0", **KW)
+    return {r["id"]: llm.generate([r["prompt_ids"]], SamplingParams(temperature=0, max_tokens=r["max_tokens"],
+                                                                     ignore_eos=True))[0][len(r["prompt_ids"]):]
+            for r in _rows()}
+
+
+def _agree(got, want):
+    tot = sum(len(v) for v in want.values())
+    ok = sum(a == b for k in want for a, b in zip(got.get(k, []), want[k]))
+    return ok / tot
+
+
+def test_pd_coordinator_single_gpu():
+    from nanovllm_self_b200.config import EngineConfig
+    from nanovllm_self_b200.pd.coordinator import PDCoordinator
+    want = _want()
+    pd = PDCoordinator(EngineConfig(model="tiny-gpu", device="cuda:0", **KW))
+    rows = _rows()
+    got = {}
+    for r in rows:
+        got[r["id"]] = pd.generate([r["prompt_ids"]], max_tokens=r["max_tokens"])[0][len(r["prompt_ids"]):]
+    assert _agree(got, want) > 0.9
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("backend", ["ipc_push", "sync_gpu"])
+def test_pd_pool_two_gpus(tmp_path, backend):
+    from nanovllm_self_b200.pd.multiprocess.pool import PDPool
+    want = _want()
+    args = ["--max-model-len", "1024", "--block-size", "16", "--num-blocks", "128", "--max-num-seqs", "16"]
+    pool = PDPool(tmp_path, 1, 1, backend, "tiny-gpu", prefill_devices=["cuda:0"], decode_devices=["cuda:1"],
+                  worker_args=args, handshake_timeout_s=60, nccl_port=29731)
+    pool.start()
+    try:
+        s = pool.run(_rows(), concurrency=2, timeout_s=300)
+    finally:
+        pool.shutdown()
+    assert s["num_errors"] == 0, pool.results
+    got = {pool.submitted[b]["row"]["id"]: r["output_ids"] for b, r in pool.results.items()}
+    assert _agree(got, want) > 0.9
