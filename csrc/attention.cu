@@ -105,21 +105,29 @@ __device__ __forceinline__ void load_tile(const AttnArgs& a, const void* cache, 
   }
 }
 
-// fp8 staging tile -> scaled bf16 swizzled tile.
-__device__ __forceinline__ void convert_fp8_tile(const AttnArgs& a, const float* scales, int b, int h, int tile,
-                                                 int k_len, const uint8_t* stage, uint8_t* dst) {
-  const int* bt = a.block_tables + (int64_t)b * a.W;
+// Per-row dequantisation scales of one 64-key tile into shared memory (threads 0..63).
+__device__ __forceinline__ void tile_row_scales(const AttnArgs& a, const float* scales, int b, int h, int tile,
+                                                int k_len, float* row_scale) {
+  if (threadIdx.x < KTILE) {
+    const int* bt = a.block_tables + (int64_t)b * a.W;
+    const int tok = tile * KTILE + threadIdx.x;
+    float s = 0.f;
+    if (tok < k_len) {
+      const int bi = tok / a.block_size;
+      const int blk = bi < a.W ? bt[bi] : -1;
+      if (blk >= 0 && blk < a.num_blocks) s = scales[(int64_t)blk * a.nkv + h];
+    }
+    row_scale[threadIdx.x] = s;
+  }
+}
+
+// fp8 staging tile -> scaled bf16 swizzled tile (row scales from tile_row_scales).
+__device__ __forceinline__ void convert_fp8_tile(const float* row_scale, const uint8_t* stage, uint8_t* dst) {
 #pragma unroll
   for (int i = 0; i < KTILE * 16 / 128; ++i) {
     int idx = threadIdx.x + i * 128;
     int r = idx >> 4, c = idx & 15;
-    int tok = tile * KTILE + r;
-    float s = 0.f;
-    if (tok < k_len) {
-      int bi = tok / a.block_size;
-      int blk = bi < a.W ? bt[bi] : -1;
-      if (blk >= 0 && blk < a.num_blocks) s = scales[(int64_t)blk * a.nkv + h];
-    }
+    const float s = row_scale[r];
     uint2 raw = *reinterpret_cast<const uint2*>(stage + r * AD + c * 8);
     float f[8];
     e4m3x4_to_f32(raw.x, f);
@@ -319,17 +327,23 @@ __global__ void __launch_bounds__(160, 2)
     uint32_t kb, vb;  // ldmatrix bases; rows are addressed as warp-local 0..15 (+ warp*16 for TMA tiles)
     int rbase;
     if (FP8) {
-      // dequantise this warp's 16 K rows and 16 V rows into its bf16 staging (row 256 B, xor swizzle)
+      // dequantise this warp's 16 K rows and 16 V rows into its bf16 staging (row 256 B, xor
+      // swizzle).  The 16 rows lie in one block (block_size >= 16), so one scale pair serves all.
+      float ksc = 0.f, vsc = 0.f;
+      if (lane == 0) {
+        const int bi = (t * KTILE + warp * 16) / a.block_size;
+        int blk = bi < a.W ? bt[bi] : 0;
+        if (blk < 0 || blk >= a.num_blocks) blk = 0;
+        ksc = a.k_scale[(int64_t)blk * a.nkv + h];
+        vsc = a.v_scale[(int64_t)blk * a.nkv + h];
+      }
+      ksc = __shfl_sync(FULL_MASK, ksc, 0);
+      vsc = __shfl_sync(FULL_MASK, vsc, 0);
 #pragma unroll
       for (int it = 0; it < 4; ++it) {
         const int idx = lane + it * 32;       // 0..127 -> (row 0..15, 16-byte fp8 chunk 0..7)
         const int r = idx >> 3, c = idx & 7;
         const int gr = warp * 16 + r;
-        const int tok = t * KTILE + gr;
-        const int bi = tok / a.block_size;
-        int blk = bi < a.W ? bt[bi] : 0;
-        if (blk < 0 || blk >= a.num_blocks) blk = 0;
-        const float ksc = a.k_scale[(int64_t)blk * a.nkv + h], vsc = a.v_scale[(int64_t)blk * a.nkv + h];
         const uint32_t soff = gr * 128 + ((c ^ (gr & 7)) << 4);
         const uint4 kr = *reinterpret_cast<const uint4*>(kt + soff);
         const uint4 vr = *reinterpret_cast<const uint4*>(vt + soff);
@@ -479,6 +493,311 @@ __global__ void __launch_bounds__(160, 2)
   }
 }
 
+// fp8 decode with the keys on the MMA's M side.  S^T[16 keys x 8 heads] = K Q^T and
+// O^T[16 dims x 8 heads] += V^T P^T, f16 tensor-core inputs, fp32 accumulators.  The fp8
+// bytes go from shared memory straight into MMA fragments (one cvt.f16x2.e4m3x2 per two
+// values; no staging copy): the reduction dimension of both products may be permuted
+// freely, so a thread's K fragment is 32 contiguous bytes of one key row (dims 32c..32c+31
+// for lane%4 = c, Q loaded in the same order) and its V fragment 16 contiguous bytes of
+// four key rows (output dims 16r..16r+15 for lane/4 = r); P^T goes from the S^T
+// accumulator to the B operand with two movmatrix transposes.  Scales: K's folds into the
+// score multiplier; V's is applied by keeping the accumulator in units of the current
+// tile's scale (the online-softmax rescale absorbs the ratio between tiles).  G <= 8,
+// block_size >= 16 (a warp's 16 keys then share one block and one scale pair).
+__device__ __forceinline__ void mma_f16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Two e4m3 pairs (the low and high 16 bits of x) -> two f16x2 words.
+__device__ __forceinline__ void e4m3x2x2_to_f16x2(uint32_t x, uint32_t& lo, uint32_t& hi) {
+  asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n cvt.rn.f16x2.e4m3x2 %0, l;\n cvt.rn.f16x2.e4m3x2 %1, h;\n}\n"
+      : "=r"(lo), "=r"(hi)
+      : "r"(x));
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(x));
+  return d;
+}
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %2, %1;" : "=r"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+__global__ void __launch_bounds__(160, 3)
+    attn_decode_fp8_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                           DecodeArgs da) {
+  const AttnArgs& a = da.a;
+  extern __shared__ __align__(1024) uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int KV_TILE = KTILE * AD;
+  constexpr int STAGE = 2 * KV_TILE;
+  const int G = a.nq / a.nkv;
+  uint8_t* comb = dsm + DSTAGES * STAGE;  // [4][G][128] f32 + [4][16][2] f32
+  uint64_t* bars = reinterpret_cast<uint64_t*>(comb + 4 * G * AD * 4 + 4 * 16 * 2 * 4);
+  int* done_ctr = reinterpret_cast<int*>(bars + 2 * DSTAGES);
+  const uint32_t bar0 = smem_u32(bars);
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z + a.seq_offset;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int k_len = a.ctx_lens[b];
+  const int qrow = a.cu_q[b];
+  const int n_tiles = (k_len + KTILE - 1) / KTILE;
+  const int per = (n_tiles + a.splits - 1) / a.splits;
+  const int t0 = split * per;
+  const int t1 = min(n_tiles, t0 + per);
+  const int qh0 = h * G;
+
+  if (t0 >= t1) {
+    if (a.splits > 1) {
+      for (int r = threadIdx.x; r < G; r += blockDim.x)
+        a.part_lse[((int64_t)b * a.nq + qh0 + r) * a.splits + split] = -INFINITY;
+    } else {
+      for (int i = threadIdx.x; i < G * AD; i += blockDim.x)
+        a.out[((int64_t)qrow * a.nq + qh0) * AD + i] = __float2bfloat16(0.f);
+    }
+    return;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < DSTAGES; ++s) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8u * s));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;" ::"r"(bar0 + 8u * (DSTAGES + s)));
+    }
+    *done_ctr = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 4) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      const int* bt = a.block_tables + (int64_t)b * a.W;
+      const int rpb = da.rows_per_box;
+      const int nsub = KTILE / rpb;
+      int issued = 0;
+      for (int t = t0; t < t1; ++t, ++issued) {
+        const int i = t - t0, s = i % DSTAGES;
+        if (!att_wait(bar0 + 8u * (DSTAGES + s), ((i / DSTAGES) & 1) ^ 1, 3)) break;
+        const uint32_t full = bar0 + 8u * s;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full), "r"(STAGE) : "memory");
+        const uint32_t kdst = smem_u32(dsm + s * STAGE), vdst = kdst + KV_TILE;
+        for (int j = 0; j < nsub; ++j) {
+          const int tok = t * KTILE + j * rpb;
+          const int bi = tok / a.block_size;
+          int blk = bi < a.W ? bt[bi] : 0;
+          if (blk < 0 || blk >= a.num_blocks) blk = 0;
+          const int row = (blk * a.nkv + h) * a.block_size + (tok % a.block_size);
+          const uint32_t off = j * rpb * AD;
+          asm volatile(
+              "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+              "[%2];" ::"r"(kdst + off), "l"(reinterpret_cast<uint64_t>(&kmap)), "r"(full), "r"(0), "r"(row)
+              : "memory");
+          asm volatile(
+              "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+              "[%2];" ::"r"(vdst + off), "l"(reinterpret_cast<uint64_t>(&vmap)), "r"(full), "r"(0), "r"(row)
+              : "memory");
+        }
+      }
+      // Do not leave while copies this thread issued may still be landing.
+      const int n = issued < DSTAGES ? issued : DSTAGES;
+      for (int i = issued - n; i < issued; ++i) {
+        const uint32_t full = bar0 + 8u * (i % DSTAGES);
+        const uint64_t tw = att_timer();
+        while (!att_try(full, (i / DSTAGES) & 1) && att_timer() - tw < ATT_WAIT_NS) {
+        }
+      }
+    }
+    return;
+  }
+
+  // --------------------------------------------------------------- consumers
+  const int r = lane >> 2, c = lane & 3;
+  // Q^T fragments (B operand): head r, dims 32c + 4kk + {0,1} and {2,3}; heads >= G are zero
+  uint32_t qf[8][2];
+  {
+    const __nv_bfloat16* qp = a.q + ((int64_t)qrow * a.nq + qh0 + (r < G ? r : 0)) * AD + 32 * c;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 v = r < G ? *reinterpret_cast<const uint4*>(qp + 8 * i) : make_uint4(0, 0, 0, 0);
+      float f[8];
+      bf16x8_to_f32(v, f);
+      qf[2 * i][0] = pack_f16(f[0], f[1]);
+      qf[2 * i][1] = pack_f16(f[2], f[3]);
+      qf[2 * i + 1][0] = pack_f16(f[4], f[5]);
+      qf[2 * i + 1][1] = pack_f16(f[6], f[7]);
+    }
+  }
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f, vsc_run = 1.f;
+  const int* bt = a.block_tables + (int64_t)b * a.W;
+  const int kr0 = warp * 16 + r, kr1 = kr0 + 8;       // this thread's K rows in the tile
+  const int vr = warp * 16 + 2 * c;                   // V rows vr, vr+1, vr+8, vr+9
+
+  for (int t = t0; t < t1; ++t) {
+    const int i = t - t0, s = i % DSTAGES;
+    if (!att_wait(bar0 + 8u * s, (i / DSTAGES) & 1, 4)) break;
+    const uint8_t* kt = dsm + s * STAGE;
+    const uint8_t* vt = kt + KV_TILE;
+    // K: bytes [32c, 32c + 32) of rows kr0 and kr1 (TMA 128-byte swizzle: chunk ^ (row & 7))
+    const uint4 ka0 = *reinterpret_cast<const uint4*>(kt + kr0 * AD + (((2 * c) ^ (kr0 & 7)) << 4));
+    const uint4 ka1 = *reinterpret_cast<const uint4*>(kt + kr0 * AD + (((2 * c + 1) ^ (kr0 & 7)) << 4));
+    const uint4 kb0 = *reinterpret_cast<const uint4*>(kt + kr1 * AD + (((2 * c) ^ (kr1 & 7)) << 4));
+    const uint4 kb1 = *reinterpret_cast<const uint4*>(kt + kr1 * AD + (((2 * c + 1) ^ (kr1 & 7)) << 4));
+    // V: bytes [16r, 16r + 16) of rows vr, vr+1, vr+8, vr+9
+    uint4 v0 = *reinterpret_cast<const uint4*>(vt + vr * AD + ((r ^ (vr & 7)) << 4));
+    uint4 v1 = *reinterpret_cast<const uint4*>(vt + (vr + 1) * AD + ((r ^ ((vr + 1) & 7)) << 4));
+    uint4 v2 = *reinterpret_cast<const uint4*>(vt + (vr + 8) * AD + ((r ^ ((vr + 8) & 7)) << 4));
+    uint4 v3 = *reinterpret_cast<const uint4*>(vt + (vr + 9) * AD + ((r ^ ((vr + 9) & 7)) << 4));
+    __syncwarp();
+    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar0 + 8u * (DSTAGES + s)) : "memory");
+    const int key0 = t * KTILE + warp * 16;
+    if (key0 + 16 > k_len) {
+      // rows past the context may hold any bytes (an e4m3 NaN included): zero them
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      if (key0 + 2 * c >= k_len) v0 = z;
+      if (key0 + 2 * c + 1 >= k_len) v1 = z;
+      if (key0 + 2 * c + 8 >= k_len) v2 = z;
+      if (key0 + 2 * c + 9 >= k_len) v3 = z;
+    }
+    float ksc = 0.f, vsc = 0.f;
+    if (lane == 0) {
+      const int bi = key0 / a.block_size;
+      int blk = bi < a.W ? bt[bi] : 0;
+      if (blk < 0 || blk >= a.num_blocks) blk = 0;
+      ksc = a.k_scale[(int64_t)blk * a.nkv + h];
+      vsc = a.v_scale[(int64_t)blk * a.nkv + h];
+    }
+    ksc = __shfl_sync(FULL_MASK, ksc, 0);
+    vsc = __shfl_sync(FULL_MASK, vsc, 0);
+
+    // S^T = K Q^T over 8 steps of 16 (permuted) dims
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint32_t w0 = word_of(kk < 4 ? ka0 : ka1, kk & 3), w1 = word_of(kk < 4 ? kb0 : kb1, kk & 3);
+      uint32_t af[4];
+      e4m3x2x2_to_f16x2(w0, af[0], af[2]);
+      e4m3x2x2_to_f16x2(w1, af[1], af[3]);
+      mma_f16(sc, af, qf[kk][0], qf[kk][1]);
+    }
+    // online softmax per head (columns 2c, 2c+1); rows are keys kr0 (sc[0..1]) and kr1 (sc[2..3])
+    const float mul = ksc * a.scale_log2;
+    const bool ok0 = key0 + r < k_len, ok1 = key0 + r + 8 < k_len;
+    sc[0] = ok0 ? sc[0] * mul : -INFINITY;
+    sc[1] = ok0 ? sc[1] * mul : -INFINITY;
+    sc[2] = ok1 ? sc[2] * mul : -INFINITY;
+    sc[3] = ok1 ? sc[3] * mul : -INFINITY;
+    float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(FULL_MASK, mx0, o));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(FULL_MASK, mx1, o));
+    }
+    const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
+    const float base0 = nm0 == -INFINITY ? 0.f : nm0, base1 = nm1 == -INFINITY ? 0.f : nm1;
+    const float al0 = exp2f(m0 - base0), al1 = exp2f(m1 - base1);
+    m0 = nm0;
+    m1 = nm1;
+    const float p0 = exp2f(sc[0] - base0), p1 = exp2f(sc[1] - base1);
+    const float p2 = exp2f(sc[2] - base0), p3 = exp2f(sc[3] - base1);
+    l0 = l0 * al0 + p0 + p2;
+    l1 = l1 * al1 + p1 + p3;
+    // the accumulator is kept in units of the current tile's V scale
+    const float ratio = vsc_run / vsc;
+    vsc_run = vsc;
+    const float f0 = al0 * ratio, f1 = al1 * ratio;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      acc[u][0] *= f0;
+      acc[u][1] *= f1;
+      acc[u][2] *= f0;
+      acc[u][3] *= f1;
+    }
+    // P^T as the B operand: transpose the [key][head] f16 pairs
+    const uint32_t pb0 = movmatrix_t(pack_f16(p0, p1));
+    const uint32_t pb1 = movmatrix_t(pack_f16(p2, p3));
+    // O^T += V^T P^T over 8 tiles of 16 output dims (dims 16r + 2u, 16r + 2u + 1)
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const uint32_t sel = (u & 1) ? 0x7362u : 0x5140u;
+      const uint32_t x = prmt(word_of(v0, u >> 1), word_of(v1, u >> 1), sel);
+      const uint32_t y = prmt(word_of(v2, u >> 1), word_of(v3, u >> 1), sel);
+      uint32_t af[4];
+      e4m3x2x2_to_f16x2(x, af[0], af[1]);
+      e4m3x2x2_to_f16x2(y, af[2], af[3]);
+      mma_f16(acc[u], af, pb0, pb1);
+    }
+  }
+
+  // publish this warp's state; the last warp to arrive merges all four
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    l0 += __shfl_xor_sync(FULL_MASK, l0, o);
+    l1 += __shfl_xor_sync(FULL_MASK, l1, o);
+  }
+  float* sm_acc = reinterpret_cast<float*>(comb);
+  float* sm_ml = sm_acc + 4 * G * AD;
+  const int h0 = 2 * c, h1 = 2 * c + 1;
+  if (r == 0) {
+    sm_ml[(warp * 16 + h0) * 2] = m0;
+    sm_ml[(warp * 16 + h0) * 2 + 1] = l0;
+    sm_ml[(warp * 16 + h1) * 2] = m1;
+    sm_ml[(warp * 16 + h1) * 2 + 1] = l1;
+  }
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    if (h0 < G)
+      *reinterpret_cast<float2*>(sm_acc + (warp * G + h0) * AD + 16 * r + 2 * u) =
+          make_float2(acc[u][0] * vsc_run, acc[u][2] * vsc_run);
+    if (h1 < G)
+      *reinterpret_cast<float2*>(sm_acc + (warp * G + h1) * AD + 16 * r + 2 * u) =
+          make_float2(acc[u][1] * vsc_run, acc[u][3] * vsc_run);
+  }
+  __threadfence_block();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = atomicAdd(done_ctr, 1) == 3;
+  last = __shfl_sync(FULL_MASK, last, 0);
+  if (!last) return;
+  __threadfence_block();
+  for (int i = lane; i < G * AD; i += 32) {
+    const int hh = i / AD, d = i % AD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_ml[(w * 16 + hh) * 2]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float f = exp2f(sm_ml[(w * 16 + hh) * 2] - M);
+        L += sm_ml[(w * 16 + hh) * 2 + 1] * f;
+        O += sm_acc[(w * G + hh) * AD + d] * f;
+      }
+    }
+    const float o = L > 0.f ? O / L : 0.f;
+    if (a.splits == 1) {
+      a.out[((int64_t)qrow * a.nq + qh0 + hh) * AD + d] = __float2bfloat16(o);
+    } else {
+      const int64_t pi = ((int64_t)b * a.nq + qh0 + hh) * a.splits + split;
+      a.part_o[pi * AD + d] = o;
+      if (d == 0) a.part_lse[pi] = L > 0.f ? M + log2f(L) : -INFINITY;
+    }
+  }
+}
+
 // Merge split partials: one CTA per (seq, q head), one thread per dim.
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                     const int* __restrict__ cu_q, __nv_bfloat16* __restrict__ out, int nq, int splits,
@@ -560,8 +879,12 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
     __syncthreads();
     int cs = st;
     if (FP8) {
-      convert_fp8_tile(a, a.k_scale, b, h, t, k_len, stg + st * KTILE * AD, sk);
-      convert_fp8_tile(a, a.v_scale, b, h, t, k_len, stg + (2 + st) * KTILE * AD, sv);
+      __shared__ float ks_row[KTILE], vs_row[KTILE];
+      tile_row_scales(a, a.k_scale, b, h, t, k_len, ks_row);
+      tile_row_scales(a, a.v_scale, b, h, t, k_len, vs_row);
+      __syncthreads();
+      convert_fp8_tile(ks_row, stg + st * KTILE * AD, sk);
+      convert_fp8_tile(vs_row, stg + (2 + st) * KTILE * AD, sv);
       __syncthreads();
       cs = 0;
     }
@@ -704,6 +1027,10 @@ static bool kv_map(CUtensorMap* m, const void* base, int64_t rows, bool fp8, int
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+static int decode_fp8_smem(int G) {
+  return 1024 + DSTAGES * 2 * KTILE * AD + 4 * G * AD * 4 + 4 * 16 * 2 * 4 + 2 * DSTAGES * 8 + 16;
+}
+
 static int decode_tma_smem(bool fp8, int G) {
   const int stage = 2 * (fp8 ? KTILE * AD : KTILE * ROWB);
   return 1024 + DSTAGES * stage + (fp8 ? 4 * 8192 : 0) + 4 * G * AD * 4 + 4 * 16 * 2 * 4 + 2 * DSTAGES * 8 + 16;
@@ -745,7 +1072,14 @@ cudaError_t launch_attn_decode(const AttnLaunch& L, cudaStream_t stream) {
   dim3 grid(L.splits, L.nkv, L.num_seqs);
   const int sm = decode_tma_smem(L.kv_fp8, L.nq / L.nkv);
   const int sm_max = decode_tma_smem(L.kv_fp8, 16);
-  if (L.kv_fp8) {
+  if (L.kv_fp8 && L.nq / L.nkv <= 8 && L.block_size >= 16) {
+    static bool cfg = false;
+    if (!cfg) {
+      cudaFuncSetAttribute(attn_decode_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_fp8_smem(8));
+      cfg = true;
+    }
+    attn_decode_fp8_kernel<<<grid, 160, decode_fp8_smem(L.nq / L.nkv), stream>>>(km, vm, da);
+  } else if (L.kv_fp8) {
     static bool cfg = false;
     if (!cfg) {
       cudaFuncSetAttribute(attn_decode_tma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_max);

@@ -33,7 +33,15 @@ __device__ __forceinline__ float to_f<float>(float v) { return v; }
 template <>
 __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
 
-// Partial (max, argmax) of the noised scores over one column chunk of one row.
+__device__ __forceinline__ void consider(float v, int c, float& best, int& bidx) {
+  if (v > best || (v == best && c < bidx)) {
+    best = v;
+    bidx = c;
+  }
+}
+
+// Partial (max, argmax) of the noised scores over one column chunk of one row.  bf16
+// rows are read 8 columns per 16-byte load when the row start is 16-byte aligned.
 template <typename T>
 __global__ void __launch_bounds__(256) sample_partial_kernel(const T* __restrict__ logits, int64_t ld, int V,
                                                              int64_t col_offset, const float* __restrict__ temps,
@@ -49,12 +57,36 @@ __global__ void __launch_bounds__(256) sample_partial_kernel(const T* __restrict
   float best = -INFINITY;
   int bidx = 0x7fffffff;
   const T* lr = logits + (int64_t)row * ld;
-  for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
-    float v = to_f<T>(lr[c]);
-    if (!greedy) v = v * inv_t + gumbel(seed, step, row, col_offset + c);
-    if (v > best || (v == best && c < bidx)) {
-      best = v;
-      bidx = c;
+  constexpr bool VEC = sizeof(T) == 2;
+  if (VEC && (((uintptr_t)(lr + c0)) & 15) == 0 && greedy) {
+    const int nv = (c1 - c0) >> 3;
+    const uint4* src = reinterpret_cast<const uint4*>(lr + c0);
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+      float f[8];
+      bf16x8_to_f32(__ldg(src + i), f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) consider(f[j], c0 + i * 8 + j, best, bidx);
+    }
+    for (int c = c0 + nv * 8 + threadIdx.x; c < c1; c += blockDim.x) consider(to_f<T>(lr[c]), c, best, bidx);
+  } else if (VEC && (((uintptr_t)(lr + c0)) & 15) == 0) {
+    const int nv = (c1 - c0) >> 3;
+    const uint4* src = reinterpret_cast<const uint4*>(lr + c0);
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+      float f[8];
+      bf16x8_to_f32(__ldg(src + i), f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = c0 + i * 8 + j;
+        consider(f[j] * inv_t + gumbel(seed, step, row, col_offset + c), c, best, bidx);
+      }
+    }
+    for (int c = c0 + nv * 8 + threadIdx.x; c < c1; c += blockDim.x)
+      consider(to_f<T>(lr[c]) * inv_t + gumbel(seed, step, row, col_offset + c), c, best, bidx);
+  } else {
+    for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
+      float v = to_f<T>(lr[c]);
+      if (!greedy) v = v * inv_t + gumbel(seed, step, row, col_offset + c);
+      consider(v, c, best, bidx);
     }
   }
   __shared__ float sv[8];
@@ -117,8 +149,10 @@ __global__ void sample_final_kernel(const float* __restrict__ part_val, const in
 }
 
 int sample_num_chunks(int rows, int V) {
-  int want = (2 * 148 + rows - 1) / (rows > 0 ? rows : 1);
-  int max_chunks = (V + 2047) / 2048;
+  // ~4 CTAs per SM in total, chunks of at least 4096 columns (a multiple of 8, so every
+  // chunk of a 16-byte-aligned row starts aligned)
+  int want = (4 * 148 + rows - 1) / (rows > 0 ? rows : 1);
+  int max_chunks = (V + 4095) / 4096;
   int n = want < max_chunks ? want : max_chunks;
   return n < 1 ? 1 : n;
 }
@@ -128,6 +162,7 @@ cudaError_t launch_sample(const void* logits, int logits_is_bf16, int64_t ld, in
                           int* out_tok, float* out_val, cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
   int chunk = (V + nchunk - 1) / nchunk;
+  chunk = (chunk + 7) & ~7;
   dim3 grid(nchunk, rows);
   if (logits_is_bf16)
     sample_partial_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), ld, V,

@@ -1,0 +1,170 @@
+"""Single-kernel cases of the hot ops, timed with CUDA events or run once for a profiler.
+
+``python -m nanovllm_self_b200.benchmarks.kernels <case> [--mode time|profile] [--iters N]``
+
+``--mode time`` (default) runs 3 warm-up launches, then ``--iters`` launches, each after a
+write of a 256 MiB buffer (> the 126 MB L2) so that every timed launch reads from HBM, and
+prints one JSON line: the median device time, the algorithmic bytes or FLOPs of one launch
+and their fraction of the peaks in ``MEASURED_PEAKS.json`` (repository root) when present.
+``--mode profile`` launches the kernel three times and exits: the small workload a
+profiler capture of one launch (``-s 1 -c 1``) needs.
+
+Shapes are Qwen3-8B's (32 query heads, 8 KV heads, head dim 128, hidden 4096,
+intermediate 12288, vocab 151936); every case holds well under 2 GB on the device.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+
+import torch
+
+from ..ops.cuda_ops import CudaOps
+
+NQ, NKV, D, HID, INTER, VOCAB = 32, 8, 128, 4096, 12288, 151936
+CASES = ("attn_decode", "attn_decode_fp8", "attn_prefill", "attn_prefill_fp8", "gemm_prefill", "gemm_decode",
+         "gemm_decode256", "qkv_post", "qkv_post_fp8", "add_rmsnorm", "silu_mul", "sample")
+
+
+class _Ctx:
+    pass
+
+
+def _paged(B, ctx_len, qlen, fp8, dev, bs=256):
+    nbps = (ctx_len + bs - 1) // bs
+    nb = B * nbps + 1
+    kc = torch.randn(nb, NKV, bs, D, device=dev).to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    ks = vs = None
+    if fp8:
+        kc, vc = kc.to(torch.float8_e4m3fn), vc.to(torch.float8_e4m3fn)
+        ks = torch.full((nb, NKV), 1.0, device=dev)
+        vs = torch.full((nb, NKV), 1.0, device=dev)
+    c = _Ctx()
+    c.block_tables = torch.arange(B * nbps, device=dev, dtype=torch.int32).view(B, nbps)
+    c.cu_seqlens_q = torch.arange(0, B * qlen + 1, qlen, device=dev, dtype=torch.int32)
+    c.context_lens = torch.full((B,), ctx_len, device=dev, dtype=torch.int32)
+    c.max_seqlen_q, c.max_seqlen_k = qlen, ctx_len
+    c.num_decode_seqs = B if qlen == 1 else 0
+    c.num_seqs = B
+    q = torch.randn(B * qlen, NQ * D, device=dev).to(torch.bfloat16)
+    return q, kc, vc, ks, vs, c
+
+
+def build_case(name: str, ops: CudaOps, dev="cuda"):
+    """Returns (launch, bytes, flops) for one case; ``launch()`` runs the op once."""
+    torch.manual_seed(0)
+    if name.startswith("attn_decode"):
+        fp8 = name.endswith("fp8")
+        B, L = 128, 2048
+        q, kc, vc, ks, vs, c = _paged(B, L, 1, fp8, dev)
+        kv_bytes = 2 * B * NKV * L * D * kc.element_size()
+        return (lambda: ops.attention(q, kc, vc, c, D ** -0.5, ks, vs)), kv_bytes + 2 * q.numel() * 2, \
+            4 * B * NQ * L * D
+    if name.startswith("attn_prefill"):
+        fp8 = name.endswith("fp8")
+        B, L = 8, 2048
+        q, kc, vc, ks, vs, c = _paged(B, L, L, fp8, dev)
+        return (lambda: ops.attention(q, kc, vc, c, D ** -0.5, ks, vs)), None, 2 * B * NQ * L * L * D
+    if name.startswith("gemm"):
+        m, n, k = {"gemm_prefill": (4096, 2 * INTER, HID), "gemm_decode": (64, (NQ + 2 * NKV) * D, HID),
+                   "gemm_decode256": (256, 2 * INTER, HID)}[name]
+        x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+        w = (torch.randn(n, k, device=dev) * 0.02).to(torch.bfloat16)
+        out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        return (lambda: ops.linear(x, w, out)), 2 * (m * k + n * k + m * n), 2 * m * n * k
+    if name.startswith("qkv_post"):
+        from ..ops.torch_ref import rope_cos_sin
+        fp8 = name.endswith("fp8")
+        T = 16384
+        qkv = torch.randn(T, (NQ + 2 * NKV) * D, device=dev).to(torch.bfloat16)
+        nb = T // 256 + 1
+        kdt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+        kc = torch.zeros(nb, NKV, 256, D, device=dev, dtype=kdt)
+        vc = torch.zeros_like(kc)
+        ks = torch.ones(nb, NKV, device=dev) if fp8 else None
+        vs = torch.ones(nb, NKV, device=dev) if fp8 else None
+        pos = torch.arange(T, device=dev, dtype=torch.int32) % 2048
+        slots = torch.arange(T, device=dev, dtype=torch.int32)
+        cs = rope_cos_sin(D, 4096, 1e6, device=dev)
+        w = torch.ones(D, device=dev, dtype=torch.bfloat16)
+        nbytes = qkv.numel() * 2 + T * NQ * D * 2 + 2 * T * NKV * D * kc.element_size()
+        return (lambda: ops.qkv_post(qkv, w, w, 1e-6, pos, cs, kc, vc, slots, ks, vs, NQ, NKV, D)), nbytes, None
+    if name == "add_rmsnorm":
+        x = torch.randn(16384, HID, device=dev).to(torch.bfloat16)
+        r = torch.randn_like(x)
+        w = torch.ones(HID, device=dev, dtype=torch.bfloat16)
+        return (lambda: ops.add_rmsnorm(x, r, w, 1e-6)), 4 * x.numel() * 2, None
+    if name == "silu_mul":
+        x = torch.randn(8192, 2 * INTER, device=dev).to(torch.bfloat16)
+        return (lambda: ops.silu_mul(x)), x.numel() * 2 * 3 // 2, None
+    if name == "sample":
+        logits = torch.randn(256, VOCAB, device=dev).to(torch.bfloat16)
+        t = torch.zeros(256, device=dev)
+        st = torch.tensor([0, 1], dtype=torch.int64, device=dev)
+        return (lambda: ops.sample(logits, t, step=st)), logits.numel() * 2, None
+    raise ValueError(f"unknown case {name!r}; one of {', '.join(CASES)}")
+
+
+def _peaks():
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def time_case(name: str, iters: int = 20) -> dict:
+    ops = CudaOps()
+    launch, nbytes, flops = build_case(name, ops)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        launch()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e3)
+    us = statistics.median(times)
+    hbm, tfl, src = _peaks()
+    out = {"case": name, "us": round(us, 2), "iters": iters, "l2": "256 MiB write before each launch",
+           "peaks": src}
+    if nbytes:
+        out["gb_s"] = round(nbytes / us / 1e3, 1)
+        out["frac_hbm"] = round(nbytes / us / 1e3 / hbm, 3)
+    if flops:
+        out["tflops"] = round(flops / us / 1e6, 1)
+        out["frac_bf16"] = round(flops / us / 1e6 / tfl, 3)
+    return out
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("case", choices=CASES + ("all",))
+    p.add_argument("--mode", choices=("time", "profile"), default="time")
+    p.add_argument("--iters", type=int, default=20)
+    a = p.parse_args(argv)
+    names = CASES if a.case == "all" else (a.case,)
+    for n in names:
+        if a.mode == "profile":
+            launch = build_case(n, CudaOps())[0]
+            for _ in range(3):
+                launch()
+            torch.cuda.synchronize()
+            print(json.dumps({"case": n, "profiled_launches": 3}), flush=True)
+        else:
+            print(json.dumps(time_case(n, a.iters)), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -142,7 +142,7 @@ class _Ctx:
 
 
 @pytest.mark.parametrize("kv_dtype", [torch.bfloat16, torch.float8_e4m3fn])
-@pytest.mark.parametrize("nq,nkv", [(16, 8), (32, 8), (4, 1), (64, 8)])
+@pytest.mark.parametrize("nq,nkv", [(16, 8), (32, 8), (4, 1), (64, 8), (16, 1)])
 @pytest.mark.parametrize("bs", [16, 256])
 def test_attention_decode_and_prefill(ops, kv_dtype, nq, nkv, bs):
     # 3 decode seqs (various ctx incl. long for split-KV) then 3 prefill seqs (prefix offset, chunk)
