@@ -15,10 +15,24 @@ struct GemmPlan {
   int64_t ws_elems;  // split-K scratch size needed (fp32 elements), 0 if none
   int tiles;         // output tiles
   int prefetch_w;    // stream the weights through an L2 prefetch lookahead
+  int streamk;       // 1: stream-K (even split of tiles x k-blocks over the grid; needs ws + counters)
+  int mt;            // 128-row sub-tiles of the token operand per output tile (1 or 2)
+  int dec;           // 1: decode kernel (all m <= 256 tokens per CTA, runtime bn, cluster split-K)
+  int stages, smem;  // decode kernel: weight-ring depth and dynamic shared memory
+  int a_stages;      // decode kernel: activation-ring depth
 };
 
-// Plan C[m, n] = X[m, k] * W[n, k]^T.  force_* < 0 / 0 = automatic.
+// Plan C[m, n] = X[m, k] * W[n, k]^T.  force_swap < 0 / force_bn 0 / force_splits 0 =
+// automatic; force_splits = -1 or -2 selects stream-K with 1 or 2 sub-tiles of 128 tokens.
 GemmPlan gemm_plan(int m, int n, int k, int force_swap, int force_bn, int force_splits);
+
+// The rank-th cheapest decode-kernel configuration for C[m, n] (m <= 256) by the cost
+// model; false if there is none.
+bool gemm_dec_plan(int m, int n, int k, int rank, GemmPlan* plan);
+
+// Decode kernel with an explicit (bn, splits, activation-ring depth) configuration.
+cudaError_t gemm_dec_explicit(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m,
+                              int n, int k, int bn, int splits, int a_stages, cudaStream_t stream);
 
 // ws: fp32 split-K scratch (plan.ws_elems); counters: 4 int32 per output tile, all zero
 // before the first launch (the kernel leaves them zero).
@@ -27,8 +41,10 @@ cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, vo
 
 // Same product, configuration chosen by timing candidates on first use of a shape (outside
 // stream capture) and cached; inside a capture the cached or heuristic plan is used.
+// ws / ws_elems / counters / num_counters: scratch for stream-K candidates (may be null).
 cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n,
-                            int k, cudaStream_t stream, GemmPlan* chosen);
+                            int k, float* ws, int64_t ws_elems, int* counters, int64_t num_counters,
+                            cudaStream_t stream, GemmPlan* chosen);
 
 // Error word written by a GEMM that gave up on a bounded wait (0 = none).
 int gemm_error_code(int reset);

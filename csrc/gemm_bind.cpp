@@ -35,7 +35,8 @@ void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c10
 }
 
 // Autotuned entry point used by the model (see gemm_bf16_tuned).
-std::vector<int64_t> linear_tuned(const at::Tensor& x, const at::Tensor& w, at::Tensor& out) {
+std::vector<int64_t> linear_tuned(const at::Tensor& x, const at::Tensor& w, at::Tensor& out,
+                                  const c10::optional<at::Tensor>& ws, const c10::optional<at::Tensor>& counters) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
                   out.scalar_type() == at::kBFloat16, "bf16 required");
@@ -44,16 +45,65 @@ std::vector<int64_t> linear_tuned(const at::Tensor& x, const at::Tensor& w, at::
   const int m = (int)x.size(0), k = (int)x.size(1), n = (int)w.size(0);
   TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == n, "shape mismatch");
   at::cuda::CUDAGuard g(x.device());
+  float* wsp = nullptr;
+  int* ctr = nullptr;
+  int64_t ws_n = 0, ctr_n = 0;
+  if (ws.has_value() && counters.has_value()) {
+    TORCH_CHECK(ws->scalar_type() == at::kFloat && counters->scalar_type() == at::kInt, "fp32 ws, int32 counters");
+    wsp = ws->data_ptr<float>();
+    ws_n = ws->numel();
+    ctr = counters->data_ptr<int>();
+    ctr_n = counters->numel();
+  }
   nvb::GemmPlan pl{};
   cudaError_t e = nvb::gemm_bf16_tuned(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(),
-                                       out.stride(0), m, n, k, at::cuda::getCurrentCUDAStream().stream(), &pl);
+                                       out.stride(0), m, n, k, wsp, ws_n, ctr, ctr_n,
+                                       at::cuda::getCurrentCUDAStream().stream(), &pl);
   TORCH_CHECK(e == cudaSuccess, "gemm_bf16 failed: ", cudaGetErrorString(e));
-  return {pl.swap, pl.bn, pl.tiles_p, pl.tiles_q, pl.splits, pl.grid};
+  // (swap, bn, tiles_p, tiles_q, splits, grid); splits < 0: stream-K with -splits sub-tiles;
+  // splits >= 100: decode kernel with splits - 100 K slices
+  return {pl.swap, pl.bn, pl.tiles_p, pl.tiles_q, pl.dec ? 100 + pl.splits : pl.streamk ? -pl.mt : pl.splits,
+          pl.grid};
 }
 
-std::vector<int64_t> plan(int64_t m, int64_t n, int64_t k) {
-  auto pl = nvb::gemm_plan((int)m, (int)n, (int)k, -1, 0, 0);
+std::vector<int64_t> plan(int64_t m, int64_t n, int64_t k, int64_t force_swap, int64_t force_bn,
+                          int64_t force_splits) {
+  auto pl = nvb::gemm_plan((int)m, (int)n, (int)k, (int)force_swap, (int)force_bn, (int)force_splits);
   return {pl.swap, pl.bn, pl.tiles_p, pl.tiles_q, pl.splits, pl.grid, pl.ws_elems, 4 * (int64_t)pl.tiles};
+}
+
+// Decode kernel with the rank-th cheapest configuration of the cost model; returns
+// (mt, bn, splits, weight stages, activation stages), empty if there is no such configuration.
+std::vector<int64_t> linear_dec(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, int64_t rank) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16, "bf16 required");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "unit inner stride required");
+  const int m = (int)x.size(0), k = (int)x.size(1), n = (int)w.size(0);
+  TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == n, "shape mismatch");
+  nvb::GemmPlan pl{};
+  if (!nvb::gemm_dec_plan(m, n, k, (int)rank, &pl)) return {};
+  at::cuda::CUDAGuard g(x.device());
+  cudaError_t e = nvb::gemm_bf16(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0),
+                                 m, n, k, pl, nullptr, nullptr, at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(e == cudaSuccess, "gemm_bf16 failed: ", cudaGetErrorString(e));
+  return {pl.mt, pl.bn, pl.splits, pl.stages, pl.a_stages};
+}
+
+// Decode kernel with an explicit (bn, splits, activation-ring depth) configuration.
+void linear_dec_cfg(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, int64_t bn, int64_t splits,
+                    int64_t a_stages) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16, "bf16 required");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "unit inner stride required");
+  const int m = (int)x.size(0), k = (int)x.size(1), n = (int)w.size(0);
+  TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == n, "shape mismatch");
+  at::cuda::CUDAGuard g(x.device());
+  cudaError_t e = nvb::gemm_dec_explicit(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(),
+                                         out.stride(0), m, n, k, (int)bn, (int)splits, (int)a_stages,
+                                         at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(e == cudaSuccess, "gemm_dec_explicit failed: ", cudaGetErrorString(e));
 }
 
 int64_t error_code(bool reset) { return nvb::gemm_error_code(reset ? 1 : 0); }
@@ -65,7 +115,12 @@ void register_gemm(pybind11::module& m) {
         pybind11::arg("out"), pybind11::arg("ws") = c10::nullopt, pybind11::arg("counters") = c10::nullopt,
         pybind11::arg("force_swap") = -1,
         pybind11::arg("force_bn") = 0, pybind11::arg("force_splits") = 0);
-  m.def("gemm_plan", &plan);
-  m.def("linear_tuned", &linear_tuned, "autotuned tcgen05 GEMM out = x @ w^T");
+  m.def("gemm_plan", &plan, pybind11::arg("m"), pybind11::arg("n"), pybind11::arg("k"),
+        pybind11::arg("force_swap") = -1, pybind11::arg("force_bn") = 0, pybind11::arg("force_splits") = 0);
+  m.def("linear_tuned", &linear_tuned, "autotuned tcgen05 GEMM out = x @ w^T", pybind11::arg("x"),
+        pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("ws") = c10::nullopt,
+        pybind11::arg("counters") = c10::nullopt);
+  m.def("linear_dec", &linear_dec, "decode-sized tcgen05 GEMM with a ranked configuration");
+  m.def("linear_dec_cfg", &linear_dec_cfg, "decode-sized tcgen05 GEMM with an explicit configuration");
   m.def("gemm_error", &error_code, pybind11::arg("reset") = false);
 }

@@ -26,6 +26,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -173,6 +174,8 @@ struct Params {
   float* ws;                 // split-K partials [splits][p_rows][q_rows_pad]
   int64_t ws_ld;
   int* counters;             // split-K arrival counters, 4 per tile (zero between launches)
+  int streamk;               // 1: stream-K split of tiles x k-blocks over the grid
+  int64_t sk_iters;          // stream-K: tiles * num_kb
 };
 
 __device__ __forceinline__ void unit_coords(const Params& p, int unit, int& tp, int& tq, int& split) {
@@ -200,7 +203,9 @@ __device__ __forceinline__ void store_chunk(const Params& p, int pi, int qc, con
 #pragma unroll
       for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = f32_to_bf16x8(f + j);
     } else {
-      for (int j = 0; j < valid; ++j) dst[j] = __float2bfloat16(f[j]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < valid) dst[j] = __float2bfloat16(f[j]);
     }
   } else {
     // C[j, pi]: the 32 lanes of a warp hold consecutive pi, so each store is coalesced
@@ -210,14 +215,77 @@ __device__ __forceinline__ void store_chunk(const Params& p, int pi, int qc, con
   }
 }
 
-template <int BN, int STAGES>
+// Stream-K work split: CTA c owns iterations [sk_start(c), sk_start(c + 1)) of the
+// (tile, k-block) space, so every CTA streams the same number of k-blocks whatever the
+// tile count.  A tile whose k-blocks span several CTAs is finished by the last CTA to
+// deposit its fp32 partial (arrival counted per epilogue warp): nobody waits on another CTA.
+__device__ __forceinline__ int64_t sk_start(const Params& p, int c) {
+  return (int64_t)c * p.sk_iters / gridDim.x;
+}
+// The CTA whose range holds iteration x: the largest c with sk_start(c) <= x.
+__device__ __forceinline__ int sk_owner(const Params& p, int64_t x) {
+  return (int)(((x + 1) * (int64_t)gridDim.x + p.sk_iters - 1) / p.sk_iters) - 1;
+}
+
+// k-blocks [k0, k1) of output tile (tp, tq): one unit of a CTA's work.
+struct Seg {
+  int tp, tq, k0, k1, tile, slot;
+  bool full;  // covers the whole K range (no partial sums)
+};
+
+struct SegIter {
+  int64_t i, e;
+  int u;
+  bool first;
+  __device__ __forceinline__ void init(const Params& p) {
+    if (p.streamk) {
+      i = sk_start(p, blockIdx.x);
+      e = sk_start(p, blockIdx.x + 1);
+    }
+    u = blockIdx.x;
+    first = true;
+  }
+  __device__ __forceinline__ bool next(const Params& p, Seg& s) {
+    int sp;
+    if (p.streamk) {
+      if (i >= e) return false;
+      const int t = (int)(i / p.num_kb);
+      s.k0 = (int)(i - (int64_t)t * p.num_kb);
+      s.k1 = (int)min((int64_t)p.num_kb, (int64_t)s.k0 + (e - i));
+      s.tile = t;
+      unit_coords(p, t, s.tp, s.tq, sp);
+      s.full = s.k0 == 0 && s.k1 == p.num_kb;
+      s.slot = blockIdx.x * 2 + (first ? 0 : 1);
+      i += s.k1 - s.k0;
+      first = false;
+      return true;
+    }
+    if (u >= p.tiles_p * p.tiles_q * p.splits) return false;
+    unit_coords(p, u, s.tp, s.tq, sp);
+    s.k0 = sp * p.kb_per_split;
+    s.k1 = min(p.num_kb, s.k0 + p.kb_per_split);
+    s.tile = u;
+    s.slot = 0;
+    s.full = true;
+    u += gridDim.x;
+    return true;
+  }
+};
+
+// MT = 128-row P sub-tiles per output tile (2: one CTA covers 256 tokens, so each weight
+// k-block it loads feeds two MMAs).  The fp32 accumulators are double-buffered in TMEM
+// when both buffers fit in its 512 columns.
+template <int BN, int STAGES, int MT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_q, Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int P_BYTES = BM * BK * 2;
   constexpr int Q_BYTES = BN * BK * 2;
-  constexpr int STAGE_BYTES = P_BYTES + Q_BYTES;
+  constexpr int STAGE_BYTES = MT * P_BYTES + Q_BYTES;
+  constexpr int ACC_COLS = MT * BN;
+  constexpr int ACC_BUFS = 2 * ACC_COLS <= 512 ? 2 : 1;
+  constexpr uint32_t TMEM_COLS = ACC_BUFS * ACC_COLS;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], final
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * STAGES + 5);
@@ -230,7 +298,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t final_bar = bar0 + 8u * (2 * STAGES + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr uint32_t TMEM_COLS = 2 * BN;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -255,8 +322,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int total_units = p.tiles_p * p.tiles_q * p.splits;
-
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -264,28 +329,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_q)) : "memory");
       uint32_t it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-        int tp, tq, sp;
-        unit_coords(p, u, tp, tq, sp);
-        const int kb0 = sp * p.kb_per_split, nkb = min(p.num_kb, kb0 + p.kb_per_split) - kb0;
-        const int rot = (tp + tq) % nkb;
+      SegIter si;
+      si.init(p);
+      Seg sg;
+      while (ok && si.next(p, sg)) {
+        const int nkb = sg.k1 - sg.k0;
+        const int rot = p.streamk ? 0 : (sg.tp + sg.tq) % nkb;
         const CUtensorMap* wmap = p.swap ? &map_p : &map_q;
-        const int wrow = p.swap ? tp * BM : tq * BN;
+        const int wrow = p.swap ? sg.tp * MT * BM : sg.tq * BN;
         if (p.prefetch_w)
-          for (int i = 0; i < min(nkb, PF_DIST); ++i) tma_prefetch_2d(wmap, (kb0 + (i + rot) % nkb) * BK, wrow);
+          for (int i = 0; i < min(nkb, PF_DIST); ++i) tma_prefetch_2d(wmap, (sg.k0 + (i + rot) % nkb) * BK, wrow);
         for (int i = 0; i < nkb; ++i, ++it) {
-          const int kb = kb0 + (i + rot) % nkb;
+          const int kb = sg.k0 + (i + rot) % nkb;
           const int s = it % STAGES;
           const uint32_t round = it / STAGES;
-          if (p.prefetch_w && i + PF_DIST < nkb) tma_prefetch_2d(wmap, (kb0 + (i + PF_DIST + rot) % nkb) * BK, wrow);
+          if (p.prefetch_w && i + PF_DIST < nkb)
+            tma_prefetch_2d(wmap, (sg.k0 + (i + PF_DIST + rot) % nkb) * BK, wrow);
           if (!mbar_wait(empty(s), (round & 1) ^ 1, abort_flag, 1)) {
             ok = false;
             break;
           }
           const uint32_t st = smem_u32(smem + s * STAGE_BYTES);
           mbar_arrive_expect_tx(full(s), STAGE_BYTES);
-          tma_load_2d(st, &map_p, full(s), kb * BK, tp * BM);
-          tma_load_2d(st + P_BYTES, &map_q, full(s), kb * BK, tq * BN);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+            tma_load_2d(st + mt * P_BYTES, &map_p, full(s), kb * BK, (sg.tp * MT + mt) * BM);
+          tma_load_2d(st + MT * P_BYTES, &map_q, full(s), kb * BK, sg.tq * BN);
         }
       }
       if (!ok) {
@@ -300,18 +369,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t IDESC = idesc_bf16<BN>();
       uint32_t it = 0, tile_it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++tile_it) {
-        int tp, tq, sp;
-        unit_coords(p, u, tp, tq, sp);
-        const int kb0 = sp * p.kb_per_split, nkb = min(p.num_kb, kb0 + p.kb_per_split) - kb0;
-        const int acc = tile_it & 1;
-        const uint32_t use = tile_it >> 1;
+      SegIter si;
+      si.init(p);
+      Seg sg;
+      while (ok && si.next(p, sg)) {
+        const int nkb = sg.k1 - sg.k0;
+        const int acc = ACC_BUFS == 2 ? (tile_it & 1) : 0;
+        const uint32_t use = ACC_BUFS == 2 ? (tile_it >> 1) : tile_it;
         if (!mbar_wait(tempty(acc), (use & 1) ^ 1, abort_flag, 2)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
         for (int i = 0; i < nkb; ++i, ++it) {
           const int s = it % STAGES;
           const uint32_t round = it / STAGES;
@@ -321,17 +391,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           tc_fence_after();
           const uint32_t st = smem_u32(smem + s * STAGE_BYTES);
-          const uint64_t pd = sdesc(st), qd = sdesc(st + P_BYTES);
+          const uint64_t qd = sdesc(st + MT * P_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             // advance 16 elements (32 bytes) along K inside the swizzle atom: +2 in the
             // 16-byte-unit start address field
-            tc_mma(d_tmem, pd + 2 * k, qd + 2 * k, IDESC, (i > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+              tc_mma(d_tmem + mt * BN, sdesc(st + mt * P_BYTES) + 2 * k, qd + 2 * k, IDESC,
+                     (i > 0 || k > 0) ? 1u : 0u);
           }
           tc_commit(empty(s));
         }
         if (!ok) break;
         tc_commit(tfull(acc));
+        ++tile_it;
       }
       // Make sure every issued MMA has finished before TMEM is released.
       tc_commit(final_bar);
@@ -340,28 +414,92 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5)
     const int q4 = warp & 3;            // TMEM lane quarter this warp may access
-    const int row = q4 * 32 + lane;     // accumulator row (P index within the tile)
+    const int row = q4 * 32 + lane;     // accumulator row (P index within a sub-tile)
     uint32_t tile_it = 0;
-    for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++tile_it) {
-      int tp, tq, sp;
-      unit_coords(p, u, tp, tq, sp);
-      const int acc = tile_it & 1;
-      const uint32_t use = tile_it >> 1;
+    SegIter si;
+    si.init(p);
+    Seg sg;
+    while (si.next(p, sg)) {
+      const int acc = ACC_BUFS == 2 ? (tile_it & 1) : 0;
+      const uint32_t use = ACC_BUFS == 2 ? (tile_it >> 1) : tile_it;
       if (!mbar_wait(tfull(acc), use & 1, abort_flag, 4)) break;
       tc_fence_after();
-      const int pi = tp * BM + row;
-      const int q0 = tq * BN;
+      const uint32_t tacc = tmem_base + ((uint32_t)(q4 * 32) << 16) + acc * ACC_COLS;
+      const int q0 = sg.tq * BN;
+      if (sg.full) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(q4 * 32) << 16) + acc * BN + c0, r);
-        float f[32];
+        for (int mt = 0; mt < MT; ++mt) {
+          const int pi = (sg.tp * MT + mt) * BM + row;
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld32(tacc + mt * BN + c0, r);
+            float f[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
-        store_chunk(p, pi, q0 + c0, f);
+            for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+            store_chunk(p, pi, q0 + c0, f);
+          }
+        }
+      } else {
+        // deposit this partial, then the last of the tile's contributors sums and stores
+        constexpr int64_t SLOT = (int64_t)MT * BM * BN;
+        float* mine = p.ws + (int64_t)sg.slot * SLOT;
+#pragma unroll 1
+        for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld32(tacc + mt * BN + c0, r);
+            float4* dst = reinterpret_cast<float4*>(mine + (int64_t)(mt * BM + row) * BN + c0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                          __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+          }
+        }
+        __threadfence();
+        __syncwarp();
+        int* ctr = p.counters + (int64_t)sg.tile * 4 + q4;
+        int prev = 0;
+        if (lane == 0) prev = atomicAdd(ctr, 1);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        const int64_t x0 = (int64_t)sg.tile * p.num_kb;
+        const int cf = sk_owner(p, x0), cl = sk_owner(p, x0 + p.num_kb - 1);
+        if (prev == cl - cf) {
+          __threadfence();
+#pragma unroll 1
+          for (int mt = 0; mt < MT; ++mt) {
+            const int pi = (sg.tp * MT + mt) * BM + row;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+              uint32_t r[32];
+              tmem_ld32(tacc + mt * BN + c0, r);
+              float f[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+              for (int c = cf; c <= cl; ++c) {
+                if (c == (int)blockIdx.x) continue;
+                const int slot = c * 2 + (sk_start(p, c) < x0 ? 1 : 0);
+                const float4* src =
+                    reinterpret_cast<const float4*>(p.ws + (int64_t)slot * SLOT + (int64_t)(mt * BM + row) * BN + c0);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const float4 v = __ldcg(src + j);
+                  f[4 * j] += v.x;
+                  f[4 * j + 1] += v.y;
+                  f[4 * j + 2] += v.z;
+                  f[4 * j + 3] += v.w;
+                }
+              }
+              store_chunk(p, pi, q0 + c0, f);
+            }
+          }
+          if (lane == 0) *ctr = 0;  // every contributor has arrived: ready for the next launch
+        }
       }
       tc_fence_before();
       if (lane == 0) mbar_arrive(tempty(acc));
+      ++tile_it;
     }
   }
   tc_fence_before();
@@ -593,9 +731,9 @@ bool make_map(CUtensorMap* m, const void* base, int rows, int k, int64_t ld_elem
   return r == CUDA_SUCCESS;
 }
 
-template <int BN>
+template <int BN, int MT = 1>
 constexpr int stages_for() {
-  return (200 * 1024) / (BM * BK * 2 + BN * BK * 2) > 8 ? 8 : (200 * 1024) / (BM * BK * 2 + BN * BK * 2);
+  return (200 * 1024) / (MT * BM * BK * 2 + BN * BK * 2) > 8 ? 8 : (200 * 1024) / (MT * BM * BK * 2 + BN * BK * 2);
 }
 
 template <int BN>
@@ -626,11 +764,11 @@ cudaError_t run_cluster(const CUtensorMap& mp, const CUtensorMap& mq, const Para
   return cudaLaunchKernelEx(&cfg, kern, mp, mq, prm);
 }
 
-template <int BN>
+template <int BN, int MT = 1>
 cudaError_t run(const CUtensorMap& mp, const CUtensorMap& mq, const Params& prm, int grid, cudaStream_t stream) {
-  constexpr int STAGES = stages_for<BN>();
-  constexpr int SMEM = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
-  auto kern = gemm_kernel<BN, STAGES>;
+  constexpr int STAGES = stages_for<BN, MT>();
+  constexpr int SMEM = STAGES * (MT * BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+  auto kern = gemm_kernel<BN, STAGES, MT>;
   static bool configured = false;  // per template instance; the attribute is process-wide
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
@@ -692,7 +830,411 @@ int cluster_capacity(int bn, int splits) {
   }
 }
 
+// Decode-sized GEMM (m <= 256 tokens): every CTA holds ALL token rows (MT sub-tiles of
+// 128) against one BN-row slice of the weights, over one K slice; the `splits` K slices of
+// a weight slice run as one thread-block cluster and are summed through distributed
+// shared memory.  BN (any multiple of 16 up to 256) and splits are runtime values chosen
+// so that the clusters fill the GPU in one wave: the weights are then streamed exactly once.
+// Streaming the weights from HBM is latency-bound at these sizes, so they get their own
+// deep ring (most of shared memory) fed by warp 0, while the activations, which hit in L2,
+// get a shallow ring fed by warp 2 (before it turns to the epilogue).
+struct DecParams {
+  int m, n, k;           // C[m, n] = X[m, k] W[n, k]^T
+  int bn, splits, kb_per_split, num_kb;
+  int w_stages, a_stages;
+  uint32_t idesc;
+  __nv_bfloat16* c;
+  int64_t ldc;
+};
+
+template <int MT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_dec_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                    DecParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int A_BYTES = MT * BM * BK * 2;
+  const int BN = p.bn, SW = p.w_stages, SA = p.a_stages;
+  const int W_BYTES = BN * BK * 2;
+  const int XLD = BN + 4;  // export row stride in floats
+  uint8_t* a_ring = smem;                   // SA x A_BYTES
+  uint8_t* w_ring = smem + SA * A_BYTES;    // SW x W_BYTES (1024-aligned: BN % 16 == 0)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(w_ring + SW * W_BYTES);
+  // bars: wfull[SW], wempty[SW], afull[SA], aempty[SA], tfull, final
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * SW + 2 * SA + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * SW + 2 * SA + 3);
+  const uint32_t bar0 = smem_u32(bars);
+  auto wfull = [&](int s) { return bar0 + 8u * s; };
+  auto wempty = [&](int s) { return bar0 + 8u * (SW + s); };
+  auto afull = [&](int s) { return bar0 + 8u * (2 * SW + s); };
+  auto aempty = [&](int s) { return bar0 + 8u * (2 * SW + SA + s); };
+  const uint32_t tfull = bar0 + 8u * (2 * SW + 2 * SA);
+  const uint32_t final_bar = tfull + 8u;
+  float* xp = reinterpret_cast<float*>(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // columns read: MT * BN, plus 16 when the last 32-column load of a sub-tile overhangs it
+  uint32_t tmem_cols = 32;
+  while (tmem_cols < (uint32_t)(MT * BN + (BN % 32 ? 16 : 0))) tmem_cols <<= 1;
+
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const int split = (int)rank;
+  const int tq = blockIdx.x / p.splits;
+  const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+  const int nkb = kb1 > kb0 ? kb1 - kb0 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(wfull(s), 1);
+      mbar_init(wempty(s), 1);
+    }
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(afull(s), 1);
+      mbar_init(aempty(s), 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if ((warp == 0 || warp == 2) && lane == 0) {
+    // ------------------------------------------------ producers: warp 0 weights, warp 2 activations
+    const bool is_w = warp == 0;
+    const CUtensorMap* map = is_w ? &map_w : &map_x;
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+    const int S = is_w ? SW : SA;
+    const uint32_t bytes = is_w ? (uint32_t)W_BYTES : (uint32_t)A_BYTES;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int i = 0; i < nkb; ++i, ++it) {
+      const int kb = kb0 + i;
+      const int s = it % S;
+      const uint32_t round = it / S;
+      if (!mbar_wait(is_w ? wempty(s) : aempty(s), (round & 1) ^ 1, abort_flag, 8)) {
+        ok = false;
+        break;
+      }
+      const uint32_t fb = is_w ? wfull(s) : afull(s);
+      mbar_arrive_expect_tx(fb, bytes);
+      if (is_w) {
+        tma_load_2d(smem_u32(w_ring + s * W_BYTES), &map_w, fb, kb * BK, tq * BN);
+      } else {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+          tma_load_2d(smem_u32(a_ring + s * A_BYTES) + mt * (BM * BK * 2), &map_x, fb, kb * BK, mt * BM);
+      }
+    }
+    if (!ok) {
+      const uint32_t n = it < (uint32_t)S ? it : (uint32_t)S;
+      for (uint32_t j = it - n; j < it; ++j) mbar_drain(is_w ? wfull(j % S) : afull(j % S), (j / S) & 1);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------ MMA issuer
+    for (int i = 0; i < nkb; ++i) {
+      const int sw = i % SW, sa = i % SA;
+      if (!mbar_wait(wfull(sw), (i / SW) & 1, abort_flag, 9)) break;
+      if (!mbar_wait(afull(sa), (i / SA) & 1, abort_flag, 9)) break;
+      tc_fence_after();
+      const uint64_t wd = sdesc(smem_u32(w_ring + sw * W_BYTES));
+      const uint32_t ab = smem_u32(a_ring + sa * A_BYTES);
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+          tc_mma(tmem_base + mt * BN, sdesc(ab + mt * (BM * BK * 2)) + 2 * k, wd + 2 * k, p.idesc,
+                 (i > 0 || k > 0) ? 1u : 0u);
+      tc_commit(wempty(sw));
+      tc_commit(aempty(sa));
+    }
+    tc_commit(tfull);
+    tc_commit(final_bar);
+    mbar_drain(final_bar, 0);
+  }
+  __syncwarp();
+  bool acc_ok = true;
+  if (warp >= 2) {
+    acc_ok = mbar_wait(tfull, 0, abort_flag, 10);
+    tc_fence_after();
+  }
+  if (p.splits == 1) {
+    // whole K in this CTA: accumulator rows straight from TMEM to the output
+    if (warp >= 2 && acc_ok) {
+      const int q4 = warp & 3;
+      const int row = q4 * 32 + lane;
+#pragma unroll 1
+      for (int mt = 0; mt < MT; ++mt) {
+        const int pi = mt * BM + row;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + ((uint32_t)(q4 * 32) << 16) + mt * BN + c0, r);
+          const int qj = tq * BN + c0;
+          const int valid = min(min(32, BN - c0), p.n - qj);
+          if (pi >= p.m || valid <= 0) continue;
+          float f[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+          __nv_bfloat16* dst = p.c + (int64_t)pi * p.ldc + qj;
+          if (valid == 32) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = f32_to_bf16x8(f + j);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < valid) dst[j] = __float2bfloat16(f[j]);
+          }
+        }
+      }
+      tc_fence_before();
+    }
+    __syncthreads();
+  } else {
+    const uint32_t xbase = smem_u32(xp);
+    const int rows_per = (BM + p.splits - 1) / p.splits;
+    const int r0 = split * rows_per, r1 = min(BM, r0 + rows_per);
+    const int C4 = BN / 4;
+#pragma unroll 1
+    for (int mt = 0; mt < MT; ++mt) {
+      if (warp >= 2 && acc_ok) {
+        // export sub-tile mt: row-major [128][BN + 4] fp32 over the idle rings
+        const int q4 = warp & 3;
+        const int row = q4 * 32 + lane;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + ((uint32_t)(q4 * 32) << 16) + mt * BN + c0, r);
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            if (c0 + j < BN)
+              *reinterpret_cast<float4*>(xp + row * XLD + c0 + j) =
+                  make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                              __uint_as_float(r[j + 3]));
+        }
+      }
+      if (warp >= 2) tc_fence_before();
+      cluster_sync_all();  // every CTA's export of sub-tile mt is visible cluster-wide
+      // one row per warp at a time, lanes along the columns (coalesced DSMEM reads and
+      // stores); two rows in flight per warp
+#pragma unroll 1
+      for (int rr = r0 + warp; rr < r1; rr += 2 * (NUM_THREADS / 32)) {
+        const int rr2 = rr + NUM_THREADS / 32;
+        const bool has2 = rr2 < r1;
+        const int pi = mt * BM + rr, pi2 = mt * BM + rr2;
+        for (int c4 = lane; c4 < C4; c4 += 32) {
+          const int qj = tq * BN + c4 * 4;
+          const uint32_t off = xbase + (uint32_t)(rr * XLD + c4 * 4) * 4u;
+          const uint32_t off2 = xbase + (uint32_t)(rr2 * XLD + c4 * 4) * 4u;
+          float4 v[8], v2[8];
+#pragma unroll
+          for (int s2 = 0; s2 < 8; ++s2)
+            if (s2 < p.splits) {
+              v[s2] = ld_dsmem_f32x4(off, (uint32_t)s2);
+              if (has2) v2[s2] = ld_dsmem_f32x4(off2, (uint32_t)s2);
+            }
+          float f[4] = {0.f, 0.f, 0.f, 0.f}, g[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int s2 = 0; s2 < 8; ++s2)
+            if (s2 < p.splits) {
+              f[0] += v[s2].x;
+              f[1] += v[s2].y;
+              f[2] += v[s2].z;
+              f[3] += v[s2].w;
+              if (has2) {
+                g[0] += v2[s2].x;
+                g[1] += v2[s2].y;
+                g[2] += v2[s2].z;
+                g[3] += v2[s2].w;
+              }
+            }
+          if (qj >= p.n) continue;
+          const int nv = min(4, p.n - qj);
+          if (pi < p.m) {
+            if (nv == 4) *reinterpret_cast<uint2*>(p.c + (int64_t)pi * p.ldc + qj) = f32_to_bf16x4(f);
+            else
+              for (int e = 0; e < nv; ++e) p.c[(int64_t)pi * p.ldc + qj + e] = __float2bfloat16(f[e]);
+          }
+          if (has2 && pi2 < p.m) {
+            if (nv == 4) *reinterpret_cast<uint2*>(p.c + (int64_t)pi2 * p.ldc + qj) = f32_to_bf16x4(g);
+            else
+              for (int e = 0; e < nv; ++e) p.c[(int64_t)pi2 * p.ldc + qj + e] = __float2bfloat16(g[e]);
+          }
+        }
+      }
+      cluster_sync_all();  // peers may still be reading this CTA's export
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
+  }
+}
+
+constexpr int DEC_SMEM_MAX = 232448;  // opt-in dynamic shared memory per block on sm_100
+
+struct DecCfg {
+  int mt, bn, splits, kb_per_split, w_stages, a_stages, smem, tiles;
+  double cost;
+};
+
+template <int MT>
+int dec_capacity(int splits, int smem) {
+  // CTAs of `splits`-wide clusters of this shape that can be resident at once
+  static std::map<std::pair<int, int>, int> cache;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  auto key = std::make_pair(splits, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  auto kern = gemm_dec_kernel<MT>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM_MAX);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(splits * 64, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = num_sms() / splits;
+  }
+  cache[key] = n * splits;
+  return n * splits;
+}
+
+// All decode-kernel shapes for C[m, n] (m <= 256), cheapest first by a bytes-per-CTA model:
+// waves x (weight + activation bytes one CTA streams + its share of the reduction + a fixed
+// pipeline-fill cost).
+std::vector<DecCfg> dec_candidates(int m, int n, int k) {
+  std::vector<DecCfg> out;
+  if (m <= 0 || m > 2 * BM || k % BK) return out;
+  const int mt = m > BM ? 2 : 1;
+  const int num_kb = k / BK;
+  const int a_bytes = mt * BM * BK * 2;
+  for (int a_st : {3, 4}) {
+    for (int bn = 32; bn <= 256; bn += 16) {
+      const int w_bytes = bn * BK * 2;
+      const int fixed = 1024 + a_st * a_bytes + 512;
+      int w_st = (DEC_SMEM_MAX - fixed) / w_bytes;
+      if (w_st > 12) w_st = 12;
+      if (w_st < 2 || 512 * (bn + 4) > a_st * a_bytes + w_st * w_bytes) continue;
+      const int smem = fixed + w_st * w_bytes;
+      const int tiles = (n + bn - 1) / bn;
+      int prev = 0;
+      for (int sp = 1; sp <= 8; ++sp) {
+        const int kbs = (num_kb + sp - 1) / sp;
+        const int s_eff = (num_kb + kbs - 1) / kbs;
+        if (s_eff == prev) continue;
+        prev = s_eff;
+        const int cap = mt == 2 ? dec_capacity<2>(s_eff, smem) : dec_capacity<1>(s_eff, smem);
+        const int units = tiles * s_eff;
+        const int waves = (units + cap - 1) / (cap > 0 ? cap : 1);
+        // time ~ waves x (weight bytes of one CTA / bytes it keeps in flight) x latency, plus
+        // the reduction and a fixed start-up cost, in units of one latency
+        const double w_cta = (double)kbs * w_bytes;
+        const double inflight = (double)(w_st < kbs ? w_st : kbs) * w_bytes;
+        const double red = s_eff > 1 ? 0.5 * mt * BM * bn * 4 / 65536.0 : 0.0;
+        DecCfg c{mt, bn, s_eff, kbs, w_st, a_st, smem, tiles, waves * (w_cta / inflight + red + 2.0)};
+        out.push_back(c);
+      }
+    }
+  }
+  std::sort(out.begin(), out.end(), [](const DecCfg& a, const DecCfg& b) { return a.cost < b.cost; });
+  return out;
+}
+
+cudaError_t run_dec(const DecCfg& d, const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc,
+                    int m, int n, int k, cudaStream_t stream) {
+  CUtensorMap mx, mw;
+  if (!make_map(&mx, x, m, k, ldx, BM) || !make_map(&mw, w, n, k, ldw, d.bn)) return cudaErrorInvalidValue;
+  DecParams p;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.bn = d.bn;
+  p.splits = d.splits;
+  p.kb_per_split = d.kb_per_split;
+  p.num_kb = k / BK;
+  p.w_stages = d.w_stages;
+  p.a_stages = d.a_stages;
+  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(d.bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  p.c = static_cast<__nv_bfloat16*>(c);
+  p.ldc = ldc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(d.tiles * d.splits, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = d.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = d.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static bool configured[3] = {false, false, false};
+  if (d.mt == 2) {
+    if (!configured[2]) {
+      cudaError_t e = cudaFuncSetAttribute(gemm_dec_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM_MAX);
+      if (e != cudaSuccess) return e;
+      configured[2] = true;
+    }
+    return cudaLaunchKernelEx(&cfg, gemm_dec_kernel<2>, mx, mw, p);
+  }
+  if (!configured[1]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_dec_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM_MAX);
+    if (e != cudaSuccess) return e;
+    configured[1] = true;
+  }
+  return cudaLaunchKernelEx(&cfg, gemm_dec_kernel<1>, mx, mw, p);
+}
+
 }  // namespace
+
+cudaError_t gemm_dec_explicit(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m,
+                              int n, int k, int bn, int splits, int a_stages, cudaStream_t stream) {
+  for (const auto& d : dec_candidates(m, n, k))
+    if (d.bn == bn && d.splits == splits && d.a_stages == a_stages)
+      return run_dec(d, x, ldx, w, ldw, c, ldc, m, n, k, stream);
+  return cudaErrorInvalidValue;
+}
+
+bool gemm_dec_plan(int m, int n, int k, int rank, GemmPlan* plan) {
+  const auto cands = dec_candidates(m, n, k);
+  if (rank < 0 || rank >= (int)cands.size()) return false;
+  const DecCfg& d = cands[rank];
+  GemmPlan pl{};
+  pl.dec = 1;
+  pl.mt = d.mt;
+  pl.bn = d.bn;
+  pl.splits = d.splits;
+  pl.kb_per_split = d.kb_per_split;
+  pl.num_kb = k / BK;
+  pl.stages = d.w_stages;
+  pl.a_stages = d.a_stages;
+  pl.smem = d.smem;
+  pl.tiles = d.tiles;
+  pl.tiles_p = 1;
+  pl.tiles_q = d.tiles;
+  pl.grid = d.tiles * d.splits;
+  *plan = pl;
+  return true;
+}
 
 GemmPlan gemm_plan(int m, int n, int k, int force_swap, int force_bn, int force_splits) {
   GemmPlan pl{};
@@ -715,6 +1257,24 @@ GemmPlan gemm_plan(int m, int n, int k, int force_swap, int force_bn, int force_
       while (bn > 128 && (int64_t)((p_rows + BM - 1) / BM) * ((q_rows + bn - 1) / bn) < (sms * 9) / 10) bn >>= 1;
   }
   pl.bn = bn;
+  pl.mt = 1;
+  pl.streamk = 0;
+  if (force_splits < 0) {
+    // stream-K over tiles of (128 * mt) x bn
+    pl.mt = -force_splits > 1 ? 2 : 1;
+    pl.streamk = 1;
+    pl.tiles_p = (p_rows + BM * pl.mt - 1) / (BM * pl.mt);
+    pl.tiles_q = (q_rows + bn - 1) / bn;
+    pl.tiles = pl.tiles_p * pl.tiles_q;
+    pl.splits = 1;
+    pl.kb_per_split = pl.num_kb;
+    const int64_t iters = (int64_t)pl.tiles * pl.num_kb;
+    pl.grid = iters < sms ? (int)iters : sms;
+    pl.ws_ld = bn;
+    pl.ws_elems = (int64_t)pl.grid * 2 * pl.mt * BM * bn;
+    pl.prefetch_w = (pl.swap ? pl.tiles_q : pl.tiles_p) <= 2;
+    return pl;
+  }
   pl.tiles_p = (p_rows + BM - 1) / BM;
   pl.tiles_q = (q_rows + bn - 1) / bn;
   const int tiles = pl.tiles_p * pl.tiles_q;
@@ -759,6 +1319,11 @@ cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, vo
   if (k % 8 || ldx % 8 || ldw % 8) return cudaErrorInvalidValue;
   if (((uintptr_t)x & 15) || ((uintptr_t)w & 15)) return cudaErrorMisalignedAddress;
   if (!pl.swap && (ldc % 8 || ((uintptr_t)c & 15))) return cudaErrorInvalidValue;
+  if (pl.dec) {
+    if (m > pl.mt * BM || k % BK) return cudaErrorInvalidValue;
+    DecCfg d{pl.mt, pl.bn, pl.splits, pl.kb_per_split, pl.stages, pl.a_stages, pl.smem, pl.tiles, 0.0};
+    return run_dec(d, x, ldx, w, ldw, c, ldc, m, n, k, stream);
+  }
   const void* pbase = pl.swap ? w : x;
   const void* qbase = pl.swap ? x : w;
   const int64_t pld = pl.swap ? ldw : ldx, qld = pl.swap ? ldx : ldw;
@@ -783,9 +1348,25 @@ cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, vo
   prm.ws = ws;
   prm.ws_ld = pl.ws_ld;
   prm.counters = counters;
-  (void)ws;
-  (void)counters;
+  prm.streamk = pl.streamk;
+  prm.sk_iters = (int64_t)pl.tiles * pl.num_kb;
   cudaError_t e;
+  if (pl.streamk) {
+    if (!ws || !counters) return cudaErrorInvalidValue;
+    if (pl.mt == 2) {
+      switch (pl.bn) {
+        case 128: return run<128, 2>(mp, mq, prm, pl.grid, stream);
+        case 256: return run<256, 2>(mp, mq, prm, pl.grid, stream);
+        default: return cudaErrorInvalidValue;
+      }
+    }
+    switch (pl.bn) {
+      case 64: return run<64>(mp, mq, prm, pl.grid, stream);
+      case 128: return run<128>(mp, mq, prm, pl.grid, stream);
+      case 256: return run<256>(mp, mq, prm, pl.grid, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   if (pl.splits > 1) {
     switch (pl.bn) {
       case 32: return run_cluster<32>(mp, mq, prm, stream);
@@ -809,6 +1390,18 @@ cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, vo
 // Key: (m bucket, n, k).  m <= 256 is keyed exactly (decode batch buckets); larger m
 // by multiples of 512.
 namespace {
+// Reads a buffer larger than L2 so that the next launch finds its operands in HBM and L2
+// holds only clean lines (a write would leave dirty lines whose write-back the timed
+// launch would pay for).
+__global__ void l2_evict_kernel(const uint4* __restrict__ p, size_t n, int* __restrict__ sink) {
+  uint32_t acc = 0;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const uint4 v = p[i];
+    acc ^= v.x ^ v.y ^ v.z ^ v.w;
+  }
+  if (acc == 0x9E3779B9u) *sink = (int)acc;  // keeps the loads; the value is irrelevant
+}
+
 std::map<std::tuple<int, int, int>, GemmPlan>& tune_cache() {
   static std::map<std::tuple<int, int, int>, GemmPlan> c;
   return c;
@@ -821,7 +1414,8 @@ int m_bucket(int m) { return m <= 256 ? m : ((m + 511) / 512) * 512; }
 }  // namespace
 
 cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n,
-                            int k, cudaStream_t stream, GemmPlan* chosen) {
+                            int k, float* ws, int64_t ws_elems, int* counters, int64_t num_counters,
+                            cudaStream_t stream, GemmPlan* chosen) {
   if (m == 0 || n == 0) return cudaSuccess;
   const auto key = std::make_tuple(m_bucket(m), n, k);
   {
@@ -829,7 +1423,7 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
     auto it = tune_cache().find(key);
     if (it != tune_cache().end()) {
       if (chosen) *chosen = it->second;
-      return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, it->second, nullptr, nullptr, stream);
+      return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, it->second, ws, counters, stream);
     }
   }
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
@@ -837,7 +1431,7 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
   GemmPlan best = gemm_plan(m, n, k, -1, 0, 0);
   if (cap != cudaStreamCaptureStatusNone) {  // cannot time inside a capture
     if (chosen) *chosen = best;
-    return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, best, nullptr, nullptr, stream);
+    return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, best, ws, counters, stream);
   }
   std::vector<GemmPlan> cands;
   cands.push_back(best);
@@ -847,35 +1441,63 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
     const int bq = m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256;
     for (int sp : {1, 2, 3, 4}) cands.push_back(gemm_plan(m, n, k, 1, bq, sp));
   }
+  if (m <= 2 * BM && k % BK == 0) {
+    GemmPlan d;
+    for (int r = 0; r < 8 && gemm_dec_plan(m, n, k, r, &d); ++r) cands.push_back(d);
+  }
+  if (ws && counters) {
+    for (int bn : {256, 128}) {
+      cands.push_back(gemm_plan(m, n, k, 0, bn, -1));
+      if (m > BM) cands.push_back(gemm_plan(m, n, k, 0, bn, -2));
+    }
+  }
+  // Each candidate is timed on a cold L2 (the weights of a real forward pass are not
+  // resident when their layer runs): a 256 MiB read precedes every timed launch.
+  const size_t flush_bytes = (size_t)256 << 20;
+  void* flush = nullptr;
+  if (cudaMalloc(&flush, flush_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    flush = nullptr;
+  }
   cudaEvent_t e0, e1;
   cudaEventCreate(&e0);
   cudaEventCreate(&e1);
   float best_ms = 1e30f;
   for (const auto& pl : cands) {
     if (pl.splits > 1 && pl.splits > 8) continue;
-    if (gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, pl, nullptr, nullptr, stream) != cudaSuccess) {
+    if (pl.streamk && (pl.ws_elems > ws_elems || 4 * (int64_t)pl.tiles > num_counters)) continue;
+    if (gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, pl, ws, counters, stream) != cudaSuccess) {
       cudaGetLastError();
       continue;
     }
-    cudaEventRecord(e0, stream);
-    for (int r = 0; r < 3; ++r) gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, pl, nullptr, nullptr, stream);
-    cudaEventRecord(e1, stream);
-    cudaEventSynchronize(e1);
-    float ms = 0.f;
-    cudaEventElapsedTime(&ms, e0, e1);
-    if (ms < best_ms) {
-      best_ms = ms;
+    float total = 0.f;
+    bool good = true;
+    for (int r = 0; r < 3 && good; ++r) {
+      if (flush)
+        l2_evict_kernel<<<num_sms() * 4, 256, 0, stream>>>(static_cast<const uint4*>(flush), flush_bytes / 16 - 16,
+                                                          static_cast<int*>(flush) + (flush_bytes / 4 - 1));
+      cudaEventRecord(e0, stream);
+      good = gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, pl, ws, counters, stream) == cudaSuccess;
+      cudaEventRecord(e1, stream);
+      cudaEventSynchronize(e1);
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, e0, e1);
+      total += ms;
+    }
+    if (good && total < best_ms) {
+      best_ms = total;
       best = pl;
     }
   }
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
+  if (flush) cudaFree(flush);
   {
     std::lock_guard<std::mutex> g(tune_mutex());
     tune_cache()[key] = best;
   }
   if (chosen) *chosen = best;
-  return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, best, nullptr, nullptr, stream);
+  return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, best, ws, counters, stream);
 }
 
 int gemm_error_code(int reset) {

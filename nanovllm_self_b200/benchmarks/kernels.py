@@ -3,11 +3,13 @@
 ``python -m nanovllm_self_b200.benchmarks.kernels <case> [--mode time|profile] [--iters N]``
 
 ``--mode time`` (default) runs 3 warm-up launches, then ``--iters`` launches, each after a
-write of a 256 MiB buffer (> the 126 MB L2) so that every timed launch reads from HBM, and
+read of a 256 MiB buffer (> the 126 MB L2; a read leaves no dirty lines whose write-back
+the timed launch would pay for) so that every timed launch reads from HBM, and
 prints one JSON line: the median device time, the algorithmic bytes or FLOPs of one launch
 and their fraction of the peaks in ``MEASURED_PEAKS.json`` (repository root) when present.
-``--mode profile`` launches the kernel three times and exits: the small workload a
-profiler capture of one launch (``-s 1 -c 1``) needs.
+``--mode profile`` runs one untimed launch (which also autotunes the GEMM cases), then
+three launches between ``cudaProfilerStart``/``cudaProfilerStop`` and exits: the small
+workload a profiler capture of one launch needs (``ncu --profile-from-start off -c 1``).
 
 Shapes are Qwen3-8B's (32 query heads, 8 KV heads, head dim 128, hidden 4096,
 intermediate 12288, vocab 151936); every case holds well under 2 GB on the device.
@@ -122,13 +124,13 @@ def _peaks():
 def time_case(name: str, iters: int = 20) -> dict:
     ops = CudaOps()
     launch, nbytes, flops = build_case(name, ops)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
     for _ in range(3):
         launch()
     torch.cuda.synchronize()
     times = []
     for _ in range(iters):
-        flush.fill_(1)
+        flush.sum()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         launch()
@@ -137,8 +139,10 @@ def time_case(name: str, iters: int = 20) -> dict:
         times.append(e0.elapsed_time(e1) * 1e3)
     us = statistics.median(times)
     hbm, tfl, src = _peaks()
-    out = {"case": name, "us": round(us, 2), "iters": iters, "l2": "256 MiB write before each launch",
+    out = {"case": name, "us": round(us, 2), "iters": iters, "l2": "256 MiB read before each launch",
            "peaks": src}
+    if name.startswith("gemm"):
+        out["plan"] = dict(zip(("swap", "bn", "tiles_p", "tiles_q", "splits", "grid"), ops.last_plan))
     if nbytes:
         out["gb_s"] = round(nbytes / us / 1e3, 1)
         out["frac_hbm"] = round(nbytes / us / 1e3 / hbm, 3)
@@ -158,9 +162,13 @@ def main(argv=None):
     for n in names:
         if a.mode == "profile":
             launch = build_case(n, CudaOps())[0]
+            launch()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
             for _ in range(3):
                 launch()
             torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
             print(json.dumps({"case": n, "profiled_launches": 3}), flush=True)
         else:
             print(json.dumps(time_case(n, a.iters)), flush=True)

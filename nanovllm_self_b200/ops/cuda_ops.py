@@ -11,7 +11,7 @@ import torch
 from . import torch_ref as R
 from ._ext import load
 
-_GEMM_WS_ELEMS = 16 << 20        # fp32 split-K scratch (64 MiB)
+_GEMM_WS_ELEMS = 24 << 20        # fp32 stream-K partial tiles (96 MiB: 2 per CTA of up to 256 x 256)
 _GEMM_COUNTERS = 1 << 16         # split-K arrival counters (4 per output tile)
 _ATTN_PART_ROWS = 1 << 16        # (seq, q head, split) rows of split-KV scratch
 _SAMPLE_PART = 1 << 16
@@ -37,6 +37,7 @@ class CudaOps:
         # Number of kernels this op set has launched (graph replays are added by the runner).
         self.launches = 0
         self._plans: dict = {}
+        self.last_plan = None
 
     def scratch(self, device) -> _Scratch:
         key = torch.device(device).index
@@ -87,7 +88,8 @@ class CudaOps:
             out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
         if x.shape[0] == 0:
             return out
-        self.C.linear_tuned(x, w, out)
+        sc = self.scratch(x.device)
+        self.last_plan = self.C.linear_tuned(x, w, out, sc.gemm, sc.gemm_counters)
         self.launches += 1
         return out
 

@@ -204,3 +204,49 @@ def test_gemm_forced_configs(ops, swap, bn, splits):
     ops.C.linear(x, w, out, sc.gemm, sc.gemm_counters, swap, bn, splits)
     assert int(sc.gemm_counters.abs().sum()) == 0  # the fix-up leaves the counters at zero
     _close(out, x.float() @ w.float().t(), 0.05, 0.02)
+
+
+@pytest.mark.parametrize("m,n,k,bn,mt", [
+    (200, 1280, 2048, 256, 2), (200, 1280, 2048, 128, 1), (256, 24576, 1024, 256, 2), (64, 6144, 4096, 256, 1),
+    (300, 4096, 12288, 128, 2), (17, 1024, 512, 64, 1),
+])
+def test_gemm_streamk(ops, m, n, k, bn, mt):
+    # stream-K: every CTA takes an equal share of the (tile, k-block) iterations; tiles split
+    # across CTAs are summed by their last contributor.  Two launches: the counters must be
+    # back at zero after each.
+    g = torch.Generator(device=DEV).manual_seed(m + n + k)
+    x = torch.randn(m, k, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(n, k, device=DEV, generator=g) * 0.05).bfloat16()
+    out = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+    sc = ops.scratch(x.device)
+    ref = x.float() @ w.float().t()
+    for _ in range(2):
+        out.fill_(0)
+        ops.C.linear(x, w, out, sc.gemm, sc.gemm_counters, 0, bn, -mt)
+        assert int(sc.gemm_counters.abs().sum()) == 0
+        _close(out, ref, 0.05 * math.sqrt(k / 2048), 0.02)
+    assert ops.C.gemm_error(True) == 0
+
+
+
+@pytest.mark.parametrize("m,n,k", [
+    (1, 1280, 1024), (7, 6144, 4096), (64, 4096, 4096), (128, 1000, 2048), (129, 24576, 1024), (200, 4096, 12288),
+    (256, 6144, 4096),
+])
+def test_gemm_decode_kernel(ops, m, n, k):
+    # all tokens in one CTA tile, runtime tile width, K split over a cluster: the four
+    # cheapest configurations of the cost model, each checked against fp32
+    g = torch.Generator(device=DEV).manual_seed(m * 3 + n + k)
+    x = torch.randn(m, k, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(n, k, device=DEV, generator=g) * 0.05).bfloat16()
+    ref = x.float() @ w.float().t()
+    seen = 0
+    for rank in range(4):
+        out = torch.zeros(m, n, device=DEV, dtype=torch.bfloat16)
+        cfg = ops.C.linear_dec(x, w, out, rank)
+        if not cfg:
+            break
+        seen += 1
+        _close(out, ref, 0.05 * math.sqrt(k / 2048), 0.02)
+    assert seen > 0
+    assert ops.C.gemm_error(True) == 0
