@@ -190,6 +190,7 @@ template <bool FP8>
 __global__ void __launch_bounds__(160, 2)
     attn_decode_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                            DecodeArgs da) {
+  pdl_trigger();  // the next kernel may start its prologue
   const AttnArgs& a = da.a;
   extern __shared__ __align__(1024) uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
@@ -539,6 +540,7 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
 __global__ void __launch_bounds__(160, 3)
     attn_decode_fp8_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                            DecodeArgs da) {
+  pdl_trigger();  // the next kernel may start its prologue
   const AttnArgs& a = da.a;
   extern __shared__ __align__(1024) uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
@@ -802,6 +804,7 @@ __global__ void __launch_bounds__(160, 3)
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                     const int* __restrict__ cu_q, __nv_bfloat16* __restrict__ out, int nq, int splits,
                                     int seq_offset) {
+  pdl_trigger();  // the next kernel may start its prologue
   const int bh = blockIdx.x;
   const int b = bh / nq + seq_offset, hq = bh % nq;
   const int64_t base = ((int64_t)b * nq + hq) * splits;
@@ -821,6 +824,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
 // ------------------------------------------------------------------------ prefill
 template <bool FP8>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
+  pdl_trigger();  // the next kernel may start its prologue
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sq = smem;                      // 64 x 256 B
   uint8_t* sk = smem + KTILE * ROWB;       // 2 x 64 x 256

@@ -72,6 +72,7 @@ __device__ bool cta_barrier(const CommArgs& a, int phase, int b, uint32_t epoch)
 
 template <int NI>
 __global__ void __launch_bounds__(256) allreduce_add_rmsnorm_kernel(CommArgs a) {
+  pdl_trigger();  // the next kernel may start its prologue
   const int b = blockIdx.x;
   __shared__ uint32_t s_epoch;
   __shared__ int s_ok;
@@ -166,6 +167,7 @@ __global__ void __launch_bounds__(256) allreduce_add_rmsnorm_kernel(CommArgs a) 
 // reach the barrier of call k+1 after every rank finished reading call k's buffer.
 template <int NI>
 __global__ void __launch_bounds__(256) allreduce_oneshot_kernel(CommArgs a) {
+  pdl_trigger();  // the next kernel may start its prologue
   const int b = blockIdx.x;
   __shared__ uint32_t s_epoch;
   __shared__ int s_ok;

@@ -73,6 +73,14 @@ __device__ __forceinline__ void e4m3x4_to_f32(uint32_t v, float* f) {
   f[0] = x.x; f[1] = x.y; f[2] = y.x; f[3] = y.y;
 }
 
+// Programmatic dependent launch.  pdl_trigger(): this CTA no longer holds back the launch
+// of the next kernel in the stream (when every CTA has triggered or exited, a kernel
+// launched with the programmatic-serialization attribute may start); pdl_wait(): block
+// until the previous kernel in the stream has completed and its writes are visible (a
+// no-op when this kernel was not launched as a programmatic dependent).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -36,15 +36,19 @@ cudaError_t gemm_dec_explicit(const void* x, int64_t ldx, const void* w, int64_t
 
 // ws: fp32 split-K scratch (plan.ws_elems); counters: 4 int32 per output tile, all zero
 // before the first launch (the kernel leaves them zero).
+// act = 1: fused SiLU-and-mul epilogue.  W's rows are gate/up interleaved in groups of 16
+// (rows 32j..32j+15 gate features 16j..16j+15, rows 32j+16..32j+31 the matching up
+// features) and C receives silu(gate) * up: [m, n / 2] with row stride ldc.  Needs n % 32
+// == 0, the normal orientation and a tile width that is a multiple of 32.
 cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n, int k,
-                      const GemmPlan& plan, float* ws, int* counters, cudaStream_t stream);
+                      const GemmPlan& plan, float* ws, int* counters, cudaStream_t stream, int act = 0);
 
 // Same product, configuration chosen by timing candidates on first use of a shape (outside
 // stream capture) and cached; inside a capture the cached or heuristic plan is used.
 // ws / ws_elems / counters / num_counters: scratch for stream-K candidates (may be null).
 cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n,
                             int k, float* ws, int64_t ws_elems, int* counters, int64_t num_counters,
-                            cudaStream_t stream, GemmPlan* chosen);
+                            cudaStream_t stream, GemmPlan* chosen, int act = 0);
 
 // Error word written by a GEMM that gave up on a bounded wait (0 = none).
 int gemm_error_code(int reset);

@@ -9,14 +9,15 @@ namespace {
 
 // out[m, n] = x[m, k] @ w[n, k]^T   (bf16 in/out, fp32 accumulation)
 void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c10::optional<at::Tensor>& ws,
-            const c10::optional<at::Tensor>& counters, int64_t force_swap, int64_t force_bn, int64_t force_splits) {
+            const c10::optional<at::Tensor>& counters, int64_t force_swap, int64_t force_bn, int64_t force_splits,
+            int64_t act) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
                   out.scalar_type() == at::kBFloat16, "bf16 required");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "2-D tensors required");
   TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "unit inner stride required");
   const int m = (int)x.size(0), k = (int)x.size(1), n = (int)w.size(0);
-  TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == n, "shape mismatch");
+  TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == (act ? n / 2 : n), "shape mismatch");
   auto pl = nvb::gemm_plan(m, n, k, (int)force_swap, (int)force_bn, (int)force_splits);
   float* wsp = nullptr;
   int* ctr = nullptr;
@@ -30,20 +31,21 @@ void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c10
   }
   at::cuda::CUDAGuard g(x.device());
   cudaError_t e = nvb::gemm_bf16(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0),
-                                 m, n, k, pl, wsp, ctr, at::cuda::getCurrentCUDAStream().stream());
+                                 m, n, k, pl, wsp, ctr, at::cuda::getCurrentCUDAStream().stream(), (int)act);
   TORCH_CHECK(e == cudaSuccess, "gemm_bf16 failed: ", cudaGetErrorString(e));
 }
 
 // Autotuned entry point used by the model (see gemm_bf16_tuned).
 std::vector<int64_t> linear_tuned(const at::Tensor& x, const at::Tensor& w, at::Tensor& out,
-                                  const c10::optional<at::Tensor>& ws, const c10::optional<at::Tensor>& counters) {
+                                  const c10::optional<at::Tensor>& ws, const c10::optional<at::Tensor>& counters,
+                                  int64_t act) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
                   out.scalar_type() == at::kBFloat16, "bf16 required");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "2-D tensors required");
   TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "unit inner stride required");
   const int m = (int)x.size(0), k = (int)x.size(1), n = (int)w.size(0);
-  TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == n, "shape mismatch");
+  TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == (act ? n / 2 : n), "shape mismatch");
   at::cuda::CUDAGuard g(x.device());
   float* wsp = nullptr;
   int* ctr = nullptr;
@@ -58,7 +60,7 @@ std::vector<int64_t> linear_tuned(const at::Tensor& x, const at::Tensor& w, at::
   nvb::GemmPlan pl{};
   cudaError_t e = nvb::gemm_bf16_tuned(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(),
                                        out.stride(0), m, n, k, wsp, ws_n, ctr, ctr_n,
-                                       at::cuda::getCurrentCUDAStream().stream(), &pl);
+                                       at::cuda::getCurrentCUDAStream().stream(), &pl, (int)act);
   TORCH_CHECK(e == cudaSuccess, "gemm_bf16 failed: ", cudaGetErrorString(e));
   // (swap, bn, tiles_p, tiles_q, splits, grid); splits < 0: stream-K with -splits sub-tiles;
   // splits >= 100: decode kernel with splits - 100 K slices
@@ -74,18 +76,20 @@ std::vector<int64_t> plan(int64_t m, int64_t n, int64_t k, int64_t force_swap, i
 
 // Decode kernel with the rank-th cheapest configuration of the cost model; returns
 // (mt, bn, splits, weight stages, activation stages), empty if there is no such configuration.
-std::vector<int64_t> linear_dec(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, int64_t rank) {
+std::vector<int64_t> linear_dec(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, int64_t rank,
+                                int64_t act) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
                   out.scalar_type() == at::kBFloat16, "bf16 required");
   TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "unit inner stride required");
   const int m = (int)x.size(0), k = (int)x.size(1), n = (int)w.size(0);
-  TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == n, "shape mismatch");
+  TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == (act ? n / 2 : n), "shape mismatch");
   nvb::GemmPlan pl{};
   if (!nvb::gemm_dec_plan(m, n, k, (int)rank, &pl)) return {};
+  if (act && pl.bn % 32) return {0};
   at::cuda::CUDAGuard g(x.device());
   cudaError_t e = nvb::gemm_bf16(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0),
-                                 m, n, k, pl, nullptr, nullptr, at::cuda::getCurrentCUDAStream().stream());
+                                 m, n, k, pl, nullptr, nullptr, at::cuda::getCurrentCUDAStream().stream(), (int)act);
   TORCH_CHECK(e == cudaSuccess, "gemm_bf16 failed: ", cudaGetErrorString(e));
   return {pl.mt, pl.bn, pl.splits, pl.stages, pl.a_stages};
 }
@@ -114,13 +118,14 @@ void register_gemm(pybind11::module& m) {
   m.def("linear", &linear, "tcgen05 GEMM out = x @ w^T", pybind11::arg("x"), pybind11::arg("w"),
         pybind11::arg("out"), pybind11::arg("ws") = c10::nullopt, pybind11::arg("counters") = c10::nullopt,
         pybind11::arg("force_swap") = -1,
-        pybind11::arg("force_bn") = 0, pybind11::arg("force_splits") = 0);
+        pybind11::arg("force_bn") = 0, pybind11::arg("force_splits") = 0, pybind11::arg("act") = 0);
   m.def("gemm_plan", &plan, pybind11::arg("m"), pybind11::arg("n"), pybind11::arg("k"),
         pybind11::arg("force_swap") = -1, pybind11::arg("force_bn") = 0, pybind11::arg("force_splits") = 0);
   m.def("linear_tuned", &linear_tuned, "autotuned tcgen05 GEMM out = x @ w^T", pybind11::arg("x"),
         pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("ws") = c10::nullopt,
-        pybind11::arg("counters") = c10::nullopt);
-  m.def("linear_dec", &linear_dec, "decode-sized tcgen05 GEMM with a ranked configuration");
+        pybind11::arg("counters") = c10::nullopt, pybind11::arg("act") = 0);
+  m.def("linear_dec", &linear_dec, "decode-sized tcgen05 GEMM with a ranked configuration", pybind11::arg("x"),
+        pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("rank"), pybind11::arg("act") = 0);
   m.def("linear_dec_cfg", &linear_dec_cfg, "decode-sized tcgen05 GEMM with an explicit configuration");
   m.def("gemm_error", &error_code, pybind11::arg("reset") = false);
 }

@@ -176,7 +176,21 @@ struct Params {
   int* counters;             // split-K arrival counters, 4 per tile (zero between launches)
   int streamk;               // 1: stream-K split of tiles x k-blocks over the grid
   int64_t sk_iters;          // stream-K: tiles * num_kb
+  int act;                   // 1: SiLU-and-mul epilogue (see act_silu_store)
 };
+
+// Fused SiLU-and-mul epilogue.  The weight rows of a gate/up projection are interleaved
+// in groups of 16 (rows 32j..32j+15 = gate features 16j.., rows 32j+16..32j+31 = the
+// matching up features), so every 32-column accumulator chunk that starts at a multiple
+// of 32 holds 16 gates and their 16 ups: out[16j + i] = silu(g_i) * u_i.
+__device__ __forceinline__ float silu_f(float g) { return g / (1.f + expf(-g)); }
+__device__ __forceinline__ void act_silu_store(__nv_bfloat16* dst, const float* f) {
+  float o[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i] = silu_f(f[i]) * f[16 + i];
+  *reinterpret_cast<uint4*>(dst) = f32_to_bf16x8(o);
+  *reinterpret_cast<uint4*>(dst + 8) = f32_to_bf16x8(o + 8);
+}
 
 __device__ __forceinline__ void unit_coords(const Params& p, int unit, int& tp, int& tq, int& split) {
   const int tiles = p.tiles_p * p.tiles_q;
@@ -196,6 +210,10 @@ __device__ __forceinline__ void unit_coords(const Params& p, int unit, int& tp, 
 // Store 32 accumulator columns [qc, qc + 32) of accumulator row pi as bf16.
 __device__ __forceinline__ void store_chunk(const Params& p, int pi, int qc, const float* f) {
   if (pi >= p.p_rows) return;
+  if (p.act) {  // normal orientation only; q_rows % 32 == 0
+    if (qc < p.q_rows) act_silu_store(p.c + (int64_t)pi * p.ldc + qc / 2, f);
+    return;
+  }
   if (!p.swap) {
     __nv_bfloat16* dst = p.c + (int64_t)pi * p.ldc + qc;
     const int valid = p.q_rows - qc;
@@ -321,6 +339,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // inputs and the output may belong to the previous kernel in the stream
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -581,6 +600,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // inputs and the output may belong to the previous kernel in the stream
 
   if (warp == 0) {
     if (lane == 0) {
@@ -662,9 +682,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr int C4 = BN / 4;
   const int total = nrows > 0 ? nrows * C4 : 0;
   const uint32_t xbase = smem_u32(xp);
+  if (p.act && BN >= 32) {
+    // 4 output features per item: gates at column g..g+3 of a 32-column group, ups at g+16
+    constexpr int O4 = BN / 8;
+    for (int idx = threadIdx.x; idx < nrows * O4; idx += NUM_THREADS) {
+      const int row = r0 + idx / O4, o4 = idx % O4;
+      const int gc = 32 * (o4 >> 2) + 4 * (o4 & 3);
+      const int pi = tp * BM + row, qg = tq * BN + gc;
+      if (pi >= p.p_rows || qg >= p.q_rows) continue;
+      const uint32_t offg = xbase + (uint32_t)(row * XLD + gc) * 4u, offu = offg + 64u;
+      float4 vg[8], vu[8];
+#pragma unroll
+      for (int s2 = 0; s2 < 8; ++s2)
+        if (s2 < p.splits) {
+          vg[s2] = ld_dsmem_f32x4(offg, (uint32_t)s2);
+          vu[s2] = ld_dsmem_f32x4(offu, (uint32_t)s2);
+        }
+      float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s2 = 0; s2 < 8; ++s2)
+        if (s2 < p.splits) {
+          g[0] += vg[s2].x; g[1] += vg[s2].y; g[2] += vg[s2].z; g[3] += vg[s2].w;
+          u[0] += vu[s2].x; u[1] += vu[s2].y; u[2] += vu[s2].z; u[3] += vu[s2].w;
+        }
+      const float o[4] = {silu_f(g[0]) * u[0], silu_f(g[1]) * u[1], silu_f(g[2]) * u[2], silu_f(g[3]) * u[3]};
+      const int oc = (tq * BN + 32 * (o4 >> 2)) / 2 + 4 * (o4 & 3);
+      *reinterpret_cast<uint2*>(p.c + (int64_t)pi * p.ldc + oc) = f32_to_bf16x4(o);
+    }
+  }
   // Each item is 4 consecutive columns of one row; all peers' float4 loads for an item
   // are issued before they are summed.
-  for (int idx = threadIdx.x; idx < total; idx += NUM_THREADS) {
+  for (int idx = p.act ? total : threadIdx.x; idx < total; idx += NUM_THREADS) {
     int row, c4;
     if (p.swap) {  // consecutive threads -> consecutive features (output-contiguous)
       c4 = idx / nrows;
@@ -754,13 +802,15 @@ cudaError_t run_cluster(const CUtensorMap& mp, const CUtensorMap& mq, const Para
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = prm.splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, mp, mq, prm);
 }
 
@@ -775,8 +825,17 @@ cudaError_t run(const CUtensorMap& mp, const CUtensorMap& mq, const Params& prm,
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  kern<<<grid, NUM_THREADS, SMEM, stream>>>(mp, mq, prm);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, mp, mq, prm);
 }
 
 int num_sms() {
@@ -805,13 +864,15 @@ int max_active_clusters(int splits) {
   cfg.gridDim = dim3(splits * 64, 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = SMEM;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 1;  // occupancy query: the cluster shape only
   int n = 0;
   if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
     cudaGetLastError();
@@ -842,6 +903,7 @@ struct DecParams {
   int m, n, k;           // C[m, n] = X[m, k] W[n, k]^T
   int bn, splits, kb_per_split, num_kb;
   int w_stages, a_stages;
+  int act;               // 1: SiLU-and-mul epilogue (interleaved gate/up rows, see act_silu_store)
   uint32_t idesc;
   __nv_bfloat16* c;
   int64_t ldc;
@@ -906,7 +968,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-
+  
   if ((warp == 0 || warp == 2) && lane == 0) {
     // ------------------------------------------------ producers: warp 0 weights, warp 2 activations
     const bool is_w = warp == 0;
@@ -914,6 +976,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
     const int S = is_w ? SW : SA;
     const uint32_t bytes = is_w ? (uint32_t)W_BYTES : (uint32_t)A_BYTES;
+    // the weights do not depend on the previous kernel: their ring fills while it finishes
+    if (!is_w) pdl_wait();
     uint32_t it = 0;
     bool ok = true;
     for (int i = 0; i < nkb; ++i, ++it) {
@@ -966,6 +1030,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     acc_ok = mbar_wait(tfull, 0, abort_flag, 10);
     tc_fence_after();
   }
+  pdl_wait();  // the output may still be read by the previous kernel in the stream
   if (p.splits == 1) {
     // whole K in this CTA: accumulator rows straight from TMEM to the output
     if (warp >= 2 && acc_ok) {
@@ -984,6 +1049,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           float f[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+          if (p.act) {  // bn % 32 == 0 and n % 32 == 0 in this mode
+            act_silu_store(p.c + (int64_t)pi * p.ldc + qj / 2, f);
+            continue;
+          }
           __nv_bfloat16* dst = p.c + (int64_t)pi * p.ldc + qj;
           if (valid == 32) {
 #pragma unroll
@@ -1023,10 +1092,43 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (warp >= 2) tc_fence_before();
       cluster_sync_all();  // every CTA's export of sub-tile mt is visible cluster-wide
+      if (p.act) {
+        // one row per warp at a time; lane item o4 = 4 output features (gates at column
+        // 32 (o4 / 4) + 4 (o4 % 4), ups 16 columns further)
+        const int O4 = BN / 8;
+#pragma unroll 1
+        for (int rr = r0 + warp; rr < r1; rr += NUM_THREADS / 32) {
+          const int pi = mt * BM + rr;
+          for (int o4 = lane; o4 < O4; o4 += 32) {
+            const int gc = 32 * (o4 >> 2) + 4 * (o4 & 3);
+            const uint32_t offg = xbase + (uint32_t)(rr * XLD + gc) * 4u, offu = offg + 64u;
+            float4 vg[8], vu[8];
+#pragma unroll
+            for (int s2 = 0; s2 < 8; ++s2)
+              if (s2 < p.splits) {
+                vg[s2] = ld_dsmem_f32x4(offg, (uint32_t)s2);
+                vu[s2] = ld_dsmem_f32x4(offu, (uint32_t)s2);
+              }
+            float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int s2 = 0; s2 < 8; ++s2)
+              if (s2 < p.splits) {
+                g[0] += vg[s2].x; g[1] += vg[s2].y; g[2] += vg[s2].z; g[3] += vg[s2].w;
+                u[0] += vu[s2].x; u[1] += vu[s2].y; u[2] += vu[s2].z; u[3] += vu[s2].w;
+              }
+            const int qg = tq * BN + gc;
+            if (pi >= p.m || qg >= p.n) continue;
+            const float o[4] = {silu_f(g[0]) * u[0], silu_f(g[1]) * u[1], silu_f(g[2]) * u[2],
+                                silu_f(g[3]) * u[3]};
+            const int oc = (tq * BN + 32 * (o4 >> 2)) / 2 + 4 * (o4 & 3);
+            *reinterpret_cast<uint2*>(p.c + (int64_t)pi * p.ldc + oc) = f32_to_bf16x4(o);
+          }
+        }
+      }
       // one row per warp at a time, lanes along the columns (coalesced DSMEM reads and
       // stores); two rows in flight per warp
 #pragma unroll 1
-      for (int rr = r0 + warp; rr < r1; rr += 2 * (NUM_THREADS / 32)) {
+      for (int rr = p.act ? r1 : r0 + warp; rr < r1; rr += 2 * (NUM_THREADS / 32)) {
         const int rr2 = rr + NUM_THREADS / 32;
         const bool has2 = rr2 < r1;
         const int pi = mt * BM + rr, pi2 = mt * BM + rr2;
@@ -1101,13 +1203,15 @@ int dec_capacity(int splits, int smem) {
   cfg.gridDim = dim3(splits * 64, 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 1;  // occupancy query: the cluster shape only
   int n = 0;
   if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
     cudaGetLastError();
@@ -1159,7 +1263,8 @@ std::vector<DecCfg> dec_candidates(int m, int n, int k) {
 }
 
 cudaError_t run_dec(const DecCfg& d, const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc,
-                    int m, int n, int k, cudaStream_t stream) {
+                    int m, int n, int k, cudaStream_t stream, int act = 0) {
+  if (act && (d.bn % 32 || n % 32)) return cudaErrorInvalidValue;
   CUtensorMap mx, mw;
   if (!make_map(&mx, x, m, k, ldx, BM) || !make_map(&mw, w, n, k, ldw, d.bn)) return cudaErrorInvalidValue;
   DecParams p;
@@ -1171,6 +1276,7 @@ cudaError_t run_dec(const DecCfg& d, const void* x, int64_t ldx, const void* w, 
   p.kb_per_split = d.kb_per_split;
   p.num_kb = k / BK;
   p.w_stages = d.w_stages;
+  p.act = act;
   p.a_stages = d.a_stages;
   p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(d.bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
   p.c = static_cast<__nv_bfloat16*>(c);
@@ -1180,13 +1286,15 @@ cudaError_t run_dec(const DecCfg& d, const void* x, int64_t ldx, const void* w, 
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = d.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = d.splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   static bool configured[3] = {false, false, false};
   if (d.mt == 2) {
     if (!configured[2]) {
@@ -1314,15 +1422,16 @@ GemmPlan gemm_plan(int m, int n, int k, int force_swap, int force_bn, int force_
 }
 
 cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n, int k,
-                      const GemmPlan& pl, float* ws, int* counters, cudaStream_t stream) {
+                      const GemmPlan& pl, float* ws, int* counters, cudaStream_t stream, int act) {
   if (m == 0 || n == 0) return cudaSuccess;
+  if (act && (pl.swap || n % 32 || pl.bn % 32)) return cudaErrorInvalidValue;
   if (k % 8 || ldx % 8 || ldw % 8) return cudaErrorInvalidValue;
   if (((uintptr_t)x & 15) || ((uintptr_t)w & 15)) return cudaErrorMisalignedAddress;
   if (!pl.swap && (ldc % 8 || ((uintptr_t)c & 15))) return cudaErrorInvalidValue;
   if (pl.dec) {
     if (m > pl.mt * BM || k % BK) return cudaErrorInvalidValue;
     DecCfg d{pl.mt, pl.bn, pl.splits, pl.kb_per_split, pl.stages, pl.a_stages, pl.smem, pl.tiles, 0.0};
-    return run_dec(d, x, ldx, w, ldw, c, ldc, m, n, k, stream);
+    return run_dec(d, x, ldx, w, ldw, c, ldc, m, n, k, stream, act);
   }
   const void* pbase = pl.swap ? w : x;
   const void* qbase = pl.swap ? x : w;
@@ -1349,6 +1458,7 @@ cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, vo
   prm.ws_ld = pl.ws_ld;
   prm.counters = counters;
   prm.streamk = pl.streamk;
+  prm.act = act;
   prm.sk_iters = (int64_t)pl.tiles * pl.num_kb;
   cudaError_t e;
   if (pl.streamk) {
@@ -1415,35 +1525,40 @@ int m_bucket(int m) { return m <= 256 ? m : ((m + 511) / 512) * 512; }
 
 cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n,
                             int k, float* ws, int64_t ws_elems, int* counters, int64_t num_counters,
-                            cudaStream_t stream, GemmPlan* chosen) {
+                            cudaStream_t stream, GemmPlan* chosen, int act) {
   if (m == 0 || n == 0) return cudaSuccess;
-  const auto key = std::make_tuple(m_bucket(m), n, k);
+  const auto key = std::make_tuple(m_bucket(m), act ? -n : n, k);
   {
     std::lock_guard<std::mutex> g(tune_mutex());
     auto it = tune_cache().find(key);
     if (it != tune_cache().end()) {
       if (chosen) *chosen = it->second;
-      return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, it->second, ws, counters, stream);
+      return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, it->second, ws, counters, stream, act);
     }
   }
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   cudaStreamIsCapturing(stream, &cap);
-  GemmPlan best = gemm_plan(m, n, k, -1, 0, 0);
+  GemmPlan best = gemm_plan(m, n, k, act ? 0 : -1, 0, 0);
   if (cap != cudaStreamCaptureStatusNone) {  // cannot time inside a capture
     if (chosen) *chosen = best;
-    return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, best, ws, counters, stream);
+    return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, best, ws, counters, stream, act);
   }
   std::vector<GemmPlan> cands;
   cands.push_back(best);
   for (int bn : {256, 128})
     for (int sp : {1, 2, 3, 4, 6, 8}) cands.push_back(gemm_plan(m, n, k, 0, bn, sp));
-  if (m <= 256) {
+  if (m <= 256 && !act) {
     const int bq = m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256;
     for (int sp : {1, 2, 3, 4}) cands.push_back(gemm_plan(m, n, k, 1, bq, sp));
   }
   if (m <= 2 * BM && k % BK == 0) {
     GemmPlan d;
-    for (int r = 0; r < 8 && gemm_dec_plan(m, n, k, r, &d); ++r) cands.push_back(d);
+    int taken = 0;
+    for (int r = 0; taken < 8 && gemm_dec_plan(m, n, k, r, &d); ++r)
+      if (!act || d.bn % 32 == 0) {
+        cands.push_back(d);
+        ++taken;
+      }
   }
   if (ws && counters) {
     for (int bn : {256, 128}) {
@@ -1466,7 +1581,7 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
   for (const auto& pl : cands) {
     if (pl.splits > 1 && pl.splits > 8) continue;
     if (pl.streamk && (pl.ws_elems > ws_elems || 4 * (int64_t)pl.tiles > num_counters)) continue;
-    if (gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, pl, ws, counters, stream) != cudaSuccess) {
+    if (gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, pl, ws, counters, stream, act) != cudaSuccess) {
       cudaGetLastError();
       continue;
     }
@@ -1477,7 +1592,7 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
         l2_evict_kernel<<<num_sms() * 4, 256, 0, stream>>>(static_cast<const uint4*>(flush), flush_bytes / 16 - 16,
                                                           static_cast<int*>(flush) + (flush_bytes / 4 - 1));
       cudaEventRecord(e0, stream);
-      good = gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, pl, ws, counters, stream) == cudaSuccess;
+      good = gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, pl, ws, counters, stream, act) == cudaSuccess;
       cudaEventRecord(e1, stream);
       cudaEventSynchronize(e1);
       float ms = 0.f;
@@ -1497,7 +1612,7 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
     tune_cache()[key] = best;
   }
   if (chosen) *chosen = best;
-  return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, best, ws, counters, stream);
+  return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, best, ws, counters, stream, act);
 }
 
 int gemm_error_code(int reset) {

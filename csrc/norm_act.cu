@@ -18,6 +18,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const __nv_bfloat16* _
                                                           const __nv_bfloat16* residual_in, __nv_bfloat16* residual_out,
                                                           const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
                                                           int H, float eps, const int* __restrict__ row_index) {
+  pdl_trigger();  // the next kernel may start its prologue
   const int row = blockIdx.x;
   const int src_row = row_index ? row_index[row] : row;
   const int nvec = H >> 3;
@@ -92,6 +93,7 @@ cudaError_t launch_add_rmsnorm(const void* x, int64_t x_stride, const void* resi
 
 // out[t, c] = silu(x[t, c]) * x[t, I + c]; 8 columns per thread.
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out, int T, int I) {
+  pdl_trigger();  // the next kernel may start its prologue
   const int64_t nvec_row = I >> 3;
   const int64_t total = (int64_t)T * nvec_row;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -122,6 +124,7 @@ cudaError_t launch_silu_mul(const void* x, void* out, int T, int I, cudaStream_t
 // Rows of a vocab shard [vocab_start, vocab_start + rows); other ids produce zeros.
 __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int rows,
                                  int vocab_start, __nv_bfloat16* __restrict__ out, int H) {
+  pdl_trigger();  // the next kernel may start its prologue
   const int t = blockIdx.x;
   const int local = ids[t] - vocab_start;
   const int nvec = H >> 3;

@@ -23,6 +23,7 @@ import zlib
 import torch
 
 from .configs import Qwen3Arch
+from ..ops.torch_ref import interleave_gate_up
 from .qwen3 import Qwen3ForCausalLM
 
 _HF = "model.layers.{i}."
@@ -139,7 +140,8 @@ def _fill(model: Qwen3ForCausalLM, src) -> Qwen3ForCausalLM:
         L.k_norm = src.get(p + "self_attn.k_norm.weight", dt)
         g = src.get(p + "mlp.gate_proj.weight", dt, rows=(r * ni, (r + 1) * ni))
         u = src.get(p + "mlp.up_proj.weight", dt, rows=(r * ni, (r + 1) * ni))
-        L.gate_up = torch.cat([g, u], 0).contiguous()
+        # gate/up rows interleaved in groups of 16: the GEMM applies SiLU-and-mul in its epilogue
+        L.gate_up = interleave_gate_up(g, u).contiguous()
         del g, u
         L.down = src.get(p + "mlp.down_proj.weight", dt, cols=(r * ni, (r + 1) * ni))
         L.ln1 = src.get(p + "input_layernorm.weight", dt)

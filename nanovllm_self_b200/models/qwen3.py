@@ -123,8 +123,7 @@ class Qwen3ForCausalLM:
             o = ops.attention(q, kc, vc, ctx, self.scale, ks, vs)
             h = ops.linear(o.view(T, nq * d), L.o, out=self._reduce_in(T))
             x, residual = self._reduce_norm(h, residual, L.ln2)
-            gu = ops.linear(x, L.gate_up)
-            a = ops.silu_mul(gu)
+            a = ops.linear_silu(x, L.gate_up)  # silu(gate) * up, fused into the GEMM epilogue
             h = ops.linear(a, L.down, out=self._reduce_in(T))
         return h, residual
 

@@ -33,7 +33,8 @@ def dense_logits(model: Qwen3ForCausalLM, token_ids: list[int]) -> torch.Tensor:
         o = R.dense_causal_attention(q, k, v, model.scale).reshape(-1, nq * d)
         x = (x.float() + R.linear(o, L.o).float()).to(x.dtype)
         h = R.rmsnorm(x, L.ln2, model.eps)
-        x = (x.float() + R.linear(R.silu_mul(R.linear(h, L.gate_up)), L.down).float()).to(x.dtype)
+        a = R.silu_mul_interleaved(R.linear(h, L.gate_up)).to(x.dtype)
+        x = (x.float() + R.linear(a, L.down).float()).to(x.dtype)
     x = R.rmsnorm(x[-1:], model.norm, model.eps)
     return R.linear(x, model.lm_head)[0].float()
 

@@ -59,6 +59,10 @@ class TorchOps:
     def silu_mul(self, x):
         return R.silu_mul(x)
 
+    def linear_silu(self, x, w_gate_up):
+        """silu(gate) * up of x @ w^T, w in the interleaved gate/up layout."""
+        return R.silu_mul_interleaved(R.linear(x, w_gate_up)).to(x.dtype)
+
     def sample(self, logits, temperatures, top_p=None, seeds=None, step=0, batch_greedy_compat=False,
                generator=None, use_top_p=True, col_offset=0):
         return R.sample(logits, temperatures, top_p, generator, batch_greedy_compat).to(torch.int32)

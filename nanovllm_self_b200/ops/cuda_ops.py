@@ -93,6 +93,17 @@ class CudaOps:
         self.launches += 1
         return out
 
+    def linear_silu(self, x, w_gate_up):
+        """silu(gate) * up of x @ w^T in one GEMM (SiLU-and-mul epilogue); w's rows are in the
+        interleaved gate/up layout of ``torch_ref.interleave_gate_up``."""
+        out = torch.empty(x.shape[0], w_gate_up.shape[0] // 2, dtype=x.dtype, device=x.device)
+        if x.shape[0] == 0:
+            return out
+        sc = self.scratch(x.device)
+        self.last_plan = self.C.linear_tuned(x, w_gate_up, out, sc.gemm, sc.gemm_counters, 1)
+        self.launches += 1
+        return out
+
     def _plan(self, m, n, k):
         key = (m, n, k)
         p = self._plans.get(key)

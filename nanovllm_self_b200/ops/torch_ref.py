@@ -138,6 +138,27 @@ def silu_mul(x: torch.Tensor) -> torch.Tensor:
     return (F.silu(g) * u).to(x.dtype)
 
 
+GATE_UP_GROUP = 16
+
+
+def interleave_gate_up(g: torch.Tensor, u: torch.Tensor, group: int = GATE_UP_GROUP) -> torch.Tensor:
+    """[I, H] gate and up weights -> [2I, H] with rows interleaved in groups of ``group``:
+    rows 2·group·j .. +group-1 are gate features group·j.., the next ``group`` rows the
+    matching up features.  Every tile of 32 output columns of ``x @ W^T`` then holds 16
+    gates and their 16 ups, which lets the GEMM apply SiLU-and-mul in its epilogue."""
+    i, h = g.shape
+    if i % group:
+        raise ValueError(f"intermediate size {i} is not a multiple of {group}")
+    return torch.stack([g.reshape(i // group, group, h), u.reshape(i // group, group, h)], 1).reshape(2 * i, h)
+
+
+def silu_mul_interleaved(y: torch.Tensor, group: int = GATE_UP_GROUP) -> torch.Tensor:
+    """y [T, 2I] in the interleaved layout of :func:`interleave_gate_up` -> silu(gate) * up [T, I]."""
+    t, n = y.shape
+    y = y.float().reshape(t, n // (2 * group), 2, group)
+    return (F.silu(y[:, :, 0]) * y[:, :, 1]).reshape(t, n // 2)
+
+
 def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return F.linear(x, w)
 

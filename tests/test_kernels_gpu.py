@@ -250,3 +250,33 @@ def test_gemm_decode_kernel(ops, m, n, k):
         _close(out, ref, 0.05 * math.sqrt(k / 2048), 0.02)
     assert seen > 0
     assert ops.C.gemm_error(True) == 0
+
+
+@pytest.mark.parametrize("m,inter,k", [(1, 512, 1024), (64, 1536, 2048), (200, 6144, 4096), (256, 12288, 1024),
+                                       (777, 1024, 512)])
+def test_gemm_silu_epilogue(ops, m, inter, k):
+    # gate/up rows interleaved in groups of 16; every GEMM variant's fused epilogue must
+    # give silu(gate) * up
+    g = torch.Generator(device=DEV).manual_seed(m + inter)
+    x = torch.randn(m, k, device=DEV, generator=g).bfloat16()
+    wg = (torch.randn(inter, k, device=DEV, generator=g) * 0.05).bfloat16()
+    wu = (torch.randn(inter, k, device=DEV, generator=g) * 0.05).bfloat16()
+    w = R.interleave_gate_up(wg, wu).contiguous()
+    ref = torch.nn.functional.silu(x.float() @ wg.float().t()) * (x.float() @ wu.float().t())
+    sc = ops.scratch(x.device)
+    tol = 0.05 * math.sqrt(k / 2048)
+    outs = [ops.linear_silu(x, w)]
+    for bn, sp in [(256, 1), (128, 3), (128, -1), (256, -2)]:
+        o = torch.zeros(m, inter, device=DEV, dtype=torch.bfloat16)
+        ops.C.linear(x, w, o, sc.gemm, sc.gemm_counters, 0, bn, sp, 1)
+        outs.append(o)
+    if m <= 256:
+        for rank in range(3):
+            o = torch.zeros(m, inter, device=DEV, dtype=torch.bfloat16)
+            cfg = ops.C.linear_dec(x, w, o, rank, 1)
+            if cfg and cfg[0]:
+                outs.append(o)
+    for o in outs:
+        _close(o, ref, tol, 0.03)
+    assert int(sc.gemm_counters.abs().sum()) == 0
+    assert ops.C.gemm_error(True) == 0
