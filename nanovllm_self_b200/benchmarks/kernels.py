@@ -27,7 +27,7 @@ from ..ops.cuda_ops import CudaOps
 
 NQ, NKV, D, HID, INTER, VOCAB = 32, 8, 128, 4096, 12288, 151936
 CASES = ("attn_decode", "attn_decode_fp8", "attn_prefill", "attn_prefill_fp8", "gemm_prefill", "gemm_decode",
-         "gemm_decode256", "qkv_post", "qkv_post_fp8", "add_rmsnorm", "silu_mul", "sample")
+         "gemm_decode256", "gemm_gate_up_silu256", "qkv_post", "qkv_post_fp8", "add_rmsnorm", "silu_mul", "sample")
 
 
 class _Ctx:
@@ -70,6 +70,12 @@ def build_case(name: str, ops: CudaOps, dev="cuda"):
         B, L = 8, 2048
         q, kc, vc, ks, vs, c = _paged(B, L, L, fp8, dev)
         return (lambda: ops.attention(q, kc, vc, c, D ** -0.5, ks, vs)), None, 2 * B * NQ * L * L * D
+    if name == "gemm_gate_up_silu256":
+        from ..ops.torch_ref import interleave_gate_up
+        m = 256
+        x = torch.randn(m, HID, device=dev).to(torch.bfloat16)
+        w = interleave_gate_up(*(torch.randn(2, INTER, HID, device=dev) * 0.02).to(torch.bfloat16)).contiguous()
+        return (lambda: ops.linear_silu(x, w)), 2 * (m * HID + 2 * INTER * HID + m * INTER), 2 * m * 2 * INTER * HID
     if name.startswith("gemm"):
         m, n, k = {"gemm_prefill": (4096, 2 * INTER, HID), "gemm_decode": (64, (NQ + 2 * NKV) * D, HID),
                    "gemm_decode256": (256, 2 * INTER, HID)}[name]
@@ -142,6 +148,7 @@ def time_case(name: str, iters: int = 20) -> dict:
     out = {"case": name, "us": round(us, 2), "iters": iters, "l2": "256 MiB read before each launch",
            "peaks": src}
     if name.startswith("gemm"):
+        # splits < 0: stream-K with -splits token sub-tiles; splits >= 100: decode kernel, splits - 100 K slices
         out["plan"] = dict(zip(("swap", "bn", "tiles_p", "tiles_q", "splits", "grid"), ops.last_plan))
     if nbytes:
         out["gb_s"] = round(nbytes / us / 1e3, 1)
