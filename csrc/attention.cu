@@ -190,6 +190,7 @@ template <bool FP8>
 __global__ void __launch_bounds__(160, 2)
     attn_decode_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                            DecodeArgs da) {
+  pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
   const AttnArgs& a = da.a;
   extern __shared__ __align__(1024) uint8_t dsm_raw[];
@@ -540,6 +541,7 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
 __global__ void __launch_bounds__(160, 3)
     attn_decode_fp8_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                            DecodeArgs da) {
+  pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
   const AttnArgs& a = da.a;
   extern __shared__ __align__(1024) uint8_t dsm_raw[];
@@ -804,6 +806,7 @@ __global__ void __launch_bounds__(160, 3)
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                     const int* __restrict__ cu_q, __nv_bfloat16* __restrict__ out, int nq, int splits,
                                     int seq_offset) {
+  pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
   const int bh = blockIdx.x;
   const int b = bh / nq + seq_offset, hq = bh % nq;
@@ -824,6 +827,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
 // ------------------------------------------------------------------------ prefill
 template <bool FP8>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
+  pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sq = smem;                      // 64 x 256 B
@@ -1082,25 +1086,25 @@ cudaError_t launch_attn_decode(const AttnLaunch& L, cudaStream_t stream) {
       cudaFuncSetAttribute(attn_decode_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_fp8_smem(8));
       cfg = true;
     }
-    attn_decode_fp8_kernel<<<grid, 160, decode_fp8_smem(L.nq / L.nkv), stream>>>(km, vm, da);
+    launch_pdl(attn_decode_fp8_kernel, grid, dim3(160), decode_fp8_smem(L.nq / L.nkv), stream, km, vm, da);
   } else if (L.kv_fp8) {
     static bool cfg = false;
     if (!cfg) {
       cudaFuncSetAttribute(attn_decode_tma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_max);
       cfg = true;
     }
-    attn_decode_tma_kernel<true><<<grid, 160, sm, stream>>>(km, vm, da);
+    launch_pdl(attn_decode_tma_kernel<true>, grid, dim3(160), sm, stream, km, vm, da);
   } else {
     static bool cfg = false;
     if (!cfg) {
       cudaFuncSetAttribute(attn_decode_tma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_max);
       cfg = true;
     }
-    attn_decode_tma_kernel<false><<<grid, 160, sm, stream>>>(km, vm, da);
+    launch_pdl(attn_decode_tma_kernel<false>, grid, dim3(160), sm, stream, km, vm, da);
   }
   NVB_LAUNCH_CHECK();
   if (L.splits > 1) {
-    attn_combine_kernel<<<L.num_seqs * L.nq, AD, 0, stream>>>(L.part_o, L.part_lse, L.cu_q, a.out, L.nq, L.splits,
+    launch_pdl(attn_combine_kernel, dim3(L.num_seqs * L.nq), dim3(AD), 0, stream, L.part_o, L.part_lse, L.cu_q, a.out, L.nq, L.splits,
                                                              L.seq_offset);
     NVB_LAUNCH_CHECK();
   }
@@ -1144,10 +1148,10 @@ cudaError_t launch_attn_prefill(const AttnLaunch& L, int max_q_len, cudaStream_t
   int sm = prefill_smem(L.kv_fp8);
   if (L.kv_fp8) {
     cudaFuncSetAttribute(attn_prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-    attn_prefill_kernel<true><<<grid, 128, sm, stream>>>(a);
+    launch_pdl(attn_prefill_kernel<true>, grid, dim3(128), sm, stream, a);
   } else {
     cudaFuncSetAttribute(attn_prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-    attn_prefill_kernel<false><<<grid, 128, sm, stream>>>(a);
+    launch_pdl(attn_prefill_kernel<false>, grid, dim3(128), sm, stream, a);
   }
   NVB_LAUNCH_CHECK();
   return cudaSuccess;

@@ -50,15 +50,45 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // Signal slot `b` of every rank, then wait until every rank signalled slot `b` here.
-// Executed by thread 0 of the CTA.  Returns false on timeout.
+// Executed by thread 0 of the CTA after a __syncthreads.  The flag stores are releases at
+// system scope: they order every write this CTA made before the barrier (cumulatively, through
+// the __syncthreads) ahead of the flag, so no separate full system fence is needed; the
+// previous kernel's writes (the GEMM that filled IN) completed at the kernel boundary.
+// Returns false on timeout.
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 __device__ bool cta_barrier(const CommArgs& a, int phase, int b, uint32_t epoch) {
-  __threadfence_system();
+  const uint32_t* mine = a.flags[a.rank] + (phase * COMM_MAX_CTAS + b) * COMM_MAX_RANKS;
+  const uint64_t t0 = comm_timer();
+  if (a.full_fence == 2) {
+    // one release fence, relaxed flag stores; relaxed polling, one acquire fence
+    fence_acq_rel_sys();
+    for (int p = 0; p < a.world; ++p)
+      st_relaxed_sys(a.flags[p] + ((phase * COMM_MAX_CTAS + b) * COMM_MAX_RANKS + a.rank), epoch);
+    for (int p = 0; p < a.world; ++p) {
+      while (ld_relaxed_sys(mine + p) != epoch) {
+        if (comm_timer() - t0 > COMM_WAIT_NS) {
+          atomicCAS(&g_comm_error, 0, 100 + phase);
+          return false;
+        }
+      }
+    }
+    fence_acq_rel_sys();
+    return true;
+  }
+  if (a.full_fence) __threadfence_system();
   for (int p = 0; p < a.world; ++p) {
     uint32_t* f = a.flags[p] + ((phase * COMM_MAX_CTAS + b) * COMM_MAX_RANKS + a.rank);
     st_release_sys(f, epoch);
   }
-  const uint32_t* mine = a.flags[a.rank] + (phase * COMM_MAX_CTAS + b) * COMM_MAX_RANKS;
-  const uint64_t t0 = comm_timer();
   for (int p = 0; p < a.world; ++p) {
     while (ld_acquire_sys(mine + p) != epoch) {
       if (comm_timer() - t0 > COMM_WAIT_NS) {
@@ -72,6 +102,7 @@ __device__ bool cta_barrier(const CommArgs& a, int phase, int b, uint32_t epoch)
 
 template <int NI>
 __global__ void __launch_bounds__(256) allreduce_add_rmsnorm_kernel(CommArgs a) {
+  pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
   const int b = blockIdx.x;
   __shared__ uint32_t s_epoch;
@@ -167,6 +198,7 @@ __global__ void __launch_bounds__(256) allreduce_add_rmsnorm_kernel(CommArgs a) 
 // reach the barrier of call k+1 after every rank finished reading call k's buffer.
 template <int NI>
 __global__ void __launch_bounds__(256) allreduce_oneshot_kernel(CommArgs a) {
+  pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
   const int b = blockIdx.x;
   __shared__ uint32_t s_epoch;
@@ -253,10 +285,10 @@ cudaError_t launch_allreduce_oneshot(const CommArgs& a, cudaStream_t stream) {
   const int threads = nvec >= 256 ? 256 : ((nvec + 31) / 32) * 32;
   const int ni = (nvec + threads - 1) / threads;
   switch (ni) {
-    case 1: allreduce_oneshot_kernel<1><<<a.ctas, threads, 0, stream>>>(a); break;
-    case 2: allreduce_oneshot_kernel<2><<<a.ctas, threads, 0, stream>>>(a); break;
-    case 3: allreduce_oneshot_kernel<3><<<a.ctas, threads, 0, stream>>>(a); break;
-    default: allreduce_oneshot_kernel<4><<<a.ctas, threads, 0, stream>>>(a); break;
+    case 1: launch_pdl(allreduce_oneshot_kernel<1>, dim3(a.ctas), dim3(threads), 0, stream, a); break;
+    case 2: launch_pdl(allreduce_oneshot_kernel<2>, dim3(a.ctas), dim3(threads), 0, stream, a); break;
+    case 3: launch_pdl(allreduce_oneshot_kernel<3>, dim3(a.ctas), dim3(threads), 0, stream, a); break;
+    default: launch_pdl(allreduce_oneshot_kernel<4>, dim3(a.ctas), dim3(threads), 0, stream, a); break;
   }
   return cudaGetLastError();
 }
@@ -269,10 +301,10 @@ cudaError_t launch_allreduce_add_rmsnorm(const CommArgs& a, cudaStream_t stream)
   const int threads = nvec >= 256 ? 256 : ((nvec + 31) / 32) * 32;
   const int ni = (nvec + threads - 1) / threads;
   switch (ni) {
-    case 1: allreduce_add_rmsnorm_kernel<1><<<a.ctas, threads, 0, stream>>>(a); break;
-    case 2: allreduce_add_rmsnorm_kernel<2><<<a.ctas, threads, 0, stream>>>(a); break;
-    case 3: allreduce_add_rmsnorm_kernel<3><<<a.ctas, threads, 0, stream>>>(a); break;
-    default: allreduce_add_rmsnorm_kernel<4><<<a.ctas, threads, 0, stream>>>(a); break;
+    case 1: launch_pdl(allreduce_add_rmsnorm_kernel<1>, dim3(a.ctas), dim3(threads), 0, stream, a); break;
+    case 2: launch_pdl(allreduce_add_rmsnorm_kernel<2>, dim3(a.ctas), dim3(threads), 0, stream, a); break;
+    case 3: launch_pdl(allreduce_add_rmsnorm_kernel<3>, dim3(a.ctas), dim3(threads), 0, stream, a); break;
+    default: launch_pdl(allreduce_add_rmsnorm_kernel<4>, dim3(a.ctas), dim3(threads), 0, stream, a); break;
   }
   return cudaGetLastError();
 }

@@ -21,6 +21,7 @@ struct CommArgs {
   uint32_t* epochs;                    // this rank's per-CTA epoch words (local memory)
   const __nv_bfloat16* weight;
   int rank, world, rows, hidden, ctas, has_residual;
+  int full_fence;                      // 1: a full system fence before each flag release
   float eps;
 };
 

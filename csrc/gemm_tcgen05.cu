@@ -83,6 +83,24 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Bounded wait for a long phase (the epilogue warps waiting for the whole mainloop): polls
+// with a back-off so the spinning warps leave the issue slots to the producer and MMA threads
+// that share their SM sub-partitions.
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, volatile int* abort_flag, int code) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    __nanosleep(512);
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > WAIT_BUDGET_NS) {
+      atomicCAS(&g_gemm_error, 0, code);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
 // Drain wait used on the error path: short budget, never sets flags.
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = globaltimer();
@@ -340,6 +358,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();  // inputs and the output may belong to the previous kernel in the stream
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -601,6 +620,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();  // inputs and the output may belong to the previous kernel in the stream
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -968,6 +988,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();  // every CTA of this grid is resident (grid <= SMs): let the next kernel launch
   
   if ((warp == 0 || warp == 2) && lane == 0) {
     // ------------------------------------------------ producers: warp 0 weights, warp 2 activations
@@ -1027,10 +1048,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncwarp();
   bool acc_ok = true;
   if (warp >= 2) {
-    acc_ok = mbar_wait(tfull, 0, abort_flag, 10);
+    acc_ok = (warp == 2 ? mbar_wait : mbar_wait_sleep)(tfull, 0, abort_flag, 10);
     tc_fence_after();
   }
   pdl_wait();  // the output may still be read by the previous kernel in the stream
+  pdl_trigger();
   if (p.splits == 1) {
     // whole K in this CTA: accumulator rows straight from TMEM to the output
     if (warp >= 2 && acc_ok) {

@@ -18,6 +18,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const __nv_bfloat16* _
                                                           const __nv_bfloat16* residual_in, __nv_bfloat16* residual_out,
                                                           const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
                                                           int H, float eps, const int* __restrict__ row_index) {
+  pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
   const int row = blockIdx.x;
   const int src_row = row_index ? row_index[row] : row;
@@ -82,10 +83,10 @@ cudaError_t launch_add_rmsnorm(const void* x, int64_t x_stride, const void* resi
   auto W = static_cast<const __nv_bfloat16*>(w);
   auto O = static_cast<__nv_bfloat16*>(out);
   switch (ni) {
-    case 1: add_rmsnorm_kernel<1><<<rows, threads, 0, stream>>>(X, x_stride, R, RO, W, O, H, eps, row_index); break;
-    case 2: add_rmsnorm_kernel<2><<<rows, threads, 0, stream>>>(X, x_stride, R, RO, W, O, H, eps, row_index); break;
-    case 3: add_rmsnorm_kernel<3><<<rows, threads, 0, stream>>>(X, x_stride, R, RO, W, O, H, eps, row_index); break;
-    default: add_rmsnorm_kernel<4><<<rows, threads, 0, stream>>>(X, x_stride, R, RO, W, O, H, eps, row_index); break;
+    case 1: launch_pdl(add_rmsnorm_kernel<1>, dim3(rows), dim3(threads), 0, stream, X, x_stride, R, RO, W, O, H, eps, row_index); break;
+    case 2: launch_pdl(add_rmsnorm_kernel<2>, dim3(rows), dim3(threads), 0, stream, X, x_stride, R, RO, W, O, H, eps, row_index); break;
+    case 3: launch_pdl(add_rmsnorm_kernel<3>, dim3(rows), dim3(threads), 0, stream, X, x_stride, R, RO, W, O, H, eps, row_index); break;
+    default: launch_pdl(add_rmsnorm_kernel<4>, dim3(rows), dim3(threads), 0, stream, X, x_stride, R, RO, W, O, H, eps, row_index); break;
   }
   NVB_LAUNCH_CHECK();
   return cudaSuccess;
@@ -93,6 +94,7 @@ cudaError_t launch_add_rmsnorm(const void* x, int64_t x_stride, const void* resi
 
 // out[t, c] = silu(x[t, c]) * x[t, I + c]; 8 columns per thread.
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out, int T, int I) {
+  pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
   const int64_t nvec_row = I >> 3;
   const int64_t total = (int64_t)T * nvec_row;
@@ -124,6 +126,7 @@ cudaError_t launch_silu_mul(const void* x, void* out, int T, int I, cudaStream_t
 // Rows of a vocab shard [vocab_start, vocab_start + rows); other ids produce zeros.
 __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int rows,
                                  int vocab_start, __nv_bfloat16* __restrict__ out, int H) {
+  pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
   const int t = blockIdx.x;
   const int local = ids[t] - vocab_start;

@@ -69,6 +69,8 @@ __device__ __forceinline__ void load_head(const QkvPostArgs& a, int t, int head,
 }
 
 __global__ void __launch_bounds__(128) qkv_post_kernel(QkvPostArgs a) {
+  pdl_wait();     // inputs come from the previous kernel in the stream
+  pdl_trigger();  // the next kernel may start its prologue
   const int lane = threadIdx.x & 31;
   const int heads = a.nq + 2 * a.nkv;
   const int64_t gw = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -144,7 +146,7 @@ cudaError_t launch_qkv_post(const void* qkv, int64_t qkv_stride, void* q_out, co
   a.kv_fp8 = kv_fp8;
   int64_t warps = (int64_t)T * (nq + 2 * nkv);
   int64_t blocks = (warps + 3) / 4;
-  qkv_post_kernel<<<(unsigned)blocks, 128, 0, stream>>>(a);
+  launch_pdl(qkv_post_kernel, dim3((unsigned)blocks), dim3(128), 0, stream, a);
   NVB_LAUNCH_CHECK();
   return cudaSuccess;
 }

@@ -48,6 +48,8 @@ __global__ void __launch_bounds__(256) sample_partial_kernel(const T* __restrict
                                                              const int64_t* __restrict__ seed_step,
                                                              float* __restrict__ part_val, int* __restrict__ part_idx,
                                                              int chunk) {
+  pdl_wait();     // inputs come from the previous kernel in the stream
+  pdl_trigger();  // the next kernel may start its prologue
   const int row = blockIdx.y, ch = blockIdx.x;
   const float t = temps[row];
   const bool greedy = !(t > 0.f);
@@ -120,6 +122,8 @@ __global__ void __launch_bounds__(256) sample_partial_kernel(const T* __restrict
 // One warp per row: reduce the chunk partials; writes the token id and the winning score.
 __global__ void sample_final_kernel(const float* __restrict__ part_val, const int* __restrict__ part_idx, int nchunk,
                                     int rows, int* __restrict__ out_tok, float* __restrict__ out_val) {
+  pdl_wait();     // inputs come from the previous kernel in the stream
+  pdl_trigger();  // the next kernel may start its prologue
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -165,14 +169,14 @@ cudaError_t launch_sample(const void* logits, int logits_is_bf16, int64_t ld, in
   chunk = (chunk + 7) & ~7;
   dim3 grid(nchunk, rows);
   if (logits_is_bf16)
-    sample_partial_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), ld, V,
-                                                                   col_offset, temps, seed_step, part_val, part_idx,
-                                                                   chunk);
+    launch_pdl(sample_partial_kernel<__nv_bfloat16>, grid, dim3(256), 0, stream,
+               static_cast<const __nv_bfloat16*>(logits), ld, V, col_offset, temps, seed_step, part_val, part_idx, chunk);
   else
-    sample_partial_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(logits), ld, V, col_offset, temps,
-                                                           seed_step, part_val, part_idx, chunk);
+    launch_pdl(sample_partial_kernel<float>, grid, dim3(256), 0, stream, static_cast<const float*>(logits), ld, V,
+               col_offset, temps, seed_step, part_val, part_idx, chunk);
   NVB_LAUNCH_CHECK();
-  sample_final_kernel<<<(rows + 3) / 4, 128, 0, stream>>>(part_val, part_idx, nchunk, rows, out_tok, out_val);
+  launch_pdl(sample_final_kernel, dim3((rows + 3) / 4), dim3(128), 0, stream, part_val, part_idx, nchunk, rows, out_tok,
+             out_val);
   NVB_LAUNCH_CHECK();
   return cudaSuccess;
 }
