@@ -28,6 +28,7 @@ from ..config import EngineConfig
 from ..models.loader import has_checkpoint
 from ..parallel.state import init_tensor_parallel
 from ..sampling_params import SamplingParams
+from ..utils.tracing import StepTracer
 from .model_runner import ModelRunner
 from .scheduler import Scheduler
 from .sequence import Sequence, SequenceStatus
@@ -46,6 +47,7 @@ class LLMEngine:
             config = config.replace(**kwargs) if kwargs else config
         self.config = config
         self.enable_profile = enable_profile
+        self.tracer = StepTracer(enabled=enable_profile)
         self.tp = init_tensor_parallel(config.tensor_parallel_size, config.device)
         self.comm = None
         if self.tp.size > 1:
@@ -108,12 +110,17 @@ class LLMEngine:
 
     def step(self):
         """One schedule -> run -> postprocess iteration. Returns (scheduled, finished, dev_ms)."""
-        seqs = self.scheduler.schedule()
+        tr = self.tracer
+        with tr.phase("schedule"):
+            seqs = self.scheduler.schedule()
         if not seqs:
             return [], [], 0.0
-        token_ids, need = self.model_runner.run(seqs)
+        with tr.phase("run"):
+            token_ids, need = self.model_runner.run(seqs)
         dev_ms = self.model_runner.last_dev_ms
-        finished = self.scheduler.postprocess(seqs, token_ids, need)
+        tr.record_step(seqs, dev_ms)
+        with tr.phase("postprocess"):
+            finished = self.scheduler.postprocess(seqs, token_ids, need)
         return seqs, finished, dev_ms
 
     def is_finished(self) -> bool:
@@ -159,6 +166,8 @@ class LLMEngine:
         wall = time.perf_counter() - t_start
         if pbar:
             pbar.close()
+        if self.enable_profile:
+            self.tracer.print_summary()
         outputs = [s.token_ids for s in seqs]
         if not return_metrics:
             return outputs
@@ -184,6 +193,8 @@ class LLMEngine:
             "num_preemptions": self.scheduler.num_preemptions,
             "block_usage": self.block_manager.get_block_usage_snapshot(),
         }
+        if self.enable_profile:
+            metrics["profile"] = self.tracer.summary()
         return {"outputs": outputs, "metrics": metrics}
 
     def shutdown(self):

@@ -76,6 +76,8 @@ class ModelRunner:
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.last_dev_ms = 0.0
+        # NVTX ranges around each step (NVB_NVTX=1): visible in an external timeline profiler
+        self.nvtx = self.is_cuda and os.environ.get("NVB_NVTX", "0") not in ("", "0")
         self.graph_launches: dict = {}
         self._use_top_p = False
         self._gen = torch.Generator(device=self.device)
@@ -323,6 +325,9 @@ class ModelRunner:
         graph_bs = None
         if self.enable_cuda_graph and all_decode and not self._use_top_p and len(seqs) <= self.graph_max_bs:
             graph_bs = next(b for b in self.graph_bs_list if b >= len(seqs))
+        nvtx = self.nvtx
+        if nvtx:
+            torch.cuda.nvtx.range_push(f"step bs={len(seqs)} {'graph' if graph_bs else 'eager'}")
         if graph_bs is not None:
             toks = self._run_graph(seqs, graph_bs)
         else:
@@ -332,6 +337,8 @@ class ModelRunner:
             toks = self._forward_and_sample(ids, pos, ctx, temps, topp)
             self._mark(1)
             toks = self._fetch(toks, len(need))
+        if nvtx:
+            torch.cuda.nvtx.range_pop()
         self.last_dev_ms = self._ev[0].elapsed_time(self._ev[1]) if self.is_cuda else 0.0
         self.sample_step += 1
         if self.is_cuda:

@@ -105,3 +105,16 @@ def test_int8_mock_and_fp8_kv_close_to_oracle(prompts):
         ref = _oracle(llm, prompts[:2], 6)
         agree = sum(a == b for o, r, p in zip(out, ref, prompts) for a, b in zip(o[len(p):], r))
         assert agree >= 10, (mode, agree)
+
+
+def test_profile_summary_and_nvtx_off(capsys):
+    from nanovllm_self_b200 import LLM, SamplingParams
+    from nanovllm_self_b200.engine.llm_engine import LLMEngine
+    eng = LLMEngine(enable_profile=True, model="tiny", device="cpu", block_size=16, max_model_len=256,
+                    dtype="fp32", num_blocks=64)
+    res = eng.generate([[1, 2, 3, 4, 5]], SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True),
+                       return_metrics=True)
+    prof = res["metrics"]["profile"]
+    assert prof["steps"] == prof["prefill_steps"] + prof["decode_steps"] and prof["decode_steps"] >= 3
+    assert prof["host_run_ms"] > 0
+    assert "[PROFILE]" in capsys.readouterr().out
