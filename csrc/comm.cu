@@ -68,23 +68,6 @@ __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_re
 __device__ bool cta_barrier(const CommArgs& a, int phase, int b, uint32_t epoch) {
   const uint32_t* mine = a.flags[a.rank] + (phase * COMM_MAX_CTAS + b) * COMM_MAX_RANKS;
   const uint64_t t0 = comm_timer();
-  if (a.full_fence == 2) {
-    // one release fence, relaxed flag stores; relaxed polling, one acquire fence
-    fence_acq_rel_sys();
-    for (int p = 0; p < a.world; ++p)
-      st_relaxed_sys(a.flags[p] + ((phase * COMM_MAX_CTAS + b) * COMM_MAX_RANKS + a.rank), epoch);
-    for (int p = 0; p < a.world; ++p) {
-      while (ld_relaxed_sys(mine + p) != epoch) {
-        if (comm_timer() - t0 > COMM_WAIT_NS) {
-          atomicCAS(&g_comm_error, 0, 100 + phase);
-          return false;
-        }
-      }
-    }
-    fence_acq_rel_sys();
-    return true;
-  }
-  if (a.full_fence) __threadfence_system();
   for (int p = 0; p < a.world; ++p) {
     uint32_t* f = a.flags[p] + ((phase * COMM_MAX_CTAS + b) * COMM_MAX_RANKS + a.rank);
     st_release_sys(f, epoch);
@@ -123,29 +106,36 @@ __global__ void __launch_bounds__(256) allreduce_add_rmsnorm_kernel(CommArgs a) 
     for (int row = r0 + b; row < r1; row += gridDim.x) {
       float v[NI][8];
       float ss = 0.f;
+      // issue every load of the row (all peers, all vectors, the residual) before using any
+      uint4 raw[NI][COMM_MAX_RANKS], rres[NI];
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < nvec) {
+#pragma unroll
+          for (int p = 0; p < COMM_MAX_RANKS; ++p)
+            if (p < a.world) raw[i][p] = __ldcv(reinterpret_cast<const uint4*>(a.in[p] + (int64_t)row * H) + c);
+          if (a.has_residual) rres[i] = reinterpret_cast<const uint4*>(a.res[a.rank] + (int64_t)row * H)[c];
+        }
+      }
 #pragma unroll
       for (int i = 0; i < NI; ++i) {
         const int c = threadIdx.x + i * blockDim.x;
         if (c < nvec) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
-          // issue every peer's load before using any (NVLink latency overlaps)
-          uint4 raw[COMM_MAX_RANKS];
-#pragma unroll
-          for (int p = 0; p < COMM_MAX_RANKS; ++p)
-            if (p < a.world) raw[p] = __ldcv(reinterpret_cast<const uint4*>(a.in[p] + (int64_t)row * H) + c);
 #pragma unroll
           for (int p = 0; p < COMM_MAX_RANKS; ++p) {
             if (p < a.world) {
               float f[8];
-              bf16x8_to_f32(raw[p], f);
+              bf16x8_to_f32(raw[i][p], f);
 #pragma unroll
               for (int j = 0; j < 8; ++j) v[i][j] += f[j];
             }
           }
           if (a.has_residual) {
             float r[8];
-            bf16x8_to_f32(reinterpret_cast<const uint4*>(a.res[a.rank] + (int64_t)row * H)[c], r);
+            bf16x8_to_f32(rres[i], r);
 #pragma unroll
             for (int j = 0; j < 8; ++j) v[i][j] = bf16_round(v[i][j] + r[j]);
           } else {
@@ -196,49 +186,119 @@ __global__ void __launch_bounds__(256) allreduce_add_rmsnorm_kernel(CommArgs a) 
 // own memory only.  The caller rotates IN over three buffers (consecutive calls never
 // share one), which is what makes the missing second barrier safe: a rank can only
 // reach the barrier of call k+1 after every rank finished reading call k's buffer.
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Per-rank barrier of the one-shot kernel: CTA 0 alone exchanges flags with the peers
+// (one NVLink round trip per call instead of one per CTA) and then releases the other
+// CTAs of this rank through a local "go" word.  The call number comes from a local
+// counter that the last CTA to finish advances, so every CTA of a call reads the same
+// value at its start.  All CTAs are resident together (grid <= the SM count).
+__device__ bool oneshot_rank_barrier(const CommArgs& a, uint32_t& epoch) {
+  uint32_t* ctrl = a.flags[a.rank] + COMM_CTRL;  // [0] calls, [1] go, [2] done
+  epoch = ld_acquire_gpu(ctrl) + 1;
+  if (blockIdx.x == 0) {
+    bool ok = true;
+    fence_acq_rel_sys();
+    for (int p = 0; p < a.world; ++p) st_relaxed_sys(a.flags[p] + COMM_ONESHOT_FLAGS + a.rank, epoch);
+    const uint32_t* mine = a.flags[a.rank] + COMM_ONESHOT_FLAGS;
+    const uint64_t t0 = comm_timer();
+    for (int p = 0; p < a.world && ok; ++p) {
+      while (ld_relaxed_sys(mine + p) != epoch) {
+        if (comm_timer() - t0 > COMM_WAIT_NS) {
+          atomicCAS(&g_comm_error, 0, 110);
+          ok = false;
+          break;
+        }
+      }
+    }
+    fence_acq_rel_sys();
+    st_release_gpu(ctrl + 1, ok ? epoch : 0xFFFFFFFFu);
+    return ok;
+  }
+  const uint64_t t0 = comm_timer();
+  uint32_t g;
+  while ((g = ld_acquire_gpu(ctrl + 1)) != epoch) {
+    if (g == 0xFFFFFFFFu) return false;
+    if (comm_timer() - t0 > COMM_WAIT_NS) {
+      atomicCAS(&g_comm_error, 0, 111);
+      return false;
+    }
+  }
+  return true;
+}
+
+// The last CTA of the call to get here advances the call counter.
+__device__ void oneshot_finish(const CommArgs& a, uint32_t epoch) {
+  uint32_t* ctrl = a.flags[a.rank] + COMM_CTRL;
+  __threadfence();
+  if (atomicAdd(ctrl + 2, 1u) == gridDim.x - 1) {
+    ctrl[2] = 0;
+    st_release_gpu(ctrl, epoch);
+  }
+}
+
 template <int NI>
 __global__ void __launch_bounds__(256) allreduce_oneshot_kernel(CommArgs a) {
   pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
-  const int b = blockIdx.x;
   __shared__ uint32_t s_epoch;
   __shared__ int s_ok;
   __shared__ float red[32];
   if (threadIdx.x == 0) {
-    s_epoch = a.epochs[b] + 1;
-    s_ok = cta_barrier(a, 0, b, s_epoch) ? 1 : 0;
-    a.epochs[b] = s_epoch;
+    uint32_t e = 0;
+    s_ok = oneshot_rank_barrier(a, e) ? 1 : 0;
+    s_epoch = e;
   }
   __syncthreads();
-  if (!s_ok) return;
+  if (!s_ok) {
+    if (threadIdx.x == 0) oneshot_finish(a, s_epoch);
+    return;
+  }
+  const int b = blockIdx.x;
   const int H = a.hidden;
   const int nvec = H >> 3;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   for (int row = b; row < a.rows; row += gridDim.x) {
     float v[NI][8];
     float ss = 0.f;
+    // issue every load of the row (all peers, all of this thread's vectors, the residual)
+    // before using any, so the NVLink latency is paid once per row, not once per load
+    uint4 raw[NI][COMM_MAX_RANKS], rres[NI];
 #pragma unroll
     for (int i = 0; i < NI; ++i) {
       const int c = threadIdx.x + i * blockDim.x;
       if (c < nvec) {
-        uint4 raw[COMM_MAX_RANKS];
 #pragma unroll
         for (int p = 0; p < COMM_MAX_RANKS; ++p)
-          if (p < a.world) raw[p] = __ldcv(reinterpret_cast<const uint4*>(a.in[p] + (int64_t)row * H) + c);
+          if (p < a.world) raw[i][p] = __ldcv(reinterpret_cast<const uint4*>(a.in[p] + (int64_t)row * H) + c);
+        if (a.has_residual) rres[i] = reinterpret_cast<const uint4*>(a.res[a.rank] + (int64_t)row * H)[c];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nvec) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
 #pragma unroll
         for (int p = 0; p < COMM_MAX_RANKS; ++p) {
           if (p < a.world) {
             float f[8];
-            bf16x8_to_f32(raw[p], f);
+            bf16x8_to_f32(raw[i][p], f);
 #pragma unroll
             for (int j = 0; j < 8; ++j) v[i][j] += f[j];
           }
         }
         if (a.has_residual) {
           float r[8];
-          bf16x8_to_f32(reinterpret_cast<const uint4*>(a.res[a.rank] + (int64_t)row * H)[c], r);
+          bf16x8_to_f32(rres[i], r);
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[i][j] = bf16_round(v[i][j] + r[j]);
         } else {
@@ -273,6 +333,7 @@ __global__ void __launch_bounds__(256) allreduce_oneshot_kernel(CommArgs a) {
     }
     __syncthreads();
   }
+  if (threadIdx.x == 0) oneshot_finish(a, s_epoch);
 }
 
 }  // namespace

@@ -10,8 +10,13 @@ namespace nvb {
 
 constexpr int COMM_MAX_RANKS = 8;
 constexpr int COMM_MAX_CTAS = 256;
-// FLAGS region: [2 phases][COMM_MAX_CTAS][COMM_MAX_RANKS] uint32.
-constexpr size_t COMM_FLAG_BYTES = 2 * COMM_MAX_CTAS * COMM_MAX_RANKS * sizeof(uint32_t);
+// FLAGS region: [2 phases][COMM_MAX_CTAS][COMM_MAX_RANKS] uint32 per-CTA flags of the
+// two-shot kernel, then [COMM_MAX_RANKS] uint32 flags of the one-shot kernel's per-rank
+// barrier, then COMM_CTRL_WORDS local control words (one-shot: call count, go, done).
+constexpr int COMM_CTRL_WORDS = 8;
+constexpr size_t COMM_ONESHOT_FLAGS = 2 * COMM_MAX_CTAS * COMM_MAX_RANKS;  // word offset
+constexpr size_t COMM_CTRL = COMM_ONESHOT_FLAGS + COMM_MAX_RANKS;         // word offset
+constexpr size_t COMM_FLAG_BYTES = (COMM_CTRL + COMM_CTRL_WORDS) * sizeof(uint32_t);
 
 struct CommArgs {
   __nv_bfloat16* in[COMM_MAX_RANKS];   // every rank's IN buffer (peer pointers)
@@ -21,7 +26,6 @@ struct CommArgs {
   uint32_t* epochs;                    // this rank's per-CTA epoch words (local memory)
   const __nv_bfloat16* weight;
   int rank, world, rows, hidden, ctas, has_residual;
-  int full_fence;                      // 1: a full system fence before each flag release
   float eps;
 };
 

@@ -56,8 +56,6 @@ void allreduce_add_rmsnorm(std::vector<int64_t> bases, int64_t in_off, int64_t r
   a.hidden = (int)hidden;
   a.ctas = (int)ctas;
   a.has_residual = has_residual ? 1 : 0;
-  static const int full_fence = getenv("NVB_COMM_FULL_FENCE") ? atoi(getenv("NVB_COMM_FULL_FENCE")) : 0;
-  a.full_fence = full_fence;
   a.eps = (float)eps;
   at::cuda::CUDAGuard g(weight.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
