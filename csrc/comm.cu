@@ -8,16 +8,19 @@
 //   IN  [rows, H] bf16  per-rank partial sums (the row-parallel GEMM writes here)
 //   RES [rows, H] bf16  residual stream (replicated)
 //   OUT [rows, H] bf16  RMSNorm output (replicated; the next GEMM reads it)
-//   FLAGS               [2 phases][MAX_CTAS][MAX_RANKS] uint32 epoch words
+//   FLAGS               cross-rank barrier flags + local control words (comm.h)
 // Two-shot algorithm, one launch, grid = NCTA CTAs on every rank:
-//   1. barrier A: CTA b tells CTA b of every peer "my IN is ready" (the GEMM that wrote
-//      IN precedes this kernel on each rank's stream) and waits for the peers;
+//   1. barrier A: CTA 0 tells every peer "my IN is ready" (the GEMM that wrote IN
+//      precedes this kernel on each rank's stream), waits for the peers, and releases the
+//      other CTAs of its rank through a local go word;
 //   2. rank r owns rows [r*T/tp, (r+1)*T/tp); CTA b takes every NCTA-th owned row,
 //      sums the row over all peers' IN (NVLink loads), adds RES, normalises, and stores
 //      the new RES row and the OUT row into every rank's buffers (NVLink stores);
-//   3. barrier B: CTA b tells CTA b of every peer "my stores are done" and waits, so on
-//      return every rank holds all rows of RES and OUT.
-// Epochs are per CTA slot in device memory, advanced by the kernel itself, so the call is
+//   3. barrier B: the last CTA of the rank to finish tells every peer "all my stores are
+//      done" and waits for the peers before it exits, so when the kernel completes every
+//      rank holds all rows of RES and OUT.
+// Barriers are per rank (one NVLink round trip per call, whatever the CTA count).  The
+// call number lives in device memory and is advanced by the kernel itself, so the call is
 // CUDA-graph capturable.  Every wait is bounded by a wall-clock budget; on expiry the
 // kernel records an error code (read with comm_error_code) and returns.
 #include <cuda_runtime.h>
@@ -39,22 +42,6 @@ __device__ __forceinline__ uint64_t comm_timer() {
   return t;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Signal slot `b` of every rank, then wait until every rank signalled slot `b` here.
-// Executed by thread 0 of the CTA after a __syncthreads.  The flag stores are releases at
-// system scope: they order every write this CTA made before the barrier (cumulatively, through
-// the __syncthreads) ahead of the flag, so no separate full system fence is needed; the
-// previous kernel's writes (the GEMM that filled IN) completed at the kernel boundary.
-// Returns false on timeout.
 __device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -64,23 +51,74 @@ __device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   return v;
 }
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
-__device__ bool cta_barrier(const CommArgs& a, int phase, int b, uint32_t epoch) {
-  const uint32_t* mine = a.flags[a.rank] + (phase * COMM_MAX_CTAS + b) * COMM_MAX_RANKS;
+// Wraparound-safe "flag has reached call e".
+__device__ __forceinline__ bool reached(uint32_t v, uint32_t e) { return (int32_t)(v - e) >= 0; }
+
+// Cross-rank part of a per-rank barrier (one thread): publish call number `epoch` in slot
+// `flags_off` of every rank, then wait until every rank published it (or a later one) here.
+__device__ bool rank_exchange(const CommArgs& a, size_t flags_off, uint32_t epoch, int code) {
+  fence_acq_rel_sys();
+  for (int p = 0; p < a.world; ++p) st_relaxed_sys(a.flags[p] + flags_off + a.rank, epoch);
+  const uint32_t* mine = a.flags[a.rank] + flags_off;
   const uint64_t t0 = comm_timer();
   for (int p = 0; p < a.world; ++p) {
-    uint32_t* f = a.flags[p] + ((phase * COMM_MAX_CTAS + b) * COMM_MAX_RANKS + a.rank);
-    st_release_sys(f, epoch);
-  }
-  for (int p = 0; p < a.world; ++p) {
-    while (ld_acquire_sys(mine + p) != epoch) {
+    while (!reached(ld_relaxed_sys(mine + p), epoch)) {
       if (comm_timer() - t0 > COMM_WAIT_NS) {
-        atomicCAS(&g_comm_error, 0, 100 + phase);
+        atomicCAS(&g_comm_error, 0, code);
+        fence_acq_rel_sys();
         return false;
       }
     }
   }
+  fence_acq_rel_sys();
   return true;
+}
+
+// Entry barrier (thread 0 of each CTA): every CTA reads this call's number from the local
+// counter; CTA 0 exchanges flags with the peers and then releases the other CTAs of this
+// rank through the local go word.  All CTAs of a call are resident together (grid <= the
+// SM count), so waiting on CTA 0 cannot stall.
+__device__ bool rank_entry_barrier(const CommArgs& a, size_t flags_off, uint32_t& epoch) {
+  uint32_t* ctrl = a.flags[a.rank] + COMM_CTRL;  // [0] calls, [1] go, [2] done, [3] go error
+  epoch = ld_acquire_gpu(ctrl) + 1;
+  if (blockIdx.x == 0) {
+    const bool ok = rank_exchange(a, flags_off, epoch, 110);
+    if (!ok) ctrl[3] = epoch;
+    st_release_gpu(ctrl + 1, epoch);
+    return ok;
+  }
+  const uint64_t t0 = comm_timer();
+  while (!reached(ld_acquire_gpu(ctrl + 1), epoch)) {
+    if (comm_timer() - t0 > COMM_WAIT_NS) {
+      atomicCAS(&g_comm_error, 0, 111);
+      return false;
+    }
+  }
+  return ld_acquire_gpu(ctrl + 3) != epoch;
+}
+
+// Exit (thread 0 of each CTA, after a __syncthreads): the last CTA of this rank to get here
+// optionally runs the exit barrier with the peers, then advances the call counter.
+__device__ void rank_exit(const CommArgs& a, uint32_t epoch, bool exit_barrier, bool ok) {
+  uint32_t* ctrl = a.flags[a.rank] + COMM_CTRL;
+  // this CTA's stores before its arrival: system scope only when they went to peers
+  if (exit_barrier) fence_acq_rel_sys();
+  else __threadfence();
+  uint32_t prev;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ctrl + 2) : "memory");
+  if (prev != gridDim.x - 1) return;
+  if (exit_barrier && ok) rank_exchange(a, COMM_TWOSHOT_B, epoch, 112);
+  ctrl[2] = 0;
+  st_release_gpu(ctrl, epoch);
 }
 
 template <int NI>
@@ -92,8 +130,9 @@ __global__ void __launch_bounds__(256) allreduce_add_rmsnorm_kernel(CommArgs a) 
   __shared__ int s_ok;
   __shared__ float red[32];
   if (threadIdx.x == 0) {
-    s_epoch = a.epochs[b] + 1;
-    s_ok = cta_barrier(a, 0, b, s_epoch) ? 1 : 0;
+    uint32_t e = 0;
+    s_ok = rank_entry_barrier(a, COMM_TWOSHOT_A, e) ? 1 : 0;
+    s_epoch = e;
   }
   __syncthreads();
   const uint32_t epoch = s_epoch;
@@ -175,10 +214,7 @@ __global__ void __launch_bounds__(256) allreduce_add_rmsnorm_kernel(CommArgs a) 
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    if (s_ok) cta_barrier(a, 1, b, epoch);
-    a.epochs[b] = epoch;  // advance even on error so every slot stays in step locally
-  }
+  if (threadIdx.x == 0) rank_exit(a, epoch, true, s_ok != 0);
 }
 
 // One-shot variant for small batches: a single barrier ("every rank's IN is ready"),
@@ -186,64 +222,6 @@ __global__ void __launch_bounds__(256) allreduce_add_rmsnorm_kernel(CommArgs a) 
 // own memory only.  The caller rotates IN over three buffers (consecutive calls never
 // share one), which is what makes the missing second barrier safe: a rank can only
 // reach the barrier of call k+1 after every rank finished reading call k's buffer.
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Per-rank barrier of the one-shot kernel: CTA 0 alone exchanges flags with the peers
-// (one NVLink round trip per call instead of one per CTA) and then releases the other
-// CTAs of this rank through a local "go" word.  The call number comes from a local
-// counter that the last CTA to finish advances, so every CTA of a call reads the same
-// value at its start.  All CTAs are resident together (grid <= the SM count).
-__device__ bool oneshot_rank_barrier(const CommArgs& a, uint32_t& epoch) {
-  uint32_t* ctrl = a.flags[a.rank] + COMM_CTRL;  // [0] calls, [1] go, [2] done
-  epoch = ld_acquire_gpu(ctrl) + 1;
-  if (blockIdx.x == 0) {
-    bool ok = true;
-    fence_acq_rel_sys();
-    for (int p = 0; p < a.world; ++p) st_relaxed_sys(a.flags[p] + COMM_ONESHOT_FLAGS + a.rank, epoch);
-    const uint32_t* mine = a.flags[a.rank] + COMM_ONESHOT_FLAGS;
-    const uint64_t t0 = comm_timer();
-    for (int p = 0; p < a.world && ok; ++p) {
-      while (ld_relaxed_sys(mine + p) != epoch) {
-        if (comm_timer() - t0 > COMM_WAIT_NS) {
-          atomicCAS(&g_comm_error, 0, 110);
-          ok = false;
-          break;
-        }
-      }
-    }
-    fence_acq_rel_sys();
-    st_release_gpu(ctrl + 1, ok ? epoch : 0xFFFFFFFFu);
-    return ok;
-  }
-  const uint64_t t0 = comm_timer();
-  uint32_t g;
-  while ((g = ld_acquire_gpu(ctrl + 1)) != epoch) {
-    if (g == 0xFFFFFFFFu) return false;
-    if (comm_timer() - t0 > COMM_WAIT_NS) {
-      atomicCAS(&g_comm_error, 0, 111);
-      return false;
-    }
-  }
-  return true;
-}
-
-// The last CTA of the call to get here advances the call counter.
-__device__ void oneshot_finish(const CommArgs& a, uint32_t epoch) {
-  uint32_t* ctrl = a.flags[a.rank] + COMM_CTRL;
-  __threadfence();
-  if (atomicAdd(ctrl + 2, 1u) == gridDim.x - 1) {
-    ctrl[2] = 0;
-    st_release_gpu(ctrl, epoch);
-  }
-}
-
 template <int NI>
 __global__ void __launch_bounds__(256) allreduce_oneshot_kernel(CommArgs a) {
   pdl_wait();     // inputs come from the previous kernel in the stream
@@ -253,12 +231,12 @@ __global__ void __launch_bounds__(256) allreduce_oneshot_kernel(CommArgs a) {
   __shared__ float red[32];
   if (threadIdx.x == 0) {
     uint32_t e = 0;
-    s_ok = oneshot_rank_barrier(a, e) ? 1 : 0;
+    s_ok = rank_entry_barrier(a, COMM_ONESHOT_FLAGS, e) ? 1 : 0;
     s_epoch = e;
   }
   __syncthreads();
   if (!s_ok) {
-    if (threadIdx.x == 0) oneshot_finish(a, s_epoch);
+    if (threadIdx.x == 0) rank_exit(a, s_epoch, false, false);
     return;
   }
   const int b = blockIdx.x;
@@ -333,7 +311,7 @@ __global__ void __launch_bounds__(256) allreduce_oneshot_kernel(CommArgs a) {
     }
     __syncthreads();
   }
-  if (threadIdx.x == 0) oneshot_finish(a, s_epoch);
+  if (threadIdx.x == 0) rank_exit(a, s_epoch, false, true);
 }
 
 }  // namespace

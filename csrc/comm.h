@@ -10,20 +10,22 @@ namespace nvb {
 
 constexpr int COMM_MAX_RANKS = 8;
 constexpr int COMM_MAX_CTAS = 256;
-// FLAGS region: [2 phases][COMM_MAX_CTAS][COMM_MAX_RANKS] uint32 per-CTA flags of the
-// two-shot kernel, then [COMM_MAX_RANKS] uint32 flags of the one-shot kernel's per-rank
-// barrier, then COMM_CTRL_WORDS local control words (one-shot: call count, go, done).
+// FLAGS region (uint32 words): [3 barriers][COMM_MAX_RANKS] cross-rank flags (one-shot,
+// two-shot phase A, two-shot phase B; slot p holds rank p's latest call number), then
+// COMM_CTRL_WORDS local control words: [0] calls completed, [1] go, [2] CTAs done.
 constexpr int COMM_CTRL_WORDS = 8;
-constexpr size_t COMM_ONESHOT_FLAGS = 2 * COMM_MAX_CTAS * COMM_MAX_RANKS;  // word offset
-constexpr size_t COMM_CTRL = COMM_ONESHOT_FLAGS + COMM_MAX_RANKS;         // word offset
-constexpr size_t COMM_FLAG_BYTES = (COMM_CTRL + COMM_CTRL_WORDS) * sizeof(uint32_t);
+constexpr size_t COMM_ONESHOT_FLAGS = 0;                      // word offsets
+constexpr size_t COMM_TWOSHOT_A = COMM_MAX_RANKS;
+constexpr size_t COMM_TWOSHOT_B = 2 * COMM_MAX_RANKS;
+constexpr size_t COMM_CTRL = 3 * COMM_MAX_RANKS;
+constexpr size_t COMM_FLAG_BYTES = 256;
+static_assert((COMM_CTRL + COMM_CTRL_WORDS) * sizeof(uint32_t) <= COMM_FLAG_BYTES, "flag region");
 
 struct CommArgs {
   __nv_bfloat16* in[COMM_MAX_RANKS];   // every rank's IN buffer (peer pointers)
   __nv_bfloat16* res[COMM_MAX_RANKS];
   __nv_bfloat16* out[COMM_MAX_RANKS];
   uint32_t* flags[COMM_MAX_RANKS];
-  uint32_t* epochs;                    // this rank's per-CTA epoch words (local memory)
   const __nv_bfloat16* weight;
   int rank, world, rows, hidden, ctas, has_residual;
   float eps;

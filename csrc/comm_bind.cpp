@@ -33,12 +33,11 @@ void symm_free(int64_t p) { check(nvb::symm_free(reinterpret_cast<void*>(p)), "s
 
 // bases[p] = rank p's buffer (opened locally); layout offsets in bytes.
 void allreduce_add_rmsnorm(std::vector<int64_t> bases, int64_t in_off, int64_t res_off, int64_t out_off,
-                           int64_t flag_off, const at::Tensor& epochs, const at::Tensor& weight, int64_t rank,
+                           int64_t flag_off, const at::Tensor& weight, int64_t rank,
                            int64_t rows, int64_t hidden, bool has_residual, double eps, int64_t ctas,
                            bool oneshot) {
   TORCH_CHECK((int)bases.size() <= nvb::COMM_MAX_RANKS, "too many ranks");
   TORCH_CHECK(weight.scalar_type() == at::kBFloat16 && weight.is_contiguous(), "weight bf16");
-  TORCH_CHECK(epochs.scalar_type() == at::kInt && epochs.numel() >= ctas, "epochs int32[ctas]");
   nvb::CommArgs a;
   std::memset(&a, 0, sizeof(a));
   for (size_t p = 0; p < bases.size(); ++p) {
@@ -48,7 +47,6 @@ void allreduce_add_rmsnorm(std::vector<int64_t> bases, int64_t in_off, int64_t r
     a.out[p] = reinterpret_cast<__nv_bfloat16*>(base + out_off);
     a.flags[p] = reinterpret_cast<uint32_t*>(base + flag_off);
   }
-  a.epochs = reinterpret_cast<uint32_t*>(epochs.data_ptr<int>());
   a.weight = reinterpret_cast<const __nv_bfloat16*>(weight.data_ptr());
   a.rank = (int)rank;
   a.world = (int)bases.size();
@@ -89,7 +87,7 @@ void register_comm(pybind11::module& m) {
   m.def("symm_close", &symm_close);
   m.def("symm_free", &symm_free);
   m.def("allreduce_add_rmsnorm", &allreduce_add_rmsnorm, pybind11::arg("bases"), pybind11::arg("in_off"),
-        pybind11::arg("res_off"), pybind11::arg("out_off"), pybind11::arg("flag_off"), pybind11::arg("epochs"),
+        pybind11::arg("res_off"), pybind11::arg("out_off"), pybind11::arg("flag_off"),
         pybind11::arg("weight"), pybind11::arg("rank"), pybind11::arg("rows"), pybind11::arg("hidden"),
         pybind11::arg("has_residual"), pybind11::arg("eps"), pybind11::arg("ctas"), pybind11::arg("oneshot") = false);
   m.def("comm_error", &comm_error, pybind11::arg("reset") = false);

@@ -24,14 +24,21 @@ class _DevPtr:
 
 class SymmetricWorkspace:
 
-    def __init__(self, tp, rows: int, hidden: int, oneshot_rows: int = 512):
+    # one-shot while the bytes each rank pulls from its peers, (world - 1) * T * H * 2,
+    # stay below this; beyond it the two-shot kernel moves 2 (world - 1) / world of that
+    ONESHOT_PEER_BYTES = 4 << 20
+
+    def __init__(self, tp, rows: int, hidden: int, oneshot_rows: int | None = None):
         self.C = load()
         self.tp = tp
         self.rows = rows
         self.hidden = hidden
-        # one-shot (single barrier, every rank reduces every row) while the peers' bytes
-        # each rank must read stay small; two-shot beyond
+        if oneshot_rows is None:
+            oneshot_rows = max(1, min(512, self.ONESHOT_PEER_BYTES // (max(1, tp.size - 1) * hidden * 2)))
         self.oneshot_rows = oneshot_rows
+        # every CTA of a call must be resident at once (the per-rank barrier releases them)
+        self.max_ctas = min(int(self.C.COMM_MAX_CTAS),
+                            torch.cuda.get_device_properties(tp.device).multi_processor_count)
         row_bytes = rows * hidden * 2
         small = min(rows, oneshot_rows) * hidden * 2
         # IN (two-shot) | IN0 IN1 IN2 (one-shot rotation) | RES | OUT | FLAGS
@@ -63,7 +70,6 @@ class SymmetricWorkspace:
         self.IN1 = [view(o, min(rows, oneshot_rows)) for o in self.in1_off]
         self.RES = view(self.res_off, rows)
         self.OUT = view(self.out_off, rows)
-        self.epochs = torch.zeros(self.C.COMM_MAX_CTAS, dtype=torch.int32, device=tp.device)
         self._k = 0  # position in the one-shot IN rotation
         dist.barrier(group=tp.group)
 
@@ -90,11 +96,11 @@ class SymmetricWorkspace:
         if has_res and residual.data_ptr() != res.data_ptr():
             res.copy_(residual)
         if one:
-            ctas = max(1, min(148, T))
+            ctas = max(1, min(self.max_ctas, T))
         else:
-            ctas = max(1, min(int(self.C.COMM_MAX_CTAS), (T + self.tp.size - 1) // self.tp.size))
+            ctas = max(1, min(self.max_ctas, (T + self.tp.size - 1) // self.tp.size))
         self.C.allreduce_add_rmsnorm(self.bases, in_off, self.res_off, self.out_off, self.flag_off,
-                                     self.epochs, w, self.tp.rank, T, self.hidden, has_res, float(eps), ctas, one)
+                                     w, self.tp.rank, T, self.hidden, has_res, float(eps), ctas, one)
         if one:
             self._k += 1
         if ops is not None and hasattr(ops, "launches"):
