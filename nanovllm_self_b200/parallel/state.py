@@ -34,8 +34,11 @@ class TPState:
 _STATE = TPState()
 
 
-def init_tensor_parallel(tp_size: int, device: str = "cuda", timeout_s: float = 600.0) -> TPState:
-    """Initialise (or reuse) the default process group for ``tp_size`` ranks."""
+def init_tensor_parallel(tp_size: int, device: str = "cuda", timeout_s: float = 600.0, gpu_offset: int = 0) -> TPState:
+    """Initialise (or reuse) the default process group for ``tp_size`` ranks.
+
+    Rank ``r`` uses GPU ``gpu_offset + LOCAL_RANK``, so two TP groups can share a node
+    (for example a prefill group on GPUs 0-3 and a decode group on GPUs 4-7)."""
     global _STATE
     is_cuda = str(device).startswith("cuda")
     if tp_size == 1:
@@ -55,8 +58,8 @@ def init_tensor_parallel(tp_size: int, device: str = "cuda", timeout_s: float = 
     rank = int(os.environ["RANK"])
     local_rank = int(os.environ.get("LOCAL_RANK", rank))
     if is_cuda:
-        torch.cuda.set_device(local_rank)
-        dev = torch.device("cuda", local_rank)
+        torch.cuda.set_device(gpu_offset + local_rank)
+        dev = torch.device("cuda", gpu_offset + local_rank)
     else:
         dev = torch.device("cpu")
     if not dist.is_initialized():

@@ -32,14 +32,25 @@ def _pct(xs, q):
 class PDPool:
     def __init__(self, work_root, num_prefill=1, num_decode=1, backend="shared_memory", model="tiny",
                  prefill_devices=None, decode_devices=None, policy="load_aware", worker_args=None,
-                 handshake_timeout_s=120.0, nccl_port=29650, python=sys.executable):
+                 handshake_timeout_s=120.0, nccl_port=29650, python=sys.executable, tp=1, device_kind="cuda"):
         self.root = Path(work_root)
         self.root.mkdir(parents=True, exist_ok=True)
         self.P, self.D = num_prefill, num_decode
         self.backend = backend
         self.model = model
-        self.pdev = prefill_devices or [f"cuda:{i}" for i in range(num_prefill)]
-        self.ddev = decode_devices or [f"cuda:{num_prefill + i}" for i in range(num_decode)]
+        # tp > 1: every worker is a tensor-parallel group of tp processes on consecutive GPUs
+        # (prefill group i on GPUs [i tp, (i+1) tp), decode group j after all prefill groups)
+        self.tp = tp
+        self.device_kind = device_kind
+        if tp > 1 and backend == "sync_gpu":
+            raise ValueError("sync_gpu P/D workers are TP=1; use ipc_push or shared_memory with tp > 1")
+        if tp > 1:
+            self.pdev = [f"{device_kind}:{i * tp}" if device_kind == "cuda" else "cpu" for i in range(num_prefill)]
+            self.ddev = [f"{device_kind}:{(num_prefill + i) * tp}" if device_kind == "cuda" else "cpu"
+                         for i in range(num_decode)]
+        else:
+            self.pdev = prefill_devices or [f"cuda:{i}" for i in range(num_prefill)]
+            self.ddev = decode_devices or [f"cuda:{num_prefill + i}" for i in range(num_decode)]
         self.p_router = Router(num_prefill, policy)
         self.d_router = Router(num_decode, policy)
         self.worker_args = list(worker_args or [])
@@ -54,10 +65,18 @@ class PDPool:
 
     # ------------------------------------------------------------- lifecycle
     def _launch(self, role, idx, device, wd, rank):
-        cmd = [self.python, "-m", "nanovllm_self_b200.pd.multiprocess.workers", role, "--work-dir", str(wd.path),
-               "--model", self.model, "--device", device, "--backend", self.backend,
-               "--global-rank", str(rank), "--world-size", str(self.P + self.D), "--nccl-port", str(self.nccl_port),
-               "--handshake-timeout-s", str(self.timeout)] + self.worker_args
+        args = [role, "--work-dir", str(wd.path), "--model", self.model, "--device", device, "--backend", self.backend,
+                "--global-rank", str(rank), "--world-size", str(self.P + self.D), "--nccl-port", str(self.nccl_port),
+                "--handshake-timeout-s", str(self.timeout)] + self.worker_args
+        if self.tp > 1:
+            # one torchrun per group; its ranks form the group's TP world
+            offset = rank * self.tp if self.device_kind == "cuda" else 0
+            cmd = [self.python, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={self.tp}",
+                   "--master-addr=127.0.0.1", f"--master-port={self.nccl_port + 1 + rank}",
+                   "-m", "nanovllm_self_b200.pd.multiprocess.workers"] + args + \
+                  ["--tp", str(self.tp), "--gpu-offset", str(offset)]
+        else:
+            cmd = [self.python, "-m", "nanovllm_self_b200.pd.multiprocess.workers"] + args
         log = open(wd.f(f"{role}.log"), "w")
         env = dict(os.environ)
         env.setdefault("NCCL_NVLS_ENABLE", "0")
@@ -192,6 +211,7 @@ def main(argv=None):
     ap.add_argument("--input-mean", type=float, default=2048)
     ap.add_argument("--output-mean", type=float, default=256)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--tp", type=int, default=1, help="each worker is a TP group of this many GPUs")
     args, rest = ap.parse_known_args(argv)
     rng = np.random.default_rng(0)
     rows = []
@@ -201,7 +221,7 @@ def main(argv=None):
         rows.append({"id": f"req-{i}", "prompt_ids": rng.integers(0, 151936, n_in).tolist(), "max_tokens": n_out,
                      "input_tokens": n_in})
     pool = PDPool(args.work_root, args.num_prefill, args.num_decode, args.backend, args.model, policy=args.policy,
-                  worker_args=rest)
+                  worker_args=rest, tp=args.tp)
     pool.start()
     try:
         summary = pool.run(rows, concurrency=args.concurrency, rate=args.rate)

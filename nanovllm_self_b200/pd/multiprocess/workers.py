@@ -20,6 +20,15 @@ KV backends:
   straight into the decode pool over NVLink and signals ``push_done``.
 
 Every wait on a peer is bounded (``--handshake-timeout-s``).
+
+A worker can be a tensor-parallel group (``--tp N``, launched with ``torch.distributed.run``,
+rank r on GPU ``--gpu-offset + r``): the group's rank 0 reads the work directory and decides,
+and every decision (serve this request, admit this payload, run a decode step, stop) is
+broadcast to the other ranks over a CPU control group, so all ranks run the same engine
+operations in lockstep.  KV moves shard by shard: prefill rank r hands its KV heads to decode
+rank r (``shared_memory``: one payload file per rank; ``ipc_push``: one exported pool per
+decode rank, one ``push_done`` per prefill rank).  ``sync_gpu`` needs one NCCL world across
+P and D and stays TP=1.
 """
 from __future__ import annotations
 
@@ -66,6 +75,9 @@ def add_common_args(ap: argparse.ArgumentParser) -> None:
     ap.add_argument("--handshake-timeout-s", type=float, default=120.0)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--enforce-eager", action="store_true")
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel size of this worker (torchrun launch)")
+    ap.add_argument("--gpu-offset", type=int, default=0, help="rank r of the group uses GPU gpu_offset + r")
+    ap.add_argument("--comm-backend", default="fused")
 
 
 def build_runner(args, kv_pool_ipc: bool = False) -> ModelRunner:
@@ -74,11 +86,72 @@ def build_runner(args, kv_pool_ipc: bool = False) -> ModelRunner:
                        max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens,
                        max_model_len=args.max_model_len, kv_cache_quant_mode=args.kv_cache_quant_mode,
                        gpu_memory_utilization=args.gpu_memory_utilization, seed=args.seed,
-                       enforce_eager=args.enforce_eager)
+                       enforce_eager=args.enforce_eager, tensor_parallel_size=args.tp,
+                       comm_backend=args.comm_backend)
+    if args.tp > 1:
+        from ...parallel.comm import TPComm
+        from ...parallel.state import init_tensor_parallel
+        kind = "cuda" if str(args.device).startswith("cuda") else "cpu"
+        tp = init_tensor_parallel(args.tp, kind, timeout_s=args.handshake_timeout_s, gpu_offset=args.gpu_offset)
+        cfg = cfg.replace(device=str(tp.device))
+        comm = TPComm(tp, backend=cfg.comm_backend, config=cfg)
+        return ModelRunner(cfg, tp, comm)
     dev = torch.device(args.device)
     if dev.type == "cuda":
         torch.cuda.set_device(dev)
     return ModelRunner(cfg, TPState(device=dev))
+
+
+class GroupControl:
+    """Lockstep control of a TP worker group: rank 0 decides, the other ranks follow.
+
+    ``sync(cmd)`` returns rank 0's command on every rank (a pickled object broadcast over a
+    CPU group); ``all_ok(flag)`` is True only if every rank passed True; ``barrier()`` waits
+    for the whole group.  With one rank these are identities."""
+
+    def __init__(self, tp: TPState):
+        self.tp = tp
+        self.group = None
+        if tp.size > 1:
+            import torch.distributed as dist
+            self.group = dist.new_group(backend="gloo")
+
+    @property
+    def leader(self) -> bool:
+        return self.tp.rank == 0
+
+    def sync(self, cmd):
+        if self.group is None:
+            return cmd
+        import torch.distributed as dist
+        box = [cmd]
+        dist.broadcast_object_list(box, src=0, group=self.group)
+        return box[0]
+
+    def all_ok(self, ok: bool) -> bool:
+        if self.group is None:
+            return ok
+        import torch.distributed as dist
+        t = torch.tensor([0 if ok else 1], dtype=torch.int32)
+        dist.all_reduce(t, group=self.group)
+        return int(t.item()) == 0
+
+    def barrier(self) -> None:
+        if self.group is not None:
+            import torch.distributed as dist
+            dist.barrier(group=self.group)
+
+
+def rank_file(name: str, rank: int, size: int) -> str:
+    """Per-rank artefact name: ``x.pkl`` -> ``x.rank2.pkl`` in a TP group, unchanged at TP=1."""
+    if size == 1:
+        return name
+    stem, dot, ext = name.rpartition(".")
+    return f"{stem}.rank{rank}.{ext}" if dot else f"{name}.rank{rank}"
+
+
+def rank_name(name: str, tp: TPState) -> str:
+    return rank_file(name, tp.rank, tp.size)
 
 
 def init_world(args) -> None:
@@ -103,9 +176,13 @@ def _error(wd: WorkDir, base: str, stage: str, exc: BaseException) -> None:
 class PrefillWorker:
     def __init__(self, args):
         self.args = args
+        if args.tp > 1 and args.backend == "sync_gpu":
+            raise ValueError("sync_gpu needs one NCCL world across P and D: use ipc_push or shared_memory with --tp")
         self.wd = WorkDir(args.work_dir)
         init_world(args)
         self.runner = build_runner(args)
+        self.tp = self.runner.tp
+        self.ctl = GroupControl(self.tp)
         cfg = self.runner.config
         if args.backend == "shared_memory":
             store = SharedMemoryKVStoreBackend()
@@ -114,7 +191,7 @@ class PrefillWorker:
         else:
             store = DictKVStoreBackend()  # unused: ipc_push never stages
         self.store = store
-        self.connector = KVConnector(cfg, "producer", f"prefill-{args.global_rank}", store,
+        self.connector = KVConnector(cfg, "producer", f"prefill-{args.global_rank}-r{self.tp.rank}", store,
                                      export=args.backend != "ipc_push")
         self.connector.register_model_runner(self.runner)
         self.engine = PrefillEngine(cfg, None, self.runner, self.connector)
@@ -122,20 +199,24 @@ class PrefillWorker:
         self.peer_pools = {}     # decode work dir -> opened pool (ipc_push)
         self.seq_idx = 0
         self.processed = set()
-        self.wd.write_json("worker_ready.json", {"pid": os.getpid(), "role": "prefill", "time": time.time()})
+        self.ctl.barrier()
+        if self.ctl.leader:
+            self.wd.write_json("worker_ready.json", {"pid": os.getpid(), "role": "prefill", "tp": self.tp.size,
+                                                     "time": time.time()})
 
     def state(self, busy: bool) -> dict:
         queued = len([p for p in self.wd.glob("*.request.json") if p.name not in self.processed])
         return {"role": "prefill", "busy": busy, "queue_depth": queued, "pending_sends": len(self.pending_sends),
-                "time": time.time()}
+                "tp": self.tp.size, "time": time.time()}
 
     # ------------------------------------------------------------- ipc push
     def _peer_pool(self, dwd: WorkDir):
         key = str(dwd.path)
         if key not in self.peer_pools:
-            if not dwd.wait_for("kv_pool.json", self.args.handshake_timeout_s):
-                raise TimeoutError(f"decode worker {key} never published its KV pool")
-            info = dwd.read_json("kv_pool.json")
+            name = rank_name("kv_pool.json", self.tp)  # this rank's counterpart in the decode group
+            if not dwd.wait_for(name, self.args.handshake_timeout_s):
+                raise TimeoutError(f"decode worker {key} never published its KV pool ({name})")
+            info = dwd.read_json(name)
             from ...ops._ext import load
             C = load()
             raw = bytes.fromhex(info["handle"])
@@ -158,8 +239,9 @@ class PrefillWorker:
         src = torch.as_tensor(meta.src_block_table, dtype=torch.int32, device=r.device)
         dsti = torch.as_tensor(dst, dtype=torch.int32, device=r.device)
         C.kv_push(r.kv_cache, src, dsti, int(ptr) + offset, int(info["num_blocks"]))
-        torch.cuda.synchronize(r.device)
-        dwd.write_json(f"{base}.push_done", {"time": time.time()})
+        if r.is_cuda:
+            torch.cuda.synchronize(r.device)
+        dwd.write_json(rank_name(f"{base}.push_done", self.tp), {"time": time.time()})
 
     # ------------------------------------------------------------- requests
     def finalize_pending_sends(self, block: bool = False) -> None:
@@ -175,11 +257,12 @@ class PrefillWorker:
                 keep.append((state, base, dwd, metrics))
         self.pending_sends = keep
 
-    def process_request(self, path: Path) -> None:
-        base = path.name[:-len(".request.json")]
-        req = json.loads(path.read_text())
+    def process_request(self, base: str, req: dict) -> None:
+        """Run on every rank of the group (the command came from rank 0)."""
+        leader = self.ctl.leader
         dwd = WorkDir(req.get("decode_work_dir") or self.args.work_dir)
         t0 = time.time()
+        payload, metrics, err = None, None, None
         try:
             if self.args.backend == "sync_gpu":
                 self.store.set_peer_rank(int(req["dst_rank"]))
@@ -196,12 +279,21 @@ class PrefillWorker:
             t1 = time.time()
             metrics = {"request_id": payload.request_id, "prefill_time_s": t1 - t0, "first_token": payload.token_ids[-1],
                        "num_prompt_tokens": payload.num_prompt_tokens, "prefill_start_time": t0,
-                       "prefix_cache_hit": payload.prefix_cache_hit, "prefix_cached_tokens": payload.prefix_cached_tokens}
-            dwd.write_pickle(f"{base}.payload.pkl", payload)
+                       "prefix_cache_hit": payload.prefix_cache_hit, "prefix_cached_tokens": payload.prefix_cached_tokens,
+                       "tp": self.tp.size}
+            dwd.write_pickle(rank_name(f"{base}.payload.pkl", self.tp), payload)
             metrics["payload_write_time_s"] = time.time() - t1
+        except Exception as e:
+            err = e
+        if not self.ctl.all_ok(err is None):
+            if leader:
+                _error(dwd, base, "prefill", err or RuntimeError("a peer rank of the prefill group failed"))
+            return
+        try:
             if payload.finished or self.args.backend == "shared_memory":
-                dwd.write_json(f"{base}.prefill_metrics.json", metrics)
-                dwd.touch(f"{base}.prefill_done")
+                if leader:
+                    dwd.write_json(f"{base}.prefill_metrics.json", metrics)
+                    dwd.touch(f"{base}.prefill_done")
             elif self.args.backend == "sync_gpu":
                 dwd.touch(f"{base}.payload_ready")
                 tw = time.time()
@@ -214,34 +306,60 @@ class PrefillWorker:
                 metrics["send_submit_time_s"] = time.time() - ts
                 self.pending_sends.append((st, base, dwd, metrics))
             else:
-                dwd.touch(f"{base}.payload_ready")
+                if leader:
+                    dwd.touch(f"{base}.payload_ready")  # every rank's payload file is written
                 tw = time.time()
                 self._push(payload, dwd, base)
                 metrics["push_time_s"] = time.time() - tw
+        except Exception as e:
+            err = e
+        if self.args.backend != "ipc_push" or payload.finished:
+            if err is not None:
+                _error(dwd, base, "prefill", err)
+            return
+        ok = self.ctl.all_ok(err is None)
+        if leader:
+            if ok:
                 dwd.write_json(f"{base}.prefill_metrics.json", metrics)
                 dwd.touch(f"{base}.prefill_done")
-        except Exception as e:  # keep serving
-            _error(dwd, base, "prefill", e)
-        finally:
+            else:
+                _error(dwd, base, "prefill", err or RuntimeError("a peer rank of the prefill group failed to push"))
+
+    def _next_command(self, idle_since: float, max_idle_s) -> dict:
+        """Rank 0: what the group does next."""
+        self.finalize_pending_sends()
+        for path in self.wd.glob("*.request.json"):
+            if path.name in self.processed:
+                continue
+            base = path.name[:-len(".request.json")]
             self.processed.add(path.name)
+            try:
+                req = json.loads(path.read_text())
+            except Exception as e:
+                _error(self.wd, base, "prefill", e)
+                path.unlink(missing_ok=True)
+                continue
             path.unlink(missing_ok=True)
+            self.wd.write_json("worker_state.json", self.state(True))
+            return {"op": "prefill", "base": base, "req": req}
+        self.wd.write_json("worker_state.json", self.state(False))
+        if self.wd.shutdown_requested():
+            return {"op": "stop"}
+        if max_idle_s is not None and time.time() - idle_since > max_idle_s:
+            return {"op": "stop"}
+        return {"op": "idle"}
 
     def serve(self, max_idle_s: float | None = None) -> None:
         idle_since = time.time()
         while True:
-            self.finalize_pending_sends()
-            reqs = [p for p in self.wd.glob("*.request.json") if p.name not in self.processed]
-            if reqs:
-                self.wd.write_json("worker_state.json", self.state(True))
-                self.process_request(reqs[0])
+            cmd = self.ctl.sync(self._next_command(idle_since, max_idle_s) if self.ctl.leader else None)
+            if cmd["op"] == "prefill":
+                self.process_request(cmd["base"], cmd["req"])
                 idle_since = time.time()
-                continue
-            self.wd.write_json("worker_state.json", self.state(False))
-            if self.wd.shutdown_requested():
+            elif cmd["op"] == "stop":
                 break
-            if max_idle_s is not None and time.time() - idle_since > max_idle_s:
-                break
-            time.sleep(self.args.poll_s)
+            else:
+                time.sleep(self.args.poll_s)
         self.finalize_pending_sends(block=True)
         self.shutdown()
 
@@ -255,19 +373,28 @@ class PrefillWorker:
                 except RuntimeError:
                     pass
         self.runner.release_graphs()
-        if self.args.backend == "sync_gpu" and self.args.world_size > 1:
-            import torch.distributed as dist
-            if dist.is_initialized():
-                dist.destroy_process_group()
+        _close_worlds(self)
+
+
+def _close_worlds(worker) -> None:
+    import torch.distributed as dist
+    if worker.tp.size > 1 and worker.runner.comm is not None:
+        worker.runner.comm.close()
+    if dist.is_initialized() and (worker.tp.size > 1 or (worker.args.backend == "sync_gpu" and worker.args.world_size > 1)):
+        dist.destroy_process_group()
 
 
 # ======================================================================== decode
 class DecodeWorker:
     def __init__(self, args):
         self.args = args
+        if args.tp > 1 and args.backend == "sync_gpu":
+            raise ValueError("sync_gpu needs one NCCL world across P and D: use ipc_push or shared_memory with --tp")
         self.wd = WorkDir(args.work_dir)
         init_world(args)
         self.runner = build_runner(args, kv_pool_ipc=args.backend == "ipc_push")
+        self.tp = self.runner.tp
+        self.ctl = GroupControl(self.tp)
         cfg = self.runner.config
         if args.backend == "shared_memory":
             store = SharedMemoryKVStoreBackend()
@@ -276,30 +403,36 @@ class DecodeWorker:
         else:
             store = DictKVStoreBackend()
         self.store = store
-        self.connector = KVConnector(cfg, "consumer", f"decode-{args.global_rank}", store)
+        self.connector = KVConnector(cfg, "consumer", f"decode-{args.global_rank}-r{self.tp.rank}", store)
         self.connector.register_model_runner(self.runner)
         self.engine = DecodeEngine(cfg, None, self.runner, self.connector)
         self.pending_recvs = {}   # base -> (state, payload)
-        self.pending_push = {}    # base -> (payload, seq blocks)
+        self.pending_push = {}    # base -> (payload, seq blocks, t0)
         self.active_bases = {}    # request_id -> (base, start time, restore_s)
         self.seen = set()
         if args.backend == "ipc_push":
             self._export_pool()
-        self.wd.write_json("worker_ready.json", {"pid": os.getpid(), "role": "decode", "time": time.time()})
+        self.ctl.barrier()
+        if self.ctl.leader:
+            self.wd.write_json("worker_ready.json", {"pid": os.getpid(), "role": "decode", "tp": self.tp.size,
+                                                     "time": time.time()})
 
     def _export_pool(self) -> None:
         r = self.runner
         handle = r.export_kv_pool()
-        self.wd.write_json("kv_pool.json", {"handle": handle.hex(), "num_blocks": r.num_blocks,
-                                            "dtype": str(r.kv_cache.dtype), "shape": list(r.kv_cache.shape)})
+        self.wd.write_json(rank_name("kv_pool.json", self.tp), {
+            "handle": handle.hex(), "num_blocks": r.num_blocks, "dtype": str(r.kv_cache.dtype),
+            "shape": list(r.kv_cache.shape)})
 
     def state(self) -> dict:
         return {"role": "decode", "busy": bool(self.engine.scheduler.running), "active": len(self.engine.active),
                 "pending_recvs": len(self.pending_recvs), "pending_push": len(self.pending_push),
-                "time": time.time()}
+                "tp": self.tp.size, "time": time.time()}
 
     def _finish(self, req) -> None:
         base, t_start, restore_s = self.active_bases.pop(req.request_id)
+        if not self.ctl.leader:
+            return
         seq = req.seq
         self.wd.write_json(f"{base}.decode_metrics.json", {
             "request_id": req.request_id, "output_ids": seq.completion_token_ids,
@@ -309,16 +442,19 @@ class DecodeWorker:
         self.wd.touch(f"{base}.decode_done")
 
     def _admit(self, base: str) -> None:
-        payload = self.wd.read_pickle(f"{base}.payload.pkl")
+        """Every rank: read this rank's payload and start receiving or restoring it."""
+        payload = self.wd.read_pickle(rank_name(f"{base}.payload.pkl", self.tp))
         if payload.finished:
-            self.wd.write_json(f"{base}.decode_metrics.json", {"request_id": payload.request_id,
-                                                               "output_ids": payload.token_ids[payload.num_prompt_tokens:],
-                                                               "decode_step_tokens": [], "finish_time": time.time()})
-            self.wd.touch(f"{base}.decode_done")
+            if self.ctl.leader:
+                self.wd.write_json(f"{base}.decode_metrics.json", {
+                    "request_id": payload.request_id, "output_ids": payload.token_ids[payload.num_prompt_tokens:],
+                    "decode_step_tokens": [], "finish_time": time.time()})
+                self.wd.touch(f"{base}.decode_done")
             return
         t0 = time.time()
         if self.args.backend == "shared_memory":
-            req = self.engine.restore_active_payload(payload, str(self.wd.f(f"{base}.payload.pkl")))
+            path = str(self.wd.f(rank_name(f"{base}.payload.pkl", self.tp)))
+            req = self.engine.restore_active_payload(payload, path)
             self.active_bases[req.request_id] = (base, t0, time.time() - t0)
         elif self.args.backend == "sync_gpu":
             self.wd.touch(f"{base}.recv_ready")  # before posting the receive
@@ -331,81 +467,131 @@ class DecodeWorker:
             self.pending_recvs[base] = (st, payload, t0)
         else:
             n = payload.transfer_meta.num_kv_blocks
-            blocks = self.runner.block_manager.allocate_block(n)
-            self.wd.write_json(f"{base}.recv_ready", {"dst_block_ids": blocks})
+            blocks = self.runner.block_manager.allocate_block(n)  # identical on every rank
+            if self.ctl.leader:
+                self.wd.write_json(f"{base}.recv_ready", {"dst_block_ids": blocks})
             self.pending_push[base] = (payload, blocks, t0)
 
-    def _poll_transfers(self) -> None:
-        for base, (st, payload, t0) in list(self.pending_recvs.items()):
-            if self.store.transfer_done(st):
-                item = self.store.finish_recv(st)
-                req = self.engine.restore_active_payload_from_kv_item(payload, item)
-                self.active_bases[req.request_id] = (base, t0, time.time() - t0)
-                del self.pending_recvs[base]
-        for base, (payload, blocks, t0) in list(self.pending_push.items()):
-            if self.wd.exists(f"{base}.push_done"):
-                seq = self.engine._new_sequence(payload)
-                seq.block_table = blocks
-                self.engine._restore_block_manager_meta(seq)
-                self.engine.scheduler.running.append(seq)
-                from ..decode_engine import ActiveDecodeRequest
-                req = ActiveDecodeRequest(payload.request_id, seq, time.time() - t0)
-                self.engine.active[payload.request_id] = req
-                self.active_bases[req.request_id] = (base, t0, time.time() - t0)
-                del self.pending_push[base]
+    def _restore_pushed(self, base: str) -> None:
+        payload, blocks, t0 = self.pending_push.pop(base)
+        seq = self.engine._new_sequence(payload)
+        seq.block_table = blocks
+        self.engine._restore_block_manager_meta(seq)
+        self.engine.scheduler.running.append(seq)
+        from ..decode_engine import ActiveDecodeRequest
+        req = ActiveDecodeRequest(payload.request_id, seq, time.time() - t0)
+        self.engine.active[payload.request_id] = req
+        self.active_bases[req.request_id] = (base, t0, time.time() - t0)
+
+    def _leader_ops(self, idle_since: float, max_idle_s) -> list:
+        """Rank 0: the operations the group applies this iteration, in order."""
+        ops = []
+        marker = "prefill_done" if self.args.backend == "shared_memory" else "payload_ready"
+        names = [p.name[:-len(f".{marker}")] for p in self.wd.glob(f"*.{marker}")]
+        if marker != "prefill_done":
+            # a request that finished on the prefill side arrives as prefill_done only
+            names += [p.name[:-len(".prefill_done")] for p in self.wd.glob("*.prefill_done")
+                      if self.wd.exists(p.name[:-len(".prefill_done")] + ".payload.pkl")
+                      or self.wd.exists(p.name[:-len(".prefill_done")] + ".payload.rank0.pkl")]
+        for base in names:
+            if base not in self.seen:
+                self.seen.add(base)
+                ops.append(("admit", base))
+        for base, (payload, blocks, t0) in self.pending_push.items():
+            done = [self.wd.exists(self._push_done_name(base, r)) for r in range(self.tp.size)]
+            if all(done):
+                ops.append(("pushed", base))
             elif time.time() - t0 > self.args.handshake_timeout_s:
-                self.runner.block_manager.free_blocks(blocks)
-                del self.pending_push[base]
+                ops.append(("push_timeout", base))
+        for base, (st, payload, t0) in self.pending_recvs.items():
+            if self.store.transfer_done(st):
+                ops.append(("received", base))
+        busy = bool(self.engine.scheduler.running) or any(o[0] in ("admit", "pushed", "received") for o in ops)
+        if not busy and not ops:
+            if self.wd.shutdown_requested() and not self.pending_recvs and not self.pending_push:
+                ops.append(("stop",))
+            elif max_idle_s is not None and time.time() - idle_since > max_idle_s:
+                ops.append(("stop",))
+        return ops
+
+    def _push_done_name(self, base: str, rank: int) -> str:
+        return rank_file(f"{base}.push_done", rank, self.tp.size)
+
+    def _apply(self, op) -> bool:
+        """Every rank applies one operation; returns False on stop."""
+        kind, base = op[0], (op[1] if len(op) > 1 else None)
+        if kind == "stop":
+            return False
+        if kind == "admit":
+            err = None
+            try:
+                self._admit(base)
+            except Exception as e:
+                err = e
+            if not self.ctl.all_ok(err is None):
+                self._drop(base)
+                if self.ctl.leader:
+                    _error(self.wd, base, "decode", err or RuntimeError("a peer rank of the decode group failed"))
+        elif kind == "pushed":
+            self._restore_pushed(base)
+        elif kind == "push_timeout":
+            payload, blocks, _ = self.pending_push.pop(base)
+            self.runner.block_manager.free_blocks(blocks)
+            if self.ctl.leader:
                 _error(self.wd, base, "decode", TimeoutError("prefill worker never pushed the KV"))
+        elif kind == "received":
+            st, payload, t0 = self.pending_recvs.pop(base)
+            item = self.store.finish_recv(st)
+            req = self.engine.restore_active_payload_from_kv_item(payload, item)
+            self.active_bases[req.request_id] = (base, t0, time.time() - t0)
+        return True
+
+    def _drop(self, base: str) -> None:
+        """Undo a partial admission on this rank (another rank failed)."""
+        if base in self.pending_push:
+            _, blocks, _ = self.pending_push.pop(base)
+            self.runner.block_manager.free_blocks(blocks)
+        for rid, (b, _, _) in list(self.active_bases.items()):
+            if b == base:
+                self.engine.abort_by_request_id(rid)
+                self.active_bases.pop(rid, None)
+
+    def _decode_step(self) -> None:
+        err = None
+        try:
+            self.engine.continuous_step()
+        except Exception as e:
+            err = e
+        if not self.ctl.all_ok(err is None):
+            for rid, (base, _, _) in list(self.active_bases.items()):
+                if self.ctl.leader:
+                    _error(self.wd, base, "decode", err or RuntimeError("a peer rank of the decode group failed"))
+                self.engine.abort_by_request_id(rid)
+                self.active_bases.pop(rid, None)
+        for req in list(self.engine.finished_active):
+            self._finish(req)
+        self.engine.finished_active.clear()
 
     def serve(self, max_idle_s: float | None = None) -> None:
         idle_since = time.time()
-        marker = "prefill_done" if self.args.backend == "shared_memory" else "payload_ready"
-        while True:
-            for p in self.wd.glob(f"*.{marker}"):
-                base = p.name[:-len(f".{marker}")]
-                if base in self.seen:
-                    continue
-                self.seen.add(base)
-                try:
-                    self._admit(base)
-                except Exception as e:
-                    _error(self.wd, base, "decode", e)
-            # a request that finished on the prefill side arrives as prefill_done only
-            if marker != "prefill_done":
-                for p in self.wd.glob("*.prefill_done"):
-                    base = p.name[:-len(".prefill_done")]
-                    if base not in self.seen and self.wd.exists(f"{base}.payload.pkl"):
-                        self.seen.add(base)
-                        try:
-                            self._admit(base)
-                        except Exception as e:
-                            _error(self.wd, base, "decode", e)
-            self._poll_transfers()
-            if self.engine.scheduler.running:
-                try:
-                    self.engine.continuous_step()
-                except Exception as e:
-                    for rid, (base, _, _) in list(self.active_bases.items()):
-                        _error(self.wd, base, "decode", e)
-                        self.engine.abort_by_request_id(rid)
-                        self.active_bases.pop(rid, None)
-                for req in list(self.engine.finished_active):
-                    self._finish(req)
-                self.engine.finished_active.clear()
+        running = True
+        while running:
+            ops = self.ctl.sync(self._leader_ops(idle_since, max_idle_s) if self.ctl.leader else None)
+            for op in ops:
+                if not self._apply(op):
+                    running = False
+                    break
+            if not running:
+                break
+            if self.engine.scheduler.running:  # identical on every rank
+                self._decode_step()
                 idle_since = time.time()
-            else:
-                if self.wd.shutdown_requested() and not self.pending_recvs and not self.pending_push:
-                    break
-                if max_idle_s is not None and time.time() - idle_since > max_idle_s:
-                    break
+            elif not ops:
                 time.sleep(self.args.poll_s)
-            self.wd.write_json("worker_state.json", self.state())
+            if self.ctl.leader:
+                self.wd.write_json("worker_state.json", self.state())
         self.runner.release_graphs()
-        if self.args.backend == "sync_gpu" and self.args.world_size > 1:
-            import torch.distributed as dist
-            if dist.is_initialized():
-                dist.destroy_process_group()
+        _close_worlds(self)
 
 
 def main(role: str, argv=None) -> None:

@@ -103,3 +103,25 @@ def test_control_socket_roundtrip(tmp_path):
     assert control_socket_path("/" + "x" * 200).startswith("/tmp/")
     with pytest.raises(TimeoutError):
         connect_control(str(tmp_path / "nobody.sock"), timeout_s=0.2)
+
+
+def test_pool_tp2_groups_match_monolithic(tmp_path):
+    # a prefill group and a decode group, each TP=2 (gloo on CPU, one torchrun per group):
+    # rank 0 of each group drives the work directory, the other rank follows in lockstep,
+    # and every rank hands its own KV-head shard over shared memory
+    rows = _rows()
+    ref = LLM("tiny", device="cpu", dtype="fp32", block_size=16, num_blocks=64, max_model_len=256)
+    want = {r["id"]: ref.generate([r["prompt_ids"]], SamplingParams(temperature=0, max_tokens=r["max_tokens"],
+                                                                    ignore_eos=True))[0][len(r["prompt_ids"]):]
+            for r in rows}
+    pool = PDPool(tmp_path, 1, 1, "shared_memory", "tiny", worker_args=ARGS, handshake_timeout_s=120, tp=2,
+                  device_kind="cpu", nccl_port=29740)
+    pool.start(ready_timeout_s=300)
+    try:
+        summary = pool.run(rows, concurrency=2, timeout_s=300)
+    finally:
+        pool.shutdown()
+    assert summary["num_errors"] == 0, pool.results
+    got = {pool.submitted[b]["row"]["id"]: r["output_ids"] for b, r in pool.results.items()}
+    assert got == want
+    assert json.loads((tmp_path / "decode_0" / "worker_ready.json").read_text())["tp"] == 2
