@@ -366,13 +366,40 @@ __global__ void kv_push_kernel(const uint4* __restrict__ src, uint4* __restrict_
   for (int64_t v = threadIdx.x; v < block_vec; v += blockDim.x) dp[v] = sp[v];
 }
 
+// Same copy for blocks whose size is a multiple of 4 bytes only (the per-block fp8 scales
+// of a few KV heads): one 4-byte word per thread.
+__global__ void kv_push_words_kernel(const uint32_t* __restrict__ src, uint32_t* __restrict__ dst,
+                                     const int* __restrict__ src_ids, const int* __restrict__ dst_ids, int n, int planes,
+                                     int nb_src, int nb_dst, int block_words) {
+  const int64_t total = (int64_t)n * planes * block_words;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int w = (int)(t % block_words);
+    const int64_t r = t / block_words;
+    const int i = (int)(r % n), plane = (int)(r / n);
+    const int s = src_ids[i], d = dst_ids[i];
+    if (s < 0 || s >= nb_src || d < 0 || d >= nb_dst) {
+      atomicCAS(&g_comm_error, 0, 201);
+      continue;
+    }
+    dst[((int64_t)plane * nb_dst + d) * block_words + w] = src[((int64_t)plane * nb_src + s) * block_words + w];
+  }
+}
+
 cudaError_t launch_kv_push(const void* src_pool, void* dst_pool, const int* src_ids, const int* dst_ids, int n,
                            int planes, int nb_src, int nb_dst, int64_t block_bytes, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
-  if (block_bytes % 16 || ((uintptr_t)src_pool & 15) || ((uintptr_t)dst_pool & 15)) return cudaErrorInvalidValue;
-  dim3 grid(n, planes);
-  kv_push_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4*>(src_pool), static_cast<uint4*>(dst_pool), src_ids,
-                                           dst_ids, nb_src, nb_dst, block_bytes / 16);
+  if (block_bytes % 16 == 0 && !((uintptr_t)src_pool & 15) && !((uintptr_t)dst_pool & 15)) {
+    dim3 grid(n, planes);
+    kv_push_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4*>(src_pool), static_cast<uint4*>(dst_pool),
+                                             src_ids, dst_ids, nb_src, nb_dst, block_bytes / 16);
+    return cudaGetLastError();
+  }
+  if (block_bytes % 4 || ((uintptr_t)src_pool & 3) || ((uintptr_t)dst_pool & 3)) return cudaErrorInvalidValue;
+  const int64_t total = (int64_t)n * planes * (block_bytes / 4);
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  kv_push_words_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint32_t*>(src_pool),
+                                                   static_cast<uint32_t*>(dst_pool), src_ids, dst_ids, n, planes,
+                                                   nb_src, nb_dst, (int)(block_bytes / 4));
   return cudaGetLastError();
 }
 

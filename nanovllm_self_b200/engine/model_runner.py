@@ -137,21 +137,30 @@ class ModelRunner:
         m, c = self.model, self.config
         shape = (2, m.num_layers, self.num_blocks, m.num_kv_heads, self.block_size, m.head_dim)
         self._kv_ipc = None
+        scale_shape = (2, m.num_layers, self.num_blocks, m.num_kv_heads)
+        self._scale_off = 0
         if c.kv_pool_ipc and self.is_cuda:
+            # one IPC allocation: the pool, then (fp8) its per-block scales at a 256-byte offset,
+            # so a peer's push kernel reaches both through one handle
             from ..ops._ext import load
             from ..parallel.symm import _DevPtr
             C = load()
             nbytes = int(np.prod(shape)) * torch.empty(0, dtype=c.kv_cache_dtype).element_size()
-            ptr, handle = C.symm_alloc(nbytes)
+            self._scale_off = (nbytes + 255) // 256 * 256
+            total = self._scale_off + (int(np.prod(scale_shape)) * 4 if c.kv_cache_quant_mode == "fp8" else 0)
+            ptr, handle = C.symm_alloc(total)
             self._kv_ipc = (C, ptr, handle)
-            raw = torch.as_tensor(_DevPtr(ptr, nbytes), device=self.device)
-            self.kv_cache = raw.view(c.kv_cache_dtype).view(shape)
+            raw = torch.as_tensor(_DevPtr(ptr, total), device=self.device)
+            self.kv_cache = raw[:nbytes].view(c.kv_cache_dtype).view(shape)
+            if c.kv_cache_quant_mode == "fp8":
+                self.kv_scale_cache = raw[self._scale_off:total].view(torch.float32).view(scale_shape)
+                self.kv_scale_cache.fill_(1.0)
         else:
             self.kv_cache = torch.zeros(shape, dtype=c.kv_cache_dtype, device=self.device)
-        self.kv_scale_cache = None
-        if c.kv_cache_quant_mode == "fp8":
-            self.kv_scale_cache = torch.ones(2, m.num_layers, self.num_blocks, m.num_kv_heads,
-                                             dtype=torch.float32, device=self.device)
+        if not (c.kv_pool_ipc and self.is_cuda and c.kv_cache_quant_mode == "fp8"):
+            self.kv_scale_cache = None
+        if c.kv_cache_quant_mode == "fp8" and self.kv_scale_cache is None:
+            self.kv_scale_cache = torch.ones(scale_shape, dtype=torch.float32, device=self.device)
         elif c.kv_cache_quant_mode == "int8_mock":
             self.kv_scale_cache = torch.ones(2, m.num_layers, self.num_blocks, m.num_kv_heads, self.block_size,
                                              dtype=torch.float32, device=self.device)
@@ -168,6 +177,11 @@ class ModelRunner:
         if self._kv_ipc is None:
             raise RuntimeError("the KV pool was not allocated for IPC (set kv_pool_ipc=True)")
         return bytes(self._kv_ipc[2]) + (0).to_bytes(8, "little")
+
+    @property
+    def kv_scale_offset(self) -> int:
+        """Byte offset of the fp8 scales inside the exported allocation (0: no scales)."""
+        return self._scale_off if self.kv_scale_cache is not None and self._kv_ipc is not None else 0
 
     def _alloc_staging(self):
         c = self.config

@@ -239,6 +239,10 @@ class PrefillWorker:
         src = torch.as_tensor(meta.src_block_table, dtype=torch.int32, device=r.device)
         dsti = torch.as_tensor(dst, dtype=torch.int32, device=r.device)
         C.kv_push(r.kv_cache, src, dsti, int(ptr) + offset, int(info["num_blocks"]))
+        if r.kv_scale_cache is not None and r.config.kv_cache_quant_mode == "fp8":
+            if not info.get("scale_offset"):
+                raise ValueError("fp8 KV needs the decode pool's scales in the exported allocation")
+            C.kv_push(r.kv_scale_cache, src, dsti, int(ptr) + int(info["scale_offset"]), int(info["num_blocks"]))
         if r.is_cuda:
             torch.cuda.synchronize(r.device)
         dwd.write_json(rank_name(f"{base}.push_done", self.tp), {"time": time.time()})
@@ -422,7 +426,7 @@ class DecodeWorker:
         handle = r.export_kv_pool()
         self.wd.write_json(rank_name("kv_pool.json", self.tp), {
             "handle": handle.hex(), "num_blocks": r.num_blocks, "dtype": str(r.kv_cache.dtype),
-            "shape": list(r.kv_cache.shape)})
+            "shape": list(r.kv_cache.shape), "scale_offset": r.kv_scale_offset})
 
     def state(self) -> dict:
         return {"role": "decode", "busy": bool(self.engine.scheduler.running), "active": len(self.engine.active),

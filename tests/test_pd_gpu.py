@@ -58,3 +58,26 @@ def test_pd_pool_two_gpus(tmp_path, backend):
     assert s["num_errors"] == 0, pool.results
     got = {pool.submitted[b]["row"]["id"]: r["output_ids"] for b, r in pool.results.items()}
     assert _agree(got, want) > 0.9
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_pd_pool_ipc_push_fp8_kv(tmp_path):
+    # fp8 KV: the push kernel moves the e4m3 blocks and their per-block scales (which live in
+    # the same exported allocation); decode must agree with a monolithic fp8 engine
+    from nanovllm_self_b200.pd.multiprocess.pool import PDPool
+    llm = LLM("tiny-gpu", device="cuda:0", kv_cache_quant_mode="fp8", **KW)
+    want = {r["id"]: llm.generate([r["prompt_ids"]], SamplingParams(temperature=0, max_tokens=r["max_tokens"],
+                                                                     ignore_eos=True))[0][len(r["prompt_ids"]):]
+            for r in _rows()}
+    args = ["--max-model-len", "1024", "--block-size", "16", "--num-blocks", "128", "--max-num-seqs", "16",
+            "--kv-cache-quant-mode", "fp8"]
+    pool = PDPool(tmp_path, 1, 1, "ipc_push", "tiny-gpu", prefill_devices=["cuda:0"], decode_devices=["cuda:1"],
+                  worker_args=args, handshake_timeout_s=60, nccl_port=29761)
+    pool.start()
+    try:
+        s = pool.run(_rows(), concurrency=2, timeout_s=300)
+    finally:
+        pool.shutdown()
+    assert s["num_errors"] == 0, pool.results
+    got = {pool.submitted[b]["row"]["id"]: r["output_ids"] for b, r in pool.results.items()}
+    assert _agree(got, want) > 0.9
