@@ -34,7 +34,11 @@ __device__ int g_comm_error = 0;
 
 namespace {
 
-constexpr uint64_t COMM_WAIT_NS = 10000000000ull;  // 10 s: ranks may autotune GEMMs at different speeds
+constexpr uint64_t COMM_WAIT_NS = 10000000000ull;  // default 10 s: ranks may autotune GEMMs at different speeds
+
+__device__ __forceinline__ uint64_t wait_budget(const CommArgs& a) {
+  return a.timeout_ns ? a.timeout_ns : COMM_WAIT_NS;
+}
 
 __device__ __forceinline__ uint64_t comm_timer() {
   uint64_t t;
@@ -72,7 +76,7 @@ __device__ bool rank_exchange(const CommArgs& a, size_t flags_off, uint32_t epoc
   const uint64_t t0 = comm_timer();
   for (int p = 0; p < a.world; ++p) {
     while (!reached(ld_relaxed_sys(mine + p), epoch)) {
-      if (comm_timer() - t0 > COMM_WAIT_NS) {
+      if (comm_timer() - t0 > wait_budget(a)) {
         atomicCAS(&g_comm_error, 0, code);
         fence_acq_rel_sys();
         return false;
@@ -98,7 +102,7 @@ __device__ bool rank_entry_barrier(const CommArgs& a, size_t flags_off, uint32_t
   }
   const uint64_t t0 = comm_timer();
   while (!reached(ld_acquire_gpu(ctrl + 1), epoch)) {
-    if (comm_timer() - t0 > COMM_WAIT_NS) {
+    if (comm_timer() - t0 > wait_budget(a)) {
       atomicCAS(&g_comm_error, 0, 111);
       return false;
     }

@@ -28,6 +28,7 @@ struct CommArgs {
   uint32_t* flags[COMM_MAX_RANKS];
   const __nv_bfloat16* weight;
   int rank, world, rows, hidden, ctas, has_residual;
+  uint64_t timeout_ns;                 // bound of every peer wait (0: the default, 10 s)
   float eps;
 };
 

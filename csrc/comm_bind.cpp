@@ -35,7 +35,7 @@ void symm_free(int64_t p) { check(nvb::symm_free(reinterpret_cast<void*>(p)), "s
 void allreduce_add_rmsnorm(std::vector<int64_t> bases, int64_t in_off, int64_t res_off, int64_t out_off,
                            int64_t flag_off, const at::Tensor& weight, int64_t rank,
                            int64_t rows, int64_t hidden, bool has_residual, double eps, int64_t ctas,
-                           bool oneshot) {
+                           bool oneshot, int64_t timeout_ns) {
   TORCH_CHECK((int)bases.size() <= nvb::COMM_MAX_RANKS, "too many ranks");
   TORCH_CHECK(weight.scalar_type() == at::kBFloat16 && weight.is_contiguous(), "weight bf16");
   nvb::CommArgs a;
@@ -54,6 +54,7 @@ void allreduce_add_rmsnorm(std::vector<int64_t> bases, int64_t in_off, int64_t r
   a.hidden = (int)hidden;
   a.ctas = (int)ctas;
   a.has_residual = has_residual ? 1 : 0;
+  a.timeout_ns = (uint64_t)(timeout_ns > 0 ? timeout_ns : 0);
   a.eps = (float)eps;
   at::cuda::CUDAGuard g(weight.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
@@ -89,7 +90,8 @@ void register_comm(pybind11::module& m) {
   m.def("allreduce_add_rmsnorm", &allreduce_add_rmsnorm, pybind11::arg("bases"), pybind11::arg("in_off"),
         pybind11::arg("res_off"), pybind11::arg("out_off"), pybind11::arg("flag_off"),
         pybind11::arg("weight"), pybind11::arg("rank"), pybind11::arg("rows"), pybind11::arg("hidden"),
-        pybind11::arg("has_residual"), pybind11::arg("eps"), pybind11::arg("ctas"), pybind11::arg("oneshot") = false);
+        pybind11::arg("has_residual"), pybind11::arg("eps"), pybind11::arg("ctas"), pybind11::arg("oneshot") = false,
+        pybind11::arg("timeout_ns") = 0);
   m.def("comm_error", &comm_error, pybind11::arg("reset") = false);
   m.def("kv_push", &kv_push);
   m.attr("COMM_FLAG_BYTES") = (int64_t)nvb::COMM_FLAG_BYTES;

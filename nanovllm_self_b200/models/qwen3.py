@@ -110,6 +110,8 @@ class Qwen3ForCausalLM:
         """Run embedding + all layers; returns (h, residual) before the final norm."""
         ops = self.ops
         T = input_ids.shape[0]
+        if self.comm is not None and self.tp_size > 1:
+            self.comm.begin_forward()
         h = ops.embedding(input_ids, self.embed, self.vocab_start)
         residual = None
         nq, nkv, d = self.num_heads, self.num_kv_heads, self.head_dim
@@ -135,7 +137,7 @@ class Qwen3ForCausalLM:
         if self.comm is not None and self.tp_size > 1:
             hs = h.index_select(0, logits_indices)
             rs = residual.index_select(0, logits_indices)
-            x, _ = self.comm.allreduce_add_rmsnorm(hs, rs, self.norm, self.eps)
+            x, _ = self.comm.allreduce_add_rmsnorm(hs, rs, self.norm, self.eps, final=True)
         else:
             x, _ = ops.add_rmsnorm_rows(h, residual, self.norm, self.eps, logits_indices)
         return ops.linear(x, self.lm_head)

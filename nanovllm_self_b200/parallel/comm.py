@@ -52,9 +52,14 @@ class TPComm:
             return self.symm.input_buffer(T)
         return None
 
-    def allreduce_add_rmsnorm(self, h, residual, w, eps):
+    def begin_forward(self) -> None:
+        if self.symm is not None:
+            self.symm.begin_forward()
+
+    def allreduce_add_rmsnorm(self, h, residual, w, eps, final: bool = False):
+        """``final``: the last reduction of a forward (the final norm before the lm_head)."""
         if self.symm is not None and h.shape[0] <= self.symm.rows:
-            return self.symm.allreduce_add_rmsnorm(h, residual, w, eps, self.ops)
+            return self.symm.allreduce_add_rmsnorm(h, residual, w, eps, self.ops, final=final)
         dist.all_reduce(h, op=dist.ReduceOp.SUM, group=self.tp.group)
         return self.ops.add_rmsnorm(h, residual, w, eps)
 

@@ -28,8 +28,11 @@ class SymmetricWorkspace:
     # stay below this; beyond it the two-shot kernel moves 2 (world - 1) / world of that
     ONESHOT_PEER_BYTES = 4 << 20
 
-    def __init__(self, tp, rows: int, hidden: int, oneshot_rows: int | None = None):
+    def __init__(self, tp, rows: int, hidden: int, oneshot_rows: int | None = None, timeout_s: float = 10.0):
         self.C = load()
+        # bound of every peer wait inside the kernels; on expiry they record an error word
+        # (``error()``) and return instead of waiting for ever
+        self.timeout_ns = int(timeout_s * 1e9)
         self.tp = tp
         self.rows = rows
         self.hidden = hidden
@@ -70,25 +73,37 @@ class SymmetricWorkspace:
         self.IN1 = [view(o, min(rows, oneshot_rows)) for o in self.in1_off]
         self.RES = view(self.res_off, rows)
         self.OUT = view(self.out_off, rows)
-        self._k = 0  # position in the one-shot IN rotation
+        # One-shot IN buffers: the layers' reductions of a forward alternate between buffers 0
+        # and 1 (reset at every forward), the forward's last reduction (the final norm) uses
+        # buffer 2.  So two consecutive reductions never share a buffer, inside a forward or
+        # across the boundary of two forwards (CUDA-graph replays repeat the same sequence):
+        # a rank then refills a buffer only after a barrier that every peer passed after its
+        # reads of that buffer (the protocol model in the tests checks this).
+        self._k = 0
         dist.barrier(group=tp.group)
 
     def _oneshot(self, T: int) -> bool:
         return T <= self.oneshot_rows
 
-    def input_buffer(self, T: int) -> torch.Tensor:
+    def begin_forward(self) -> None:
+        self._k = 0
+
+    def _slot(self, final: bool) -> int:
+        return 2 if final else self._k % 2
+
+    def input_buffer(self, T: int, final: bool = False) -> torch.Tensor:
         """Where the next reduction's input should be written (the GEMM writes straight here)."""
         if self._oneshot(T):
-            return self.IN1[self._k % 3][:T]
+            return self.IN1[self._slot(final)][:T]
         return self.IN[:T]
 
-    def allreduce_add_rmsnorm(self, h, residual, w, eps, ops=None):
+    def allreduce_add_rmsnorm(self, h, residual, w, eps, ops=None, final: bool = False):
         T = h.shape[0]
         if T > self.rows:
             raise ValueError(f"{T} rows exceed the symmetric workspace ({self.rows})")
         one = self._oneshot(T)
-        inv = self.input_buffer(T)
-        in_off = self.in1_off[self._k % 3] if one else self.in_off
+        inv = self.input_buffer(T, final)
+        in_off = self.in1_off[self._slot(final)] if one else self.in_off
         if h.data_ptr() != inv.data_ptr():
             inv.copy_(h)
         res = self.RES[:T]
@@ -100,8 +115,8 @@ class SymmetricWorkspace:
         else:
             ctas = max(1, min(self.max_ctas, (T + self.tp.size - 1) // self.tp.size))
         self.C.allreduce_add_rmsnorm(self.bases, in_off, self.res_off, self.out_off, self.flag_off,
-                                     w, self.tp.rank, T, self.hidden, has_res, float(eps), ctas, one)
-        if one:
+                                     w, self.tp.rank, T, self.hidden, has_res, float(eps), ctas, one, self.timeout_ns)
+        if one and not final:
             self._k += 1
         if ops is not None and hasattr(ops, "launches"):
             ops.launches += 1

@@ -83,3 +83,51 @@ def test_tp2_fused_matches_nccl_and_tp1(tmp_path):
     agree = sum(a == b for x, y in zip(res["fused"]["out"], res["nccl"]["out"]) for a, b in zip(x, y))
     total = sum(len(x) for x in res["fused"]["out"])
     assert agree / total > 0.9
+
+
+def _timeout_worker(rank, world, port, out_path):
+    # A peer that never arrives: rank 1 skips one all-reduce (it decides so on the host and
+    # waits there).  Rank 0's kernel must give up after its 1 s bound, record the error word
+    # and return, leaving the context usable; nothing faults or hangs.
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import time
+    import torch.distributed as dist
+    from nanovllm_self_b200.ops.cuda_ops import CudaOps
+    from nanovllm_self_b200.parallel.state import init_tensor_parallel
+    from nanovllm_self_b200.parallel.symm import SymmetricWorkspace
+    tp = init_tensor_parallel(world, "cuda")
+    ops = CudaOps()
+    symm = SymmetricWorkspace(tp, rows=64, hidden=256, timeout_s=1.0)
+    w = torch.ones(256, device=tp.device, dtype=torch.bfloat16)
+    h = symm.input_buffer(8)
+    h.fill_(1.0)
+    out, _ = symm.allreduce_add_rmsnorm(h, None, w, 1e-6, ops)  # both ranks: completes
+    torch.cuda.synchronize()
+    ok_first = symm.error() == 0 and bool(torch.isfinite(out.float()).all())
+    dist.barrier()
+    res = None
+    if rank == 0:
+        h = symm.input_buffer(8)
+        h.fill_(1.0)
+        t0 = time.time()
+        symm.allreduce_add_rmsnorm(h, None, w, 1e-6, ops)  # rank 1 never joins this call
+        torch.cuda.synchronize()
+        res = {"elapsed_s": time.time() - t0, "err": symm.error(reset=True), "ok_first": ok_first}
+        x = torch.ones(4, device=tp.device) * 3  # the context still runs work
+        res["after"] = float(x.sum().item())
+        torch.save(res, out_path)
+    dist.barrier()
+    symm.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_allreduce_peer_timeout_reports_error(tmp_path):
+    out = tmp_path / "timeout.pt"
+    mp.spawn(_timeout_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    res = torch.load(out)
+    assert res["ok_first"]
+    assert res["err"] == 110          # the entry barrier of the one-shot kernel gave up
+    assert 0.8 < res["elapsed_s"] < 10.0
+    assert res["after"] == 12.0
