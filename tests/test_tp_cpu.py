@@ -40,7 +40,9 @@ def _worker(rank, world, port, out_path, temperature):
         json.dump(out, f)
     import torch.distributed as dist
     dist.barrier()
-    dist.destroy_process_group()
+    # leave without tearing the gloo group down: its destructor can race with its own
+    # threads at interpreter exit (std::terminate), which is a harness artefact, not a result
+    os._exit(0)
 
 
 @pytest.mark.parametrize("temperature", [0.0, 0.9])
