@@ -100,9 +100,11 @@ __device__ bool rank_entry_barrier(const CommArgs& a, size_t flags_off, uint32_t
     st_release_gpu(ctrl + 1, epoch);
     return ok;
   }
+  // twice CTA 0's budget: when the peers fail to arrive, CTA 0 gives up first, records why
+  // (110) and releases this CTA through the go word; 111 means CTA 0 itself never got there
   const uint64_t t0 = comm_timer();
   while (!reached(ld_acquire_gpu(ctrl + 1), epoch)) {
-    if (comm_timer() - t0 > wait_budget(a)) {
+    if (comm_timer() - t0 > 2 * wait_budget(a)) {
       atomicCAS(&g_comm_error, 0, 111);
       return false;
     }
