@@ -1,9 +1,12 @@
 """Reference arm of ``bench.py``: the unmodified reference engine on the same workload.
 
 The reference (Xhkkji/nanovllm_self) ships no packaging metadata, so ``pip install`` of
-it fails ("neither setup.py nor pyproject.toml"); its own documentation runs it from the
-source tree on ``PYTHONPATH``.  ``baseline/_ref`` therefore holds an unmodified copy of
-its ``nanovllm`` and ``pd_self`` packages, imported from there.
+its source tree fails ("neither setup.py nor pyproject.toml").  ``install_reference()``
+(run by ``__graft_entry__.build()``) first tries exactly that install into
+``baseline/_ref``; when it fails it copies the tree's ``nanovllm`` and ``pd_self``
+packages, unmodified, to a temporary directory, adds a ``pyproject.toml`` that only names
+those two packages, and runs the same offline ``pip install --target baseline/_ref`` on
+the copy.  The arm then imports the reference from ``baseline/_ref``.
 
 What the harness does around the reference (none of it changes the reference's code):
 
@@ -35,6 +38,63 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 CKPT_ROOT = "/tmp/nvb_ref_ckpt"
+_PYPROJECT = """[build-system]
+requires = ["setuptools"]
+build-backend = "setuptools.build_meta"
+
+[project]
+name = "nanovllm-self-reference"
+version = "0.0.0"
+
+[tool.setuptools.packages.find]
+where = ["."]
+include = ["nanovllm*", "pd_self*"]
+namespaces = true
+"""
+
+
+def reference_source() -> str | None:
+    """The reference's source tree: $NVB_REFERENCE_SRC, else BASELINE.json's reference_path."""
+    src = os.environ.get("NVB_REFERENCE_SRC")
+    if not src:
+        try:
+            with open(os.path.join(ROOT, "BASELINE.json")) as f:
+                src = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            src = None
+    return src if src and os.path.isdir(os.path.join(src, "nanovllm")) else None
+
+
+def install_reference(quiet: bool = True) -> str:
+    """Install the unmodified reference into baseline/_ref (offline); returns what happened.
+
+    Never raises: a machine without the reference tree simply leaves the arm unavailable.
+    """
+    import shutil
+    import subprocess
+    import tempfile
+    if os.path.isdir(os.path.join(REF_DIR, "nanovllm")):
+        return "already installed"
+    src = reference_source()
+    if src is None:
+        return "reference source tree not found"
+    pip = [sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation", "--find-links",
+           "/opt/wheelhouse", "--target", REF_DIR]
+    out = subprocess.DEVNULL if quiet else None
+    try:
+        if subprocess.call(pip + [src], stdout=out, stderr=out, timeout=600) == 0:
+            return f"pip install of {src}"
+        tmp = tempfile.mkdtemp(prefix="nvb_ref_src_")
+        for pkg in ("nanovllm", "pd_self"):
+            shutil.copytree(os.path.join(src, pkg), os.path.join(tmp, pkg),
+                            ignore=shutil.ignore_patterns("__pycache__"))
+        with open(os.path.join(tmp, "pyproject.toml"), "w") as f:
+            f.write(_PYPROJECT)
+        rc = subprocess.call(pip + ["--no-deps", tmp], stdout=out, stderr=out, timeout=600)
+        shutil.rmtree(tmp, ignore_errors=True)
+        return f"pip install of a packaged copy of {src}" if rc == 0 else f"pip install failed (rc={rc})"
+    except (OSError, subprocess.SubprocessError) as e:
+        return f"install failed: {e!r}"
 
 
 def unavailable(reason: str) -> None:
@@ -122,9 +182,10 @@ class StepTimer:
         return ms
 
 
-def run_reference_arm(args, workload, ClockSampler, dist_info, reduce_max, metric, model_names):
+def run_reference_arm(args, workload, step_seed, ClockSampler, dist_info, reduce_max, metric, model_names):
     if not os.path.isdir(os.path.join(REF_DIR, "nanovllm")):
-        unavailable("reference not installed under baseline/_ref (copy of its nanovllm/ and pd_self/ packages)")
+        unavailable("reference not installed under baseline/_ref (build() installs it when the reference source tree "
+                    "is present)")
         return
     import torch
     import torch.distributed as dist
@@ -169,17 +230,22 @@ def run_reference_arm(args, workload, ClockSampler, dist_info, reduce_max, metri
             dist.destroy_process_group()
         return
     timer = StepTimer(llm.model_runner.model, llm.model_runner.sampler)
-    inputs = [torch.tensor(p, dtype=torch.long) for p in prompts]
     sps = [RefSP(temperature=0.0, max_tokens=o, ignore_eos=True) for o in outs]
+
+    def step_inputs(phase, i):
+        ps = workload(args.num_requests, arch.vocab_size, token_seed=step_seed(phase, i))[0]
+        return ps, [torch.tensor(p, dtype=torch.long) for p in ps]
+
     try:
-        for _ in range(args.warmup):
-            llm.generate(inputs, sps)
+        for i in range(args.warmup):
+            llm.generate(step_inputs("warmup", i)[1], sps)
     except Exception as e:
         if rank == 0:
             unavailable(f"reference generate failed: {e!r}"[:300])
         if world > 1 and dist.is_initialized():
             dist.destroy_process_group()
         return
+    timed = [step_inputs("timed", i) for i in range(args.steps)]
     timer.take_ms()
     if world > 1:
         dist.barrier()
@@ -189,11 +255,11 @@ def run_reference_arm(args, workload, ClockSampler, dist_info, reduce_max, metri
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     gen = 0
-    for _ in range(args.steps):
+    for step_prompts, inputs in timed:
         # return_metrics=True raises in this reference snapshot (it reads a
         # ``prefill_backend`` attribute its PagedAttention no longer has), so count here
         outs_ids = llm.generate(inputs, sps)
-        gen += sum(len(o) - len(p) for o, p in zip(outs_ids, prompts))
+        gen += sum(len(o) - len(p) for o, p in zip(outs_ids, step_prompts))
     ev1.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -215,6 +281,8 @@ def run_reference_arm(args, workload, ClockSampler, dist_info, reduce_max, metri
                        "kv_cache": "bf16", "num_blocks": ref_engine.config.num_blocks,
                        "attention_backend": "flash_attn (reference default)",
                        "l2": "no flush: each step streams the full weights (>> 126 MB L2)",
+                       "prompts": "fresh token ids every warm-up and timed step (same lengths)",
+                       "reference_dir": REF_DIR,
                        "step": "one LLM_self.generate over all requests"},
             "generated_tokens_per_step": gen // max(args.steps, 1), "clocks": clk,
             "e2e": {"value": round(gen / (wall_max / 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": h2d,

@@ -5,7 +5,9 @@ output lengths uniform in [100, 1024], uniform-random prompt token ids, greedy,
 ignore_eos; paged KV with block 256; CUDA-graph decode buckets.
 
 One "step" is one complete ``LLM.generate`` over the 256 requests (prefill + decode
-until every request finishes).  W warm-up steps, then exactly K timed steps bracketed
+until every request finishes).  Every warm-up and timed step draws fresh prompt token
+ids (same lengths), so no prefill is served from the prefix cache; the JSON line
+reports the timed prefix-cache hits (``prefix_hit_blocks_timed``, expected 0).  W warm-up steps, then exactly K timed steps bracketed
 by a barrier and ``torch.cuda.synchronize()`` on both sides.
 
 * ``value``: generated tokens / summed device time of the engine steps (CUDA events
@@ -38,13 +40,24 @@ METRIC = "output tok/s (device-timed, max over ranks) Qwen3-8B TP1/2/4/8; p50 TT
 MODEL_NAMES = {"qwen3-8b": "Qwen3-8B", "qwen3-0.6b": "Qwen3-0.6B", "qwen3-32b": "Qwen3-32B"}
 
 
-def workload(n: int, vocab: int, seed: int = 0, in_range=(100, 1024), out_range=(100, 1024)):
+def workload(n: int, vocab: int, seed: int = 0, in_range=(100, 1024), out_range=(100, 1024), token_seed=None):
+    """`n` requests: lengths drawn from `seed`, prompt token ids from `token_seed` (default `seed`).
+
+    Every benchmark step passes its own `token_seed`, so no step repeats another step's prompts
+    and no prefill is served from the prefix cache; the lengths, and so the work, stay the same.
+    """
     import numpy as np
     rng = np.random.default_rng(seed)
     ins = rng.integers(in_range[0], in_range[1] + 1, size=n)
     outs = rng.integers(out_range[0], out_range[1] + 1, size=n)
-    prompts = [rng.integers(0, vocab, size=int(l)).tolist() for l in ins]
+    trng = rng if token_seed is None else np.random.default_rng([seed, int(token_seed)])
+    prompts = [trng.integers(0, vocab, size=int(l)).tolist() for l in ins]
     return prompts, [int(o) for o in outs]
+
+
+def step_seed(phase: str, i: int) -> int:
+    """Token seed of warm-up step i ("warmup") or timed step i ("timed"); all distinct."""
+    return (1 if phase == "warmup" else 2) * 100000 + i
 
 
 class ClockSampler:
@@ -135,12 +148,15 @@ def run_ours(args):
               max_num_seqs=256, max_num_batched_tokens=16384, block_size=256, cuda_graph_max_bs=512,
               kv_cache_quant_mode=kv_mode, comm_backend=args.comm)
     vocab = llm.model_runner.arch.vocab_size
-    prompts, outs = workload(args.num_requests, vocab)
+    _, outs = workload(args.num_requests, vocab)
     sps = [SamplingParams(temperature=0.0, max_tokens=o, ignore_eos=True) for o in outs]
-    for _ in range(args.warmup):
-        llm.generate(prompts, sps)
+    for i in range(args.warmup):
+        llm.generate(workload(args.num_requests, vocab, token_seed=step_seed("warmup", i))[0], sps)
+    timed_prompts = [workload(args.num_requests, vocab, token_seed=step_seed("timed", i))[0]
+                     for i in range(args.steps)]
     runner = llm.model_runner
     ops = runner.ops
+    bm = llm.block_manager
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -148,13 +164,14 @@ def run_ours(args):
     clocks.start()
     launches0 = getattr(ops, "launches", 0) + (llm.comm.launches if llm.comm is not None else 0)
     h2d0, d2h0 = runner.h2d_bytes, runner.d2h_bytes
+    hits0 = bm.num_prefix_hit_blocks
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     dev_ms = 0.0
     gen = 0
     steps_engine = 0
     ttft, tpot = [], []
-    for _ in range(args.steps):
+    for prompts in timed_prompts:
         res = llm.generate(prompts, sps, return_metrics=True)
         m = res["metrics"]
         dev_ms += m["total_time_s"] * 1e3
@@ -170,6 +187,7 @@ def run_ours(args):
     clk = clocks.stop()
     launches = getattr(ops, "launches", 0) + (llm.comm.launches if llm.comm is not None else 0) - launches0
     h2d, d2h = runner.h2d_bytes - h2d0, runner.d2h_bytes - d2h0
+    prefix_hits = bm.num_prefix_hit_blocks - hits0
     dev_max, wall_max = reduce_max([dev_ms, wall_ms], world, device)
     llm.shutdown()
     if rank == 0:
@@ -185,8 +203,10 @@ def run_ours(args):
                        "parallelism": f"tp{args.gpus}", "kv_cache": args.kv, "comm_backend": args.comm,
                        "block_size": 256, "cuda_graph_buckets": "1,2,4,8,16..256",
                        "l2": "no flush: each step streams the full weights (>> 126 MB L2)",
+                       "prompts": "fresh token ids every warm-up and timed step (same lengths)",
                        "step": "one LLM.generate over all requests", "engine_steps_per_step": steps_engine
                        // max(args.steps, 1)},
+            "prefix_hit_blocks_timed": int(prefix_hits),
             "generated_tokens_per_step": gen // max(args.steps, 1),
             "ttft_ms_p50": round(sum(ttft) / len(ttft), 3), "tpot_ms_p50": round(sum(tpot) / len(tpot), 3),
             "clocks": clk,
@@ -203,7 +223,7 @@ def run_ours(args):
 
 def run_reference(args):
     from baseline_ref import run_reference_arm  # noqa: WPS433 (kept beside bench.py)
-    run_reference_arm(args, workload, ClockSampler, dist_info, reduce_max, METRIC, MODEL_NAMES)
+    run_reference_arm(args, workload, step_seed, ClockSampler, dist_info, reduce_max, METRIC, MODEL_NAMES)
 
 
 def main():

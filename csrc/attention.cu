@@ -816,7 +816,11 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
   float L = 0.f, O = 0.f;
   if (M != -INFINITY) {
     for (int s = 0; s < splits; ++s) {
-      float w = exp2f(part_lse[base + s] - M);
+      // An empty split (no keys) writes only its -inf log-sum-exp, never its output row:
+      // skip it, so stale scratch (possibly NaN) never meets a zero weight.
+      const float lse = part_lse[base + s];
+      if (lse == -INFINITY) continue;
+      const float w = exp2f(lse - M);
       L += w;
       O += w * part_o[(base + s) * AD + threadIdx.x];
     }
@@ -1081,25 +1085,19 @@ cudaError_t launch_attn_decode(const AttnLaunch& L, cudaStream_t stream) {
   const int sm = decode_tma_smem(L.kv_fp8, L.nq / L.nkv);
   const int sm_max = decode_tma_smem(L.kv_fp8, 16);
   if (L.kv_fp8 && L.nq / L.nkv <= 8 && L.block_size >= 16) {
-    static bool cfg = false;
-    if (!cfg) {
-      cudaFuncSetAttribute(attn_decode_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_fp8_smem(8));
-      cfg = true;
-    }
+    static std::atomic<uint64_t> done{0};
+    cudaError_t e = smem_opt_in(done, attn_decode_fp8_kernel, decode_fp8_smem(8));
+    if (e != cudaSuccess) return e;
     launch_pdl(attn_decode_fp8_kernel, grid, dim3(160), decode_fp8_smem(L.nq / L.nkv), stream, km, vm, da);
   } else if (L.kv_fp8) {
-    static bool cfg = false;
-    if (!cfg) {
-      cudaFuncSetAttribute(attn_decode_tma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_max);
-      cfg = true;
-    }
+    static std::atomic<uint64_t> done{0};
+    cudaError_t e = smem_opt_in(done, attn_decode_tma_kernel<true>, sm_max);
+    if (e != cudaSuccess) return e;
     launch_pdl(attn_decode_tma_kernel<true>, grid, dim3(160), sm, stream, km, vm, da);
   } else {
-    static bool cfg = false;
-    if (!cfg) {
-      cudaFuncSetAttribute(attn_decode_tma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_max);
-      cfg = true;
-    }
+    static std::atomic<uint64_t> done{0};
+    cudaError_t e = smem_opt_in(done, attn_decode_tma_kernel<false>, sm_max);
+    if (e != cudaSuccess) return e;
     launch_pdl(attn_decode_tma_kernel<false>, grid, dim3(160), sm, stream, km, vm, da);
   }
   NVB_LAUNCH_CHECK();
@@ -1147,10 +1145,14 @@ cudaError_t launch_attn_prefill(const AttnLaunch& L, int max_q_len, cudaStream_t
   dim3 grid((max_q_len + 63) / 64, L.num_seqs, L.nq);
   int sm = prefill_smem(L.kv_fp8);
   if (L.kv_fp8) {
-    cudaFuncSetAttribute(attn_prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    static std::atomic<uint64_t> done{0};
+    cudaError_t e = smem_opt_in(done, attn_prefill_kernel<true>, sm);
+    if (e != cudaSuccess) return e;
     launch_pdl(attn_prefill_kernel<true>, grid, dim3(128), sm, stream, a);
   } else {
-    cudaFuncSetAttribute(attn_prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    static std::atomic<uint64_t> done{0};
+    cudaError_t e = smem_opt_in(done, attn_prefill_kernel<false>, sm);
+    if (e != cudaSuccess) return e;
     launch_pdl(attn_prefill_kernel<false>, grid, dim3(128), sm, stream, a);
   }
   NVB_LAUNCH_CHECK();

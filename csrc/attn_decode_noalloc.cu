@@ -15,8 +15,11 @@
 //   * a call needs num_seqs * nq * splits rows; larger requests are rejected with
 //     cudaErrorInvalidValue before anything is launched (lower `splits`, or split the
 //     batch into several calls);
-//   * nothing in the scratch has to start at zero: each call writes every row it later
-//     reads, so stale contents from an earlier call are never observed;
+//   * nothing in the scratch has to start at zero.  Every row of the partial log-sum-exps a
+//     call reads is written by that call; a split that gets no keys writes only its
+//     log-sum-exp (-inf), and the combine step skips such splits without reading their
+//     partial-output rows, so stale contents from an earlier call (NaN included) never
+//     reach the output;
 //   * all calls share the one array per device.  Two calls whose kernels may overlap on
 //     the GPU (different streams without ordering between them) race on it; order them
 //     on one stream, or with events;
@@ -25,10 +28,12 @@
 //     That first call per device should therefore happen before any stream capture;
 //   * no cudaMalloc, cudaFree or allocating library routine is called.
 //
-// Inputs are the same as launch_attn_decode's (see kernels.h); the caller passes the
-// output buffer.  Returns a cudaError_t value (0 on success).
+// The C declarations are in attn_decode_noalloc.h.  Inputs are the same as
+// launch_attn_decode's (kernels.h); the caller passes the output buffer.  Returns a
+// cudaError_t value (0 on success).
 #include <mutex>
 
+#include "attn_decode_noalloc.h"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -70,6 +75,13 @@ extern "C" __attribute__((visibility("default"))) int nvb_attn_decode_noalloc(
     float softmax_scale, cudaStream_t stream) {
   if (num_seqs <= 0) return (int)cudaSuccess;
   if (head_dim != NOALLOC_HEAD_DIM || splits < 1) return (int)cudaErrorInvalidValue;
+  // checked here, before any division by nkv or launch
+  if (nq <= 0 || nkv <= 0 || nq % nkv || nq / nkv > 16) return (int)cudaErrorInvalidValue;
+  if (block_size <= 0 || (block_size & (block_size - 1)) || num_blocks <= 0 || block_table_width <= 0)
+    return (int)cudaErrorInvalidValue;
+  if (!q || !k_cache || !v_cache || !block_tables || !cu_seqlens_q || !context_lens || !out)
+    return (int)cudaErrorInvalidValue;
+  if (kv_fp8 && (!k_scale || !v_scale)) return (int)cudaErrorInvalidValue;
   if ((long long)num_seqs * nq * splits > NOALLOC_MAX_ROWS) return (int)cudaErrorInvalidValue;
   float* scratch = nullptr;
   cudaError_t e = scratch_ptr(&scratch);
@@ -101,4 +113,4 @@ extern "C" __attribute__((visibility("default"))) int nvb_attn_decode_noalloc(
 }
 
 // Largest num_seqs * nq * splits one call may use.
-extern "C" __attribute__((visibility("default"))) int nvb_attn_decode_noalloc_max_rows() { return NOALLOC_MAX_ROWS; }
+extern "C" __attribute__((visibility("default"))) int nvb_attn_decode_noalloc_max_rows(void) { return NOALLOC_MAX_ROWS; }

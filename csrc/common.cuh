@@ -5,6 +5,8 @@
 #include <cuda_fp8.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace nvb {
 
 constexpr unsigned FULL_MASK = 0xffffffffu;
@@ -98,6 +100,34 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Runs `set_up` (kernel attribute calls such as the dynamic shared-memory opt-in) once per
+// device.  Kernel attributes belong to one device, so a process that launches on several GPUs
+// has to set them on each; `done` is a bitmask of the devices already set up, owned by the
+// caller (one per kernel).  Devices numbered 64 and above are set up on every call.  Two
+// threads may both run `set_up` for the same device; the calls are idempotent.
+template <typename F>
+inline cudaError_t once_per_device(std::atomic<uint64_t>& done, F&& set_up) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev >= 0 && dev < 64 ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = set_up();
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+// Opt `kern` in to `bytes` of dynamic shared memory on the current device (once per device).
+template <typename K>
+inline cudaError_t smem_opt_in(std::atomic<uint64_t>& done, K kern, int bytes, bool nonportable_cluster = false) {
+  return once_per_device(done, [&]() -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && nonportable_cluster)
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    return e;
+  });
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

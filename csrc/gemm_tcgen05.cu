@@ -809,14 +809,9 @@ cudaError_t run_cluster(const CUtensorMap& mp, const CUtensorMap& mq, const Para
   constexpr int STAGES = stages_for<BN>();
   constexpr int SMEM = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
   auto kern = gemm_cluster_kernel<BN, STAGES>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> done{0};  // per template instance: devices already opted in
+  cudaError_t e = smem_opt_in(done, kern, SMEM, /*nonportable_cluster=*/true);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(prm.tiles_p * prm.tiles_q * prm.splits, 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
@@ -839,12 +834,9 @@ cudaError_t run(const CUtensorMap& mp, const CUtensorMap& mq, const Params& prm,
   constexpr int STAGES = stages_for<BN, MT>();
   constexpr int SMEM = STAGES * (MT * BM * BK * 2 + BN * BK * 2) + 1024 + 256;
   auto kern = gemm_kernel<BN, STAGES, MT>;
-  static bool configured = false;  // per template instance; the attribute is process-wide
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> done{0};  // per template instance: devices already opted in
+  cudaError_t e = smem_opt_in(done, kern, SMEM);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
@@ -1317,20 +1309,14 @@ cudaError_t run_dec(const DecCfg& d, const void* x, int64_t ldx, const void* w, 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  static bool configured[3] = {false, false, false};
+  static std::atomic<uint64_t> done[3];  // devices already opted in, per MMA row-tile count
   if (d.mt == 2) {
-    if (!configured[2]) {
-      cudaError_t e = cudaFuncSetAttribute(gemm_dec_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM_MAX);
-      if (e != cudaSuccess) return e;
-      configured[2] = true;
-    }
+    cudaError_t e = smem_opt_in(done[2], gemm_dec_kernel<2>, DEC_SMEM_MAX);
+    if (e != cudaSuccess) return e;
     return cudaLaunchKernelEx(&cfg, gemm_dec_kernel<2>, mx, mw, p);
   }
-  if (!configured[1]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_dec_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM_MAX);
-    if (e != cudaSuccess) return e;
-    configured[1] = true;
-  }
+  cudaError_t e = smem_opt_in(done[1], gemm_dec_kernel<1>, DEC_SMEM_MAX);
+  if (e != cudaSuccess) return e;
   return cudaLaunchKernelEx(&cfg, gemm_dec_kernel<1>, mx, mw, p);
 }
 
