@@ -67,16 +67,15 @@ __device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
 // Wraparound-safe "flag has reached call e".
 __device__ __forceinline__ bool reached(uint32_t v, uint32_t e) { return (int32_t)(v - e) >= 0; }
 
-// Cross-rank part of a per-rank barrier (one thread): publish call number `epoch` in slot
-// `flags_off` of every rank, then wait until every rank published it (or a later one) here.
-__device__ bool rank_exchange(const CommArgs& a, size_t flags_off, uint32_t epoch, int code) {
-  fence_acq_rel_sys();
-  for (int p = 0; p < a.world; ++p) st_relaxed_sys(a.flags[p] + flags_off + a.rank, epoch);
-  const uint32_t* mine = a.flags[a.rank] + flags_off;
+// Wait (one thread) until every rank's word in slot `flags_off` of this rank's flags has
+// reached call number `epoch`; false (after recording `code`) when `budget_ns` runs out.
+__device__ bool wait_all_flags(uint32_t* const* flags, int rank, int world, size_t flags_off, uint32_t epoch,
+                               uint64_t budget_ns, int code) {
+  const uint32_t* mine = flags[rank] + flags_off;
   const uint64_t t0 = comm_timer();
-  for (int p = 0; p < a.world; ++p) {
+  for (int p = 0; p < world; ++p) {
     while (!reached(ld_relaxed_sys(mine + p), epoch)) {
-      if (comm_timer() - t0 > wait_budget(a)) {
+      if (comm_timer() - t0 > budget_ns) {
         atomicCAS(&g_comm_error, 0, code);
         fence_acq_rel_sys();
         return false;
@@ -85,6 +84,19 @@ __device__ bool rank_exchange(const CommArgs& a, size_t flags_off, uint32_t epoc
   }
   fence_acq_rel_sys();
   return true;
+}
+
+// Cross-rank part of a per-rank barrier (one thread): publish call number `epoch` in slot
+// `flags_off` of every rank, then wait until every rank published it (or a later one) here.
+__device__ bool rank_exchange_raw(uint32_t* const* flags, int rank, int world, size_t flags_off, uint32_t epoch,
+                                  uint64_t budget_ns, int code) {
+  fence_acq_rel_sys();
+  for (int p = 0; p < world; ++p) st_relaxed_sys(flags[p] + flags_off + rank, epoch);
+  return wait_all_flags(flags, rank, world, flags_off, epoch, budget_ns, code);
+}
+
+__device__ bool rank_exchange(const CommArgs& a, size_t flags_off, uint32_t epoch, int code) {
+  return rank_exchange_raw(a.flags, a.rank, a.world, flags_off, epoch, wait_budget(a), code);
 }
 
 // Entry barrier (thread 0 of each CTA): every CTA reads this call's number from the local
@@ -320,7 +332,134 @@ __global__ void __launch_bounds__(256) allreduce_oneshot_kernel(CommArgs a) {
   if (threadIdx.x == 0) rank_exit(a, s_epoch, false, true);
 }
 
+
+// Owner side of the GEMM -> reduce-scatter path (see RsNormArgs in comm.h).  Every CTA waits
+// on this rank's RS flags itself (local polling), so no CTA waits on another before the rows.
+template <int NI>
+__global__ void __launch_bounds__(256) rs_add_rmsnorm_ag_kernel(RsNormArgs a) {
+  pdl_wait();     // the reduce-scatter GEMM before this kernel has completed on this rank
+  pdl_trigger();  // the next kernel may start its prologue (its loads wait for this grid)
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_ok;
+  __shared__ float red[32];
+  uint32_t* ctrl = a.flags[a.rank] + COMM_CTRL;
+  const uint64_t budget = a.timeout_ns ? a.timeout_ns : COMM_WAIT_NS;
+  if (threadIdx.x == 0) {
+    const uint32_t e = ld_acquire_gpu(ctrl) + 1;
+    s_epoch = e;
+    s_ok = wait_all_flags(a.flags, a.rank, a.world, COMM_RS_FLAGS, e, budget, 120) ? 1 : 0;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  if (s_ok) {
+    const int H = a.hidden;
+    const int nvec = H >> 3;
+    const int r0 = a.rank * a.rs_rows, r1 = min(a.rows, r0 + a.rs_rows);
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int64_t slot = (int64_t)COMM_RS_MAX_ROWS * H;  // elements of one source rank's slot
+    for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
+      const int lr = row - r0;
+      float v[NI][8];
+      float ss = 0.f;
+      uint4 raw[NI][COMM_MAX_RANKS], rres[NI];
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < nvec) {
+#pragma unroll
+          for (int p = 0; p < COMM_MAX_RANKS; ++p)
+            if (p < a.world)  // written by peers over NVLink: bypass L1
+              raw[i][p] = __ldcv(reinterpret_cast<const uint4*>(a.rs + p * slot + (int64_t)lr * H) + c);
+          if (a.has_residual) rres[i] = reinterpret_cast<const uint4*>(a.res + (int64_t)row * H)[c];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < nvec) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+#pragma unroll
+          for (int p = 0; p < COMM_MAX_RANKS; ++p) {
+            if (p < a.world) {
+              float f[8];
+              bf16x8_to_f32(raw[i][p], f);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[i][j] += f[j];
+            }
+          }
+          if (a.has_residual) {
+            float r[8];
+            bf16x8_to_f32(rres[i], r);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i][j] = bf16_round(v[i][j] + r[j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i][j] = bf16_round(v[i][j]);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) red[wid] = ss;
+      __syncthreads();
+      if (wid == 0) {
+        float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
+        t = warp_sum(t);
+        if (lane == 0) red[0] = rsqrtf(t / (float)H + a.eps);
+      }
+      __syncthreads();
+      const float inv = red[0];
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < nvec) {
+          float wf[8], o[8];
+          bf16x8_to_f32(reinterpret_cast<const uint4*>(a.weight)[c], wf);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = v[i][j] * inv * wf[j];
+          reinterpret_cast<uint4*>(a.res + (int64_t)row * H)[c] = f32_to_bf16x8(v[i]);
+          const uint4 ou = f32_to_bf16x8(o);
+          for (int p = 0; p < a.world; ++p) reinterpret_cast<uint4*>(a.out[p] + (int64_t)row * H)[c] = ou;
+        }
+      }
+      __syncthreads();  // red[] is reused by the next row
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // this CTA's OUT stores (peers included) before its arrival; the last CTA of the rank
+    // publishes "my rows are everywhere" and waits until every rank has published it
+    fence_acq_rel_sys();
+    uint32_t prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ctrl + 2) : "memory");
+    if (prev == gridDim.x - 1) {
+      if (s_ok) rank_exchange_raw(a.flags, a.rank, a.world, COMM_AG_FLAGS, epoch, budget, 121);
+      ctrl[2] = 0;
+      st_release_gpu(ctrl, epoch);
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_rs_add_rmsnorm_ag(const RsNormArgs& a, cudaStream_t stream) {
+  if (a.rows == 0) return cudaSuccess;
+  if (a.hidden % 8 || a.hidden > 8 * 256 * 4 || a.world > COMM_MAX_RANKS || a.world < 1 || a.ctas > COMM_MAX_CTAS ||
+      a.ctas < 1 || a.rs_rows < 1 || a.rs_rows > COMM_RS_MAX_ROWS || (int64_t)a.rs_rows * a.world < a.rows)
+    return cudaErrorInvalidValue;
+  const int nvec = a.hidden / 8;
+  const int threads = nvec >= 256 ? 256 : ((nvec + 31) / 32) * 32;
+  const int ni = (nvec + threads - 1) / threads;
+  switch (ni) {
+    case 1: launch_pdl(rs_add_rmsnorm_ag_kernel<1>, dim3(a.ctas), dim3(threads), 0, stream, a); break;
+    case 2: launch_pdl(rs_add_rmsnorm_ag_kernel<2>, dim3(a.ctas), dim3(threads), 0, stream, a); break;
+    case 3: launch_pdl(rs_add_rmsnorm_ag_kernel<3>, dim3(a.ctas), dim3(threads), 0, stream, a); break;
+    default: launch_pdl(rs_add_rmsnorm_ag_kernel<4>, dim3(a.ctas), dim3(threads), 0, stream, a); break;
+  }
+  return cudaGetLastError();
+}
 
 cudaError_t launch_allreduce_oneshot(const CommArgs& a, cudaStream_t stream) {
   if (a.rows == 0) return cudaSuccess;

@@ -62,6 +62,38 @@ void allreduce_add_rmsnorm(std::vector<int64_t> bases, int64_t in_off, int64_t r
         "allreduce_add_rmsnorm");
 }
 
+// Owner side of the GEMM -> reduce-scatter path (RsNormArgs): rs_off = this rank's receive
+// area, res_off / out_off / flag_off as in allreduce_add_rmsnorm.
+void rs_add_rmsnorm_ag(std::vector<int64_t> bases, int64_t rs_off, int64_t res_off, int64_t out_off, int64_t flag_off,
+                       const at::Tensor& weight, int64_t rank, int64_t rows, int64_t rs_rows, int64_t hidden,
+                       bool has_residual, double eps, int64_t ctas, int64_t timeout_ns) {
+  TORCH_CHECK((int)bases.size() <= nvb::COMM_MAX_RANKS, "too many ranks");
+  TORCH_CHECK(rank >= 0 && rank < (int64_t)bases.size(), "rank out of range");
+  TORCH_CHECK(weight.scalar_type() == at::kBFloat16 && weight.is_contiguous(), "weight bf16");
+  nvb::RsNormArgs a;
+  std::memset(&a, 0, sizeof(a));
+  for (size_t p = 0; p < bases.size(); ++p) {
+    char* base = reinterpret_cast<char*>(bases[p]);
+    a.out[p] = reinterpret_cast<__nv_bfloat16*>(base + out_off);
+    a.flags[p] = reinterpret_cast<uint32_t*>(base + flag_off);
+  }
+  char* mine = reinterpret_cast<char*>(bases[rank]);
+  a.rs = reinterpret_cast<const __nv_bfloat16*>(mine + rs_off);
+  a.res = reinterpret_cast<__nv_bfloat16*>(mine + res_off);
+  a.weight = reinterpret_cast<const __nv_bfloat16*>(weight.data_ptr());
+  a.rank = (int)rank;
+  a.world = (int)bases.size();
+  a.rows = (int)rows;
+  a.rs_rows = (int)rs_rows;
+  a.hidden = (int)hidden;
+  a.ctas = (int)ctas;
+  a.has_residual = has_residual ? 1 : 0;
+  a.timeout_ns = (uint64_t)(timeout_ns > 0 ? timeout_ns : 0);
+  a.eps = (float)eps;
+  at::cuda::CUDAGuard g(weight.device());
+  check(nvb::launch_rs_add_rmsnorm_ag(a, at::cuda::getCurrentCUDAStream().stream()), "rs_add_rmsnorm_ag");
+}
+
 int64_t comm_error(bool reset) { return nvb::comm_error_code(reset ? 1 : 0); }
 
 // Push blocks of a local KV pool [2, L, NB, ...] into a peer pool (raw pointer, nb_dst blocks).
@@ -92,8 +124,13 @@ void register_comm(pybind11::module& m) {
         pybind11::arg("weight"), pybind11::arg("rank"), pybind11::arg("rows"), pybind11::arg("hidden"),
         pybind11::arg("has_residual"), pybind11::arg("eps"), pybind11::arg("ctas"), pybind11::arg("oneshot") = false,
         pybind11::arg("timeout_ns") = 0);
+  m.def("rs_add_rmsnorm_ag", &rs_add_rmsnorm_ag, pybind11::arg("bases"), pybind11::arg("rs_off"),
+        pybind11::arg("res_off"), pybind11::arg("out_off"), pybind11::arg("flag_off"), pybind11::arg("weight"),
+        pybind11::arg("rank"), pybind11::arg("rows"), pybind11::arg("rs_rows"), pybind11::arg("hidden"),
+        pybind11::arg("has_residual"), pybind11::arg("eps"), pybind11::arg("ctas"), pybind11::arg("timeout_ns") = 0);
   m.def("comm_error", &comm_error, pybind11::arg("reset") = false);
   m.def("kv_push", &kv_push);
   m.attr("COMM_FLAG_BYTES") = (int64_t)nvb::COMM_FLAG_BYTES;
   m.attr("COMM_MAX_CTAS") = (int64_t)nvb::COMM_MAX_CTAS;
+  m.attr("COMM_RS_MAX_ROWS") = (int64_t)nvb::COMM_RS_MAX_ROWS;
 }

@@ -50,6 +50,30 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
                             int k, float* ws, int64_t ws_elems, int* counters, int64_t num_counters,
                             cudaStream_t stream, GemmPlan* chosen, int act = 0);
 
+// Reduce-scatter epilogue of the decode GEMM (tensor parallelism): instead of writing C
+// locally, output row i is stored straight into the memory of the rank that owns it, rank
+// i / rows, at dst[owner] + (i % rows) * ldc (that rank's receive slot for this rank; a peer
+// pointer for every rank but this one).  When every CTA has stored its rows, the last CTA to
+// finish raises this rank's arrival word at every rank: *flag[r] = *calls + 1, the number of
+// the reduction this GEMM feeds.  *ctas_done counts the finished CTAs and is zero between
+// launches (the last CTA resets it).
+struct GemmRsEpilogue {
+  int rows = 0;          // output rows per owner rank (0: plain local output)
+  int world = 0;
+  void* dst[8] = {};     // bf16 [rows][ldc] receive slot per owner rank
+  uint32_t* flag[8] = {};
+  const uint32_t* calls = nullptr;
+  uint32_t* ctas_done = nullptr;
+};
+
+// C[m, n] = X W^T with the reduce-scatter epilogue (decode kernel, m <= 256, k % 64 == 0).
+// The configuration is chosen on first use of a shape by timing the decode-kernel candidates
+// with a plain local output into tune_c[m, n] (row stride tune_ldc; outside stream capture),
+// then cached.  Returns cudaErrorNotSupported for shapes the decode kernel cannot run.
+cudaError_t gemm_bf16_rs(const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t ldc, int m, int n, int k,
+                         const GemmRsEpilogue& rs, void* tune_c, int64_t tune_ldc, cudaStream_t stream,
+                         GemmPlan* chosen);
+
 // Error word written by a GEMM that gave up on a bounded wait (0 = none).
 int gemm_error_code(int reset);
 

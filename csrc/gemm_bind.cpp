@@ -3,6 +3,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "comm.h"
 #include "gemm.h"
 
 namespace {
@@ -110,6 +111,44 @@ void linear_dec_cfg(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, i
   TORCH_CHECK(e == cudaSuccess, "gemm_dec_explicit failed: ", cudaGetErrorString(e));
 }
 
+// Row-parallel GEMM with the reduce-scatter epilogue (tensor parallelism): x @ w^T whose row i
+// is stored into rank i / rs_rows's symmetric receive area (slot `rank`) instead of locally;
+// bases[p] = rank p's symmetric buffer, rs_off / flag_off = byte offsets of the receive area
+// and the flag words in it.  tune_out [m, n] receives the plain output of the candidates timed
+// on the first use of a shape.  Returns (mt, bn, splits) of the decode-kernel plan used.
+std::vector<int64_t> linear_rs(const at::Tensor& x, const at::Tensor& w, std::vector<int64_t> bases, int64_t rs_off,
+                               int64_t flag_off, int64_t rank, int64_t rs_rows, at::Tensor& tune_out) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && tune_out.is_cuda(), "CUDA tensors required");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                  tune_out.scalar_type() == at::kBFloat16, "bf16 required");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1 && tune_out.stride(1) == 1,
+              "2-D tensors with unit inner stride required");
+  const int m = (int)x.size(0), k = (int)x.size(1), n = (int)w.size(0);
+  const int world = (int)bases.size();
+  TORCH_CHECK(w.size(1) == k && tune_out.size(0) >= m && tune_out.size(1) == n, "shape mismatch");
+  TORCH_CHECK(world >= 1 && world <= nvb::COMM_MAX_RANKS && rank >= 0 && rank < world, "bad rank / world");
+  TORCH_CHECK(rs_rows >= 1 && rs_rows <= nvb::COMM_RS_MAX_ROWS && (int64_t)rs_rows * world >= m, "bad rs_rows");
+  nvb::GemmRsEpilogue rs;
+  rs.rows = (int)rs_rows;
+  rs.world = world;
+  const int64_t slot_bytes = (int64_t)nvb::COMM_RS_MAX_ROWS * n * 2;
+  for (int p = 0; p < world; ++p) {
+    char* base = reinterpret_cast<char*>(bases[p]);
+    rs.dst[p] = base + rs_off + rank * slot_bytes;
+    rs.flag[p] = reinterpret_cast<uint32_t*>(base + flag_off) + nvb::COMM_RS_FLAGS + rank;
+  }
+  char* mine = reinterpret_cast<char*>(bases[rank]);
+  rs.calls = reinterpret_cast<const uint32_t*>(mine + flag_off) + nvb::COMM_CTRL;
+  rs.ctas_done = reinterpret_cast<uint32_t*>(mine + flag_off) + nvb::COMM_CTRL_GEMM_DONE;
+  at::cuda::CUDAGuard g(x.device());
+  nvb::GemmPlan pl{};
+  cudaError_t e = nvb::gemm_bf16_rs(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), n, m, n, k, rs,
+                                    tune_out.data_ptr(), tune_out.stride(0),
+                                    at::cuda::getCurrentCUDAStream().stream(), &pl);
+  TORCH_CHECK(e == cudaSuccess, "gemm_bf16_rs failed: ", cudaGetErrorString(e));
+  return {pl.mt, pl.bn, pl.splits};
+}
+
 int64_t error_code(bool reset) { return nvb::gemm_error_code(reset ? 1 : 0); }
 
 }  // namespace
@@ -127,5 +166,6 @@ void register_gemm(pybind11::module& m) {
   m.def("linear_dec", &linear_dec, "decode-sized tcgen05 GEMM with a ranked configuration", pybind11::arg("x"),
         pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("rank"), pybind11::arg("act") = 0);
   m.def("linear_dec_cfg", &linear_dec_cfg, "decode-sized tcgen05 GEMM with an explicit configuration");
+  m.def("linear_rs", &linear_rs, "tcgen05 decode GEMM whose rows are stored at their owner rank (reduce-scatter)");
   m.def("gemm_error", &error_code, pybind11::arg("reset") = false);
 }

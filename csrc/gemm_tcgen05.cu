@@ -919,7 +919,35 @@ struct DecParams {
   uint32_t idesc;
   __nv_bfloat16* c;
   int64_t ldc;
+  GemmRsEpilogue rs;     // rs.rows > 0: reduce-scatter epilogue (rows stored at their owner rank)
 };
+
+// Destination of output row pi: local C, or the owner rank's receive slot for this rank.
+__device__ __forceinline__ __nv_bfloat16* dec_row(const DecParams& p, int pi) {
+  if (p.rs.rows > 0) {
+    const int o = pi / p.rs.rows;
+    return static_cast<__nv_bfloat16*>(p.rs.dst[o]) + (int64_t)(pi - o * p.rs.rows) * p.ldc;
+  }
+  return p.c + (int64_t)pi * p.ldc;
+}
+
+// Reduce-scatter arrival (thread 0 of each CTA, after the CTA's stores): the last CTA of the
+// grid to arrive publishes this rank's arrival word, the reduction's call number, at every
+// rank.  Each CTA's system-scope fence orders its row stores (peer stores included) before
+// its arrival on the local counter; the last CTA's acquire of that counter and its own fence
+// order all of them before the flag stores.
+__device__ __forceinline__ void dec_rs_arrive(const GemmRsEpilogue& rs) {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  uint32_t prev;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(rs.ctas_done) : "memory");
+  if (prev != gridDim.x * gridDim.y * gridDim.z - 1) return;
+  uint32_t calls;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(calls) : "l"(rs.calls) : "memory");
+  *rs.ctas_done = 0;  // the next launch that counts starts after this grid completes
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  for (int r = 0; r < rs.world; ++r)
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(rs.flag[r]), "r"(calls + 1) : "memory");
+}
 
 template <int MT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -1064,10 +1092,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
           if (p.act) {  // bn % 32 == 0 and n % 32 == 0 in this mode
-            act_silu_store(p.c + (int64_t)pi * p.ldc + qj / 2, f);
+            act_silu_store(dec_row(p, pi) + qj / 2, f);
             continue;
           }
-          __nv_bfloat16* dst = p.c + (int64_t)pi * p.ldc + qj;
+          __nv_bfloat16* dst = dec_row(p, pi) + qj;
           if (valid == 32) {
 #pragma unroll
             for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = f32_to_bf16x8(f + j);
@@ -1135,7 +1163,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const float o[4] = {silu_f(g[0]) * u[0], silu_f(g[1]) * u[1], silu_f(g[2]) * u[2],
                                 silu_f(g[3]) * u[3]};
             const int oc = (tq * BN + 32 * (o4 >> 2)) / 2 + 4 * (o4 & 3);
-            *reinterpret_cast<uint2*>(p.c + (int64_t)pi * p.ldc + oc) = f32_to_bf16x4(o);
+            *reinterpret_cast<uint2*>(dec_row(p, pi) + oc) = f32_to_bf16x4(o);
           }
         }
       }
@@ -1175,19 +1203,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (qj >= p.n) continue;
           const int nv = min(4, p.n - qj);
           if (pi < p.m) {
-            if (nv == 4) *reinterpret_cast<uint2*>(p.c + (int64_t)pi * p.ldc + qj) = f32_to_bf16x4(f);
+            if (nv == 4) *reinterpret_cast<uint2*>(dec_row(p, pi) + qj) = f32_to_bf16x4(f);
             else
-              for (int e = 0; e < nv; ++e) p.c[(int64_t)pi * p.ldc + qj + e] = __float2bfloat16(f[e]);
+              for (int e = 0; e < nv; ++e) dec_row(p, pi)[qj + e] = __float2bfloat16(f[e]);
           }
           if (has2 && pi2 < p.m) {
-            if (nv == 4) *reinterpret_cast<uint2*>(p.c + (int64_t)pi2 * p.ldc + qj) = f32_to_bf16x4(g);
+            if (nv == 4) *reinterpret_cast<uint2*>(dec_row(p, pi2) + qj) = f32_to_bf16x4(g);
             else
-              for (int e = 0; e < nv; ++e) p.c[(int64_t)pi2 * p.ldc + qj + e] = __float2bfloat16(g[e]);
+              for (int e = 0; e < nv; ++e) dec_row(p, pi2)[qj + e] = __float2bfloat16(g[e]);
           }
         }
       }
       cluster_sync_all();  // peers may still be reading this CTA's export
     }
+  }
+  if (p.rs.rows > 0) {
+    __syncthreads();  // every row store of this CTA is issued
+    if (threadIdx.x == 0) dec_rs_arrive(p.rs);
   }
   if (warp == 1) {
     tc_fence_after();
@@ -1277,7 +1309,7 @@ std::vector<DecCfg> dec_candidates(int m, int n, int k) {
 }
 
 cudaError_t run_dec(const DecCfg& d, const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc,
-                    int m, int n, int k, cudaStream_t stream, int act = 0) {
+                    int m, int n, int k, cudaStream_t stream, int act = 0, const GemmRsEpilogue* rs = nullptr) {
   if (act && (d.bn % 32 || n % 32)) return cudaErrorInvalidValue;
   CUtensorMap mx, mw;
   if (!make_map(&mx, x, m, k, ldx, BM) || !make_map(&mw, w, n, k, ldw, d.bn)) return cudaErrorInvalidValue;
@@ -1295,6 +1327,14 @@ cudaError_t run_dec(const DecCfg& d, const void* x, int64_t ldx, const void* w, 
   p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(d.bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
   p.c = static_cast<__nv_bfloat16*>(c);
   p.ldc = ldc;
+  if (rs) {
+    if (act || rs->rows <= 0 || rs->world < 1 || rs->world > 8 || !rs->calls || !rs->ctas_done ||
+        (int64_t)rs->rows * rs->world < m || ldc % 8)
+      return cudaErrorInvalidValue;
+    for (int r = 0; r < rs->world; ++r)
+      if (!rs->dst[r] || !rs->flag[r] || ((uintptr_t)rs->dst[r] & 15)) return cudaErrorInvalidValue;
+    p.rs = *rs;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(d.tiles * d.splits, 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
@@ -1621,6 +1661,82 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
   }
   if (chosen) *chosen = best;
   return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, best, ws, counters, stream, act);
+}
+
+cudaError_t gemm_bf16_rs(const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t ldc, int m, int n, int k,
+                         const GemmRsEpilogue& rs, void* tune_c, int64_t tune_ldc, cudaStream_t stream,
+                         GemmPlan* chosen) {
+  if (m == 0 || n == 0) return cudaSuccess;
+  if (m > 2 * BM || k % BK || k % 8 || ldx % 8 || ldw % 8) return cudaErrorNotSupported;
+  if (((uintptr_t)x & 15) || ((uintptr_t)w & 15)) return cudaErrorMisalignedAddress;
+  static std::map<std::tuple<int, int, int>, GemmPlan> cache;  // guarded by tune_mutex()
+  const auto key = std::make_tuple(m, n, k);
+  GemmPlan best{};
+  bool have = false;
+  {
+    std::lock_guard<std::mutex> g(tune_mutex());
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      best = it->second;
+      have = true;
+    }
+  }
+  if (!have) {
+    std::vector<GemmPlan> cands;
+    GemmPlan d;
+    for (int r = 0; cands.size() < 8 && gemm_dec_plan(m, n, k, r, &d); ++r) cands.push_back(d);
+    if (cands.empty()) return cudaErrorNotSupported;
+    best = cands[0];
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(stream, &cap);
+    if (cap == cudaStreamCaptureStatusNone && tune_c && cands.size() > 1) {
+      // time the candidates with a plain local output (the reduce-scatter stores and flags
+      // must only happen once per reduction), each after a 256 MiB read (cold L2)
+      const size_t flush_bytes = (size_t)256 << 20;
+      void* flush = nullptr;
+      if (cudaMalloc(&flush, flush_bytes) != cudaSuccess) {
+        cudaGetLastError();
+        flush = nullptr;
+      }
+      cudaEvent_t e0, e1;
+      cudaEventCreate(&e0);
+      cudaEventCreate(&e1);
+      float best_ms = 1e30f;
+      for (const auto& pl : cands) {
+        DecCfg dc{pl.mt, pl.bn, pl.splits, pl.kb_per_split, pl.stages, pl.a_stages, pl.smem, pl.tiles, 0.0};
+        if (run_dec(dc, x, ldx, w, ldw, tune_c, tune_ldc, m, n, k, stream) != cudaSuccess) {
+          cudaGetLastError();
+          continue;
+        }
+        float total = 0.f;
+        bool good = true;
+        for (int r = 0; r < 3 && good; ++r) {
+          if (flush)
+            l2_evict_kernel<<<num_sms() * 4, 256, 0, stream>>>(static_cast<const uint4*>(flush), flush_bytes / 16 - 16,
+                                                              static_cast<int*>(flush) + (flush_bytes / 4 - 1));
+          cudaEventRecord(e0, stream);
+          good = run_dec(dc, x, ldx, w, ldw, tune_c, tune_ldc, m, n, k, stream) == cudaSuccess;
+          cudaEventRecord(e1, stream);
+          cudaEventSynchronize(e1);
+          float ms = 0.f;
+          cudaEventElapsedTime(&ms, e0, e1);
+          total += ms;
+        }
+        if (good && total < best_ms) {
+          best_ms = total;
+          best = pl;
+        }
+      }
+      cudaEventDestroy(e0);
+      cudaEventDestroy(e1);
+      if (flush) cudaFree(flush);
+      std::lock_guard<std::mutex> g(tune_mutex());
+      cache[key] = best;
+    }
+  }
+  if (chosen) *chosen = best;
+  DecCfg dc{best.mt, best.bn, best.splits, best.kb_per_split, best.stages, best.a_stages, best.smem, best.tiles, 0.0};
+  return run_dec(dc, x, ldx, w, ldw, nullptr, ldc, m, n, k, stream, 0, &rs);
 }
 
 int gemm_error_code(int reset) {

@@ -91,6 +91,10 @@ class EngineConfig:
 
     tensor_parallel_size: int = 1
     comm_backend: str = "fused"
+    # Fused backend, decode-sized steps (<= 256 tokens): the o_proj / down_proj GEMMs store
+    # their output rows at the owner rank (reduce-scatter in the GEMM epilogue) and the owner
+    # normalises and all-gathers.  False: those steps use the all-reduce kernel as well.
+    fused_reduce_scatter: bool = True
     enable_cuda_graph: bool = True
     cuda_graph_max_bs: int = 512
     enable_prefix_cache: bool = True

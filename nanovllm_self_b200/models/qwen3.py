@@ -11,7 +11,10 @@ B200-first layout (not the reference's module-per-projection layout):
   ``[2 I, H]`` weight -> one GEMM whose output feeds the SiLU-and-mul kernel;
 * q/k RMSNorm + RoPE + KV-cache store are one kernel over the QKV GEMM output;
 * residual add + RMSNorm are one kernel; under tensor parallelism that kernel also
-  performs the all-reduce of the row-parallel GEMM output (fused comm backend);
+  performs the all-reduce of the row-parallel GEMM output (fused comm backend), and on
+  decode-sized steps the reduce-scatter half of it moves into the o_proj / down_proj GEMM
+  epilogue (each output row stored at its owner rank), the owner then normalises and
+  all-gathers;
 * the embedding table and lm_head are vocab-parallel under TP (the reference keeps
   full replicas on every rank, ``:255-258,285``);
 * the final norm runs only on the rows that are sampled.
@@ -106,8 +109,18 @@ class Qwen3ForCausalLM:
             return self.comm.allreduce_add_rmsnorm(h, residual, w, self.eps)
         return self.ops.add_rmsnorm(h, residual, w, self.eps)
 
+    def _rs(self, T: int, k: int) -> bool:
+        """Row-parallel GEMMs of this step store their rows at the owner rank (decode steps)."""
+        return self.comm is not None and self.tp_size > 1 and self.comm.rs_ok(T, k)
+
     def forward_hidden(self, input_ids: torch.Tensor, positions: torch.Tensor, ctx, kv_caches, kv_scales=None):
-        """Run embedding + all layers; returns (h, residual) before the final norm."""
+        """Run embedding + all layers.
+
+        Returns (h, residual, normed): with ``normed`` False, h and residual are the last
+        layer's output before the final norm (the final norm then runs on the sampled rows
+        only); with ``normed`` True (tensor-parallel decode steps, whose row-parallel GEMMs
+        reduce-scatter in their epilogue) h already holds the final-normed rows of every token.
+        """
         ops = self.ops
         T = input_ids.shape[0]
         if self.comm is not None and self.tp_size > 1:
@@ -115,26 +128,42 @@ class Qwen3ForCausalLM:
         h = ops.embedding(input_ids, self.embed, self.vocab_start)
         residual = None
         nq, nkv, d = self.num_heads, self.num_kv_heads, self.head_dim
+        rs = self._rs(T, nq * d) and self._rs(T, self.intermediate)
+        n = len(self.layers)
+        x = None
         for i, L in enumerate(self.layers):
-            x, residual = self._reduce_norm(h, residual, L.ln1)
+            if not rs or i == 0:
+                x, residual = self._reduce_norm(h, residual, L.ln1)
             qkv = ops.linear(x, L.qkv)
             kc, vc = kv_caches[i]
             ks, vs = kv_scales[i] if kv_scales is not None else (None, None)
             q = ops.qkv_post(qkv, L.q_norm, L.k_norm, self.eps, positions, self.cos_sin, kc, vc,
                              ctx.slot_mapping, ks, vs, nq, nkv, d)
             o = ops.attention(q, kc, vc, ctx, self.scale, ks, vs)
-            h = ops.linear(o.view(T, nq * d), L.o, out=self._reduce_in(T))
-            x, residual = self._reduce_norm(h, residual, L.ln2)
+            if rs:
+                x, residual = self.comm.linear_rs_norm(o.view(T, nq * d), L.o, L.ln2, self.eps)
+            else:
+                h = ops.linear(o.view(T, nq * d), L.o, out=self._reduce_in(T))
+                x, residual = self._reduce_norm(h, residual, L.ln2)
             a = ops.linear_silu(x, L.gate_up)  # silu(gate) * up, fused into the GEMM epilogue
-            h = ops.linear(a, L.down, out=self._reduce_in(T))
-        return h, residual
+            if rs:
+                # the next layer's ln1, or the final norm after the last layer
+                w_next = self.layers[i + 1].ln1 if i + 1 < n else self.norm
+                x, residual = self.comm.linear_rs_norm(a, L.down, w_next, self.eps)
+            else:
+                h = ops.linear(a, L.down, out=self._reduce_in(T))
+        if rs:
+            return x, residual, True
+        return h, residual, False
 
-    def compute_logits(self, h, residual, logits_indices: torch.Tensor) -> torch.Tensor:
+    def compute_logits(self, h, residual, logits_indices: torch.Tensor, normed: bool = False) -> torch.Tensor:
         """Final norm on the sampled rows only, then the (vocab-parallel) lm_head."""
         ops = self.ops
         if logits_indices.numel() == 0:
             return torch.empty(0, self.vocab_end - self.vocab_start, device=h.device, dtype=torch.float32)
-        if self.comm is not None and self.tp_size > 1:
+        if normed:
+            x = h.index_select(0, logits_indices)
+        elif self.comm is not None and self.tp_size > 1:
             hs = h.index_select(0, logits_indices)
             rs = residual.index_select(0, logits_indices)
             x, _ = self.comm.allreduce_add_rmsnorm(hs, rs, self.norm, self.eps, final=True)
@@ -143,5 +172,5 @@ class Qwen3ForCausalLM:
         return ops.linear(x, self.lm_head)
 
     def forward(self, input_ids, positions, ctx, kv_caches, kv_scales=None):
-        h, residual = self.forward_hidden(input_ids, positions, ctx, kv_caches, kv_scales)
-        return self.compute_logits(h, residual, ctx.logits_indices)
+        h, residual, normed = self.forward_hidden(input_ids, positions, ctx, kv_caches, kv_scales)
+        return self.compute_logits(h, residual, ctx.logits_indices, normed)

@@ -6,6 +6,10 @@ The reference reduces the row-parallel o_proj/down_proj outputs with an in-place
 
 Here every reduction is fused with what follows it:
 
+* ``linear_rs_norm(x, w, w_norm)`` (decode-sized steps): the row-parallel GEMM stores each
+  output row straight into the memory of the rank that owns it (reduce-scatter in the GEMM
+  epilogue, NVLink peer stores); the owner sums the partials, adds the residual,
+  RMS-normalises and all-gathers the rows by peer stores, in one kernel.
 * ``allreduce_add_rmsnorm(h, residual, w)``: sum the per-rank partial ``h`` over the TP
   group, add the residual, RMS-normalise.  Backend ``"fused"`` does all three in ONE
   kernel that reads the peers' partials straight from their HBM over NVLink (symmetric
@@ -33,6 +37,8 @@ class TPComm:
         self.symm = None
         self.ops = None
         self.launches = 0
+        # GEMM -> reduce-scatter path for decode-sized steps (fused backend only)
+        self.rs_enabled = bool(getattr(config, "fused_reduce_scatter", True)) if config is not None else True
 
     def bind(self, runner):
         self.runner = runner
@@ -62,6 +68,19 @@ class TPComm:
             return self.symm.allreduce_add_rmsnorm(h, residual, w, eps, self.ops, final=final)
         dist.all_reduce(h, op=dist.ReduceOp.SUM, group=self.tp.group)
         return self.ops.add_rmsnorm(h, residual, w, eps)
+
+    # ----------------------------------------- GEMM -> reduce-scatter (decode steps)
+    def rs_ok(self, T: int, k: int) -> bool:
+        """The row-parallel GEMM of a T-token step with inner size k can store its rows at their
+        owners (fused backend, decode-sized step, K a multiple of the GEMM's 64-wide k-block)."""
+        return self.symm is not None and self.rs_enabled and k % 64 == 0 and self.symm.rs_ok(T)
+
+    def linear_rs_norm(self, x, w, w_norm, eps):
+        """rmsnorm(allreduce(x @ w^T) + residual) with the reduce-scatter in the GEMM epilogue:
+        the GEMM stores each output row at the rank that owns it, the owner sums the partials,
+        adds its residual rows, normalises and all-gathers.  Returns (normed rows, residual)."""
+        self.symm.linear_rs(x, w, self.ops)
+        return self.symm.rs_add_rmsnorm(x.shape[0], w_norm, eps, self.ops)
 
     def all_reduce(self, x):
         dist.all_reduce(x, op=dist.ReduceOp.SUM, group=self.tp.group)

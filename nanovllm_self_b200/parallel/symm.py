@@ -3,9 +3,15 @@
 Each rank ``cudaMalloc``s one buffer (via the extension, outside torch's caching
 allocator), exports its IPC handle, gathers every peer's handle over the process group
 and opens them, so every rank holds a pointer to every rank's buffer.  The buffer is
-laid out as ``IN | RES | OUT | FLAGS`` (see ``csrc/comm.cu``).  The fused
+laid out as ``IN | IN0 IN1 IN2 | RES | OUT | RS | FLAGS`` (see ``csrc/comm.cu``).  The fused
 ``allreduce_add_rmsnorm`` kernel reads the peers' IN rows and writes every rank's RES
 and OUT rows over NVLink.
+
+Decode-sized steps (at most ``COMM_RS_MAX_ROWS`` tokens) take the GEMM -> reduce-scatter
+path instead: the row-parallel GEMM stores each output row straight into the RS area of
+the rank that owns it (``linear_rs``), and one kernel on the owner sums the partials, adds
+the residual, normalises and all-gathers the rows into every rank's OUT
+(``rs_add_rmsnorm``).  Only the owner keeps the residual of its rows there.
 """
 from __future__ import annotations
 
@@ -44,12 +50,15 @@ class SymmetricWorkspace:
                             torch.cuda.get_device_properties(tp.device).multi_processor_count)
         row_bytes = rows * hidden * 2
         small = min(rows, oneshot_rows) * hidden * 2
-        # IN (two-shot) | IN0 IN1 IN2 (one-shot rotation) | RES | OUT | FLAGS
+        self.rs_max_rows = int(self.C.COMM_RS_MAX_ROWS)
+        rs_bytes = tp.size * self.rs_max_rows * hidden * 2
+        # IN (two-shot) | IN0 IN1 IN2 (one-shot rotation) | RES | OUT | RS (reduce-scatter) | FLAGS
         self.in_off = 0
         self.in1_off = [row_bytes, row_bytes + small, row_bytes + 2 * small]
         self.res_off = row_bytes + 3 * small
         self.out_off = 2 * row_bytes + 3 * small
-        self.flag_off = 3 * row_bytes + 3 * small
+        self.rs_off = 3 * row_bytes + 3 * small
+        self.flag_off = self.rs_off + rs_bytes
         self.nbytes = self.flag_off + int(self.C.COMM_FLAG_BYTES)
         torch.cuda.set_device(tp.device)
         self.base, handle = self.C.symm_alloc(self.nbytes)
@@ -121,6 +130,37 @@ class SymmetricWorkspace:
         if ops is not None and hasattr(ops, "launches"):
             ops.launches += 1
         return self.OUT[:T], res
+
+    # ------------------------------------------------ GEMM -> reduce-scatter path
+    def rs_ok(self, T: int) -> bool:
+        """Whether a step of T tokens can take the GEMM -> reduce-scatter path."""
+        return 0 < T <= min(self.rs_max_rows, self.rows)
+
+    def rs_rows(self, T: int) -> int:
+        return (T + self.tp.size - 1) // self.tp.size
+
+    def linear_rs(self, x, w, ops=None):
+        """Row-parallel GEMM x @ w^T whose output rows are stored at their owner ranks."""
+        T = x.shape[0]
+        plan = self.C.linear_rs(x, w, self.bases, self.rs_off, self.flag_off, self.tp.rank, self.rs_rows(T),
+                                self.IN[:T])
+        if ops is not None and hasattr(ops, "launches"):
+            ops.launches += 1
+        return plan
+
+    def rs_add_rmsnorm(self, T: int, w, eps, ops=None):
+        """Owner-side sum + residual + RMSNorm + all-gather of the rows ``linear_rs`` stored.
+
+        Returns (OUT[:T], RES[:T]): every rank holds all normalised rows; the residual rows
+        are current only on their owner (they are only ever read there).
+        """
+        rr = self.rs_rows(T)
+        ctas = max(1, min(self.max_ctas, rr))
+        self.C.rs_add_rmsnorm_ag(self.bases, self.rs_off, self.res_off, self.out_off, self.flag_off, w,
+                                 self.tp.rank, T, rr, self.hidden, True, float(eps), ctas, self.timeout_ns)
+        if ops is not None and hasattr(ops, "launches"):
+            ops.launches += 1
+        return self.OUT[:T], self.RES[:T]
 
     def error(self, reset: bool = False) -> int:
         return int(self.C.comm_error(reset))
