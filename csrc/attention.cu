@@ -1026,6 +1026,451 @@ static PFN_cuTensorMapEncodeTiled_v12000 attn_encode() {
   return fn;
 }
 
+// ------------------------------------------------------------- prefill on tcgen05
+// Prefix-aware causal flash-attention prefill on the 5th-generation tensor cores (bf16 KV).
+//
+// One CTA per (query tile, KV head, sequence).  GQA is packed into the MMA's 128 rows: row
+// r holds query token t0 + r / G of query head h G + r % G, so the G heads that share a KV
+// head share every K/V tile a CTA loads (G = nq / nkv, 128 / G tokens per tile).  Per 128-key
+// tile j:
+//   S_j = Q K_j^T      tcgen05.mma, A = Q (smem, K-major), B = K_j (smem, K-major), D in TMEM
+//   P_j = exp2(S_j - m) softmax warps: one TMEM lane (= one row) per thread, no shuffles;
+//                      P_j is written back into TMEM over S_j as packed bf16
+//   O  += P_j V_j      tcgen05.mma, A = P_j (TMEM), B = V_j (smem, MN-major), D = O in TMEM
+// S is double-buffered in TMEM (S_{j+1} runs on the tensor cores while the softmax warps
+// work on S_j); K and V stream through a 2-stage TMA ring straight from the paged pool
+// (one box per KV block, out-of-range blocks read as zeros).  The running maximum m is only
+// raised, and O rescaled, when a row's maximum grows by more than 8 (a factor 256 in P,
+// harmless in fp32 / bf16), so most tiles skip the rescale.
+// Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer, 2-5 softmax / correction / output.
+// Every mbarrier wait is time-bounded (error word g_attn_error, codes 40-49).
+namespace pf {
+
+constexpr int TQ_ROWS = 128;  // MMA M: (query token, query head) rows per CTA
+constexpr int TK = 128;       // keys per tile (MMA N of S, K of P V)
+constexpr int NSTAGE = 2;     // K/V ring depth
+constexpr int THREADS = 192;
+constexpr int HALF = TQ_ROWS * 64 * 2;  // bytes of one 64-dim half of a 128-row tile (16 KB)
+constexpr int TILE = 2 * HALF;          // 32 KB: a 128 x 128 bf16 tile
+constexpr float RESCALE_LOG2 = 8.f;
+
+struct Args {
+  const int* block_tables;
+  int W;
+  const int* cu_q;
+  const int* ctx_lens;
+  __nv_bfloat16* out;
+  int nq, nkv, G, block_size, num_blocks, seq_offset;
+  int kv_box;       // rows per K/V TMA box: min(block_size, 128)
+  int kv_rows;      // rows of the 2-D [NB * nkv * BS, 128] pool view (an out-of-range row start)
+  float scale_log2;
+};
+
+__device__ __forceinline__ void bar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tma2d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma3d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// D (TMEM) (+)= A (smem descriptor) * B (smem descriptor)
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// D (TMEM) (+)= A (TMEM) * B (smem descriptor)
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+// Shared-memory matrix descriptor, 128-byte swizzle, version 1 (sm_100).  K-major operands:
+// 8-row groups 1024 B apart (sbo), lbo unused.  MN-major operands: lbo = distance between
+// 64-element blocks along M/N, sbo = distance between 8-row groups along K.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFF) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// bf16 x bf16 -> f32, M = 128, N = 128; `b_mn_major`: B stored MN-major (V).
+__device__ __forceinline__ constexpr uint32_t idesc(bool b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn_major ? (1u << 16) : 0u) | ((uint32_t)(128 >> 3) << 17) |
+         ((uint32_t)(128 >> 4) << 24);
+}
+
+// TMEM columns: S buffers at 0 and 128, O at 256.
+__device__ __forceinline__ constexpr uint32_t s_col(int s) { return s ? 128u : 0u; }
+constexpr uint32_t O_COL = 256;
+
+}  // namespace pf
+
+__global__ void __launch_bounds__(pf::THREADS, 1)
+    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                           const __grid_constant__ CUtensorMap vmap, pf::Args a) {
+  using namespace pf;
+  pdl_wait();     // inputs come from the previous kernel in the stream
+  pdl_trigger();  // the next kernel may start its prologue
+  extern __shared__ __align__(1024) uint8_t pf_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(pf_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = sm;                           // Q: [2 halves][128 rows][128 B]
+  uint8_t* sk = sq + TILE;                    // K ring: NSTAGE x TILE
+  uint8_t* sv = sk + NSTAGE * TILE;           // V ring: NSTAGE x TILE
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + NSTAGE * TILE);
+  // bars: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_ready[2], s_free[2], o_done, o_final
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 17);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18);
+  const uint32_t b0 = smem_u32(bars);
+  const uint32_t q_full = b0;
+  auto k_full = [&](int s) { return b0 + 8u * (1 + s); };
+  auto k_empty = [&](int s) { return b0 + 8u * (3 + s); };
+  auto v_full = [&](int s) { return b0 + 8u * (5 + s); };
+  auto v_empty = [&](int s) { return b0 + 8u * (7 + s); };
+  auto s_full = [&](int s) { return b0 + 8u * (9 + s); };
+  auto p_ready = [&](int s) { return b0 + 8u * (11 + s); };
+  auto s_free = [&](int s) { return b0 + 8u * (13 + s); };
+  const uint32_t o_done = b0 + 8u * 15, o_final = b0 + 8u * 16;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int G = a.G, TQ = TQ_ROWS / G;
+  const int b = blockIdx.z + a.seq_offset;
+  const int h = blockIdx.y;
+  const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest (latest) query tiles first
+  const int qs = a.cu_q[b];
+  const int q_len = a.cu_q[b + 1] - qs;
+  const int t0 = qt * TQ;
+  if (t0 >= q_len) return;  // uniform over the CTA: nothing initialised yet
+  const int k_len = a.ctx_lens[b];
+  const int off = k_len - q_len;
+  const int kmax = min(k_len, off + min(q_len, t0 + TQ));
+  const int n_tiles = (kmax + TK - 1) / TK;
+
+  if (threadIdx.x == 0) {
+    bar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      bar_init(k_full(s), 1);
+      bar_init(k_empty(s), 1);
+      bar_init(v_full(s), 1);
+      bar_init(v_empty(s), 1);
+      bar_init(s_full(s), 1);
+      bar_init(p_ready(s), 128);
+      bar_init(s_free(s), 1);
+    }
+    bar_init(o_done, 1);
+    bar_init(o_final, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)), "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tslot;
+
+  auto wait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
+    if (att_try(bar, parity)) return true;
+    const uint64_t tstart = att_timer();
+    while (!att_try(bar, parity)) {
+      if (*abort_flag) return false;
+      if (att_timer() - tstart > ATT_WAIT_NS) {
+        atomicCAS(&g_attn_error, 0, code);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+    return true;
+  };
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&qmap)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&vmap)) : "memory");
+    expect_tx(q_full, TILE);
+    for (int half = 0; half < 2; ++half)
+      tma3d(smem_u32(sq + half * HALF), &qmap, q_full, half * 64, h * G, qs + t0);
+    const int* bt = a.block_tables + (int64_t)b * a.W;
+    const int boxes = TK / a.kv_box;
+    bool ok = true;
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      const int s = j & 1;
+      const uint32_t par = ((j >> 1) & 1) ^ 1;
+      for (int kv = 0; kv < 2 && ok; ++kv) {
+        if (!wait(kv ? v_empty(s) : k_empty(s), par, 40)) {
+          ok = false;
+          break;
+        }
+        const uint32_t full = kv ? v_full(s) : k_full(s);
+        uint8_t* dst = (kv ? sv : sk) + s * TILE;
+        expect_tx(full, TILE);
+        for (int bx = 0; bx < boxes; ++bx) {
+          const int tk = j * TK + bx * a.kv_box;
+          const int bi = tk / a.block_size;
+          int row = a.kv_rows;  // past the end: the box reads as zeros
+          if (tk < k_len && bi < a.W) {
+            const int blk = bt[bi];
+            if (blk >= 0 && blk < a.num_blocks) row = (blk * a.nkv + h) * a.block_size + (tk % a.block_size);
+          }
+          for (int half = 0; half < 2; ++half)
+            tma2d(smem_u32(dst + half * HALF + bx * a.kv_box * 128), kv ? &vmap : &kmap, full, half * 64, row);
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------------ MMA issuer
+    const uint32_t id_qk = idesc(false), id_pv = idesc(true);
+    bool ok = wait(q_full, 0, 41);
+    const uint32_t qa = smem_u32(sq);
+    for (int j = 0; j <= n_tiles && ok; ++j) {
+      if (j < n_tiles) {
+        const int s = j & 1;
+        if (!wait(k_full(s), (j >> 1) & 1, 42)) break;
+        if (j >= 2 && !wait(s_free(s), ((j - 2) >> 1) & 1, 43)) break;
+        fence_after();
+        const uint32_t kb = smem_u32(sk + s * TILE);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t ho = (k >> 2) * HALF + (k & 3) * 32;  // 16-element step inside a 64-dim half
+          mma_ss(tmem + s_col(s), desc_sw128(qa + ho, 16, 1024), desc_sw128(kb + ho, 16, 1024), id_qk, k > 0);
+        }
+        commit(s_full(s));
+        commit(k_empty(s));
+      }
+      if (j >= 1) {
+        const int jj = j - 1, s = jj & 1;
+        if (!wait(p_ready(s), (jj >> 1) & 1, 44)) break;
+        if (!wait(v_full(s), (jj >> 1) & 1, 45)) break;
+        fence_after();
+        const uint32_t vb = smem_u32(sv + s * TILE);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)  // 16 keys per step: P columns 8k.., V rows 16k..
+          mma_ts(tmem + O_COL, tmem + s_col(s) + 8 * k, desc_sw128(vb + k * 16 * 128, HALF, 1024), id_pv,
+                 (jj > 0 || k > 0) ? 1u : 0u);
+        commit(o_done);
+        commit(v_empty(s));
+        commit(s_free(s));
+      }
+    }
+    commit(o_final);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------------ softmax / output
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const int t = t0 + r / G, g = r % G;
+    const int pos = off + t;
+    const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s = j & 1;
+      if (!wait(s_full(s), (j >> 1) & 1, 46)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      uint32_t raw[TK];
+#pragma unroll
+      for (int c = 0; c < TK; c += 32) tmem_ld32(lane_base + s_col(s) + c, raw + c);
+      tmem_ld_wait();
+      const int key0 = j * TK;
+      const int lim = min(pos + 1, k_len) - key0;  // keys [0, lim) of this tile are visible
+      float x[TK];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < TK; ++c) {
+        x[c] = c < lim ? __uint_as_float(raw[c]) * a.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, x[c]);
+      }
+      if (mx > m_used + RESCALE_LOG2 || m_used == -INFINITY) {
+        // raise the running maximum; O (if any) must be rescaled first
+        const float m_new = mx;
+        if (j > 0 && m_used != -INFINITY) {
+          if (!wait(o_done, (j - 1) & 1, 47)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const float f = exp2f(m_used - m_new);
+#pragma unroll 1
+          for (int c = 0; c < 128; c += 32) {
+            uint32_t o[32];
+            tmem_ld32(lane_base + O_COL + c, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+            tmem_st32(lane_base + O_COL + c, o);
+          }
+          tmem_st_wait();
+          l *= f;
+        }
+        if (m_new != -INFINITY) m_used = m_new;
+      }
+      const float base = m_used == -INFINITY ? 0.f : m_used;
+      uint32_t p[TK / 2];
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < TK; c += 2) {
+        const float p0 = exp2f(x[c] - base), p1 = exp2f(x[c + 1] - base);
+        rs += p0 + p1;
+        p[c / 2] = pack_bf16(p0, p1);
+      }
+      l += rs;
+      tmem_st32(lane_base + s_col(s), p);
+      tmem_st32(lane_base + s_col(s) + 32, p + 32);
+      tmem_st_wait();
+      fence_before();
+      arrive(p_ready(s));
+    }
+    if (ok && wait(o_final, 0, 48)) {
+      fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst = a.out + ((int64_t)(qs + t) * a.nq + h * G + g) * 128;
+      const bool valid = t < q_len;
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        uint32_t o[32];
+        tmem_ld32(lane_base + O_COL + c, o);
+        tmem_ld_wait();
+        if (valid) {
+          float f[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(o[e]) * inv;
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) *reinterpret_cast<uint4*>(dst + c + e) = f32_to_bf16x8(f + e);
+        }
+      }
+    }
+    fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+static int prefill_tc_smem() { return 1024 + pf::TILE * (1 + 2 * pf::NSTAGE) + 256; }
+
+// 3-D view of q [T, nq, 128] for the packed (token, head) rows: box = 64 dims x G heads x 128/G tokens.
+static bool q_map(CUtensorMap* m, const void* q, int T, int nq, int G) {
+  auto enc = attn_encode();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)AD, (cuuint64_t)nq, (cuuint64_t)T};
+  cuuint64_t strides[2] = {(cuuint64_t)AD * 2, (cuuint64_t)nq * AD * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)G, (cuuint32_t)(pf::TQ_ROWS / G)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 2-D view [num_blocks * nkv * block_size rows, 128 dims] of a bf16 K or V pool, box 64 x box_rows.
+static bool kv_map_tc(CUtensorMap* m, const void* base, int64_t rows, int box_rows) {
+  auto enc = attn_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)AD, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)AD * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Whether the tcgen05 prefill kernel serves this launch (bf16 KV, GQA group dividing 128).
+static bool prefill_tc_ok(const AttnLaunch& L) {
+  const int G = L.nq / L.nkv;
+  if (L.kv_fp8 || L.head_dim != AD || L.nq % L.nkv || G < 1 || 128 % G) return false;
+  if (L.block_size < 8) return false;  // a K/V box holds at least 8 rows (one swizzle group)
+  if (((uintptr_t)L.q & 15) || ((uintptr_t)L.k_cache & 15) || ((uintptr_t)L.v_cache & 15)) return false;
+  const int64_t rows = (int64_t)L.num_blocks * L.nkv * L.block_size;
+  return rows < (int64_t)INT32_MAX - 256;
+}
+
+static cudaError_t launch_attn_prefill_tc(const AttnLaunch& L, int max_q_len, int total_q, cudaStream_t stream) {
+  const int G = L.nq / L.nkv;
+  pf::Args a;
+  a.block_tables = L.block_tables;
+  a.W = L.W;
+  a.cu_q = L.cu_q;
+  a.ctx_lens = L.ctx_lens;
+  a.out = static_cast<__nv_bfloat16*>(L.out);
+  a.nq = L.nq;
+  a.nkv = L.nkv;
+  a.G = G;
+  a.block_size = L.block_size;
+  a.num_blocks = L.num_blocks;
+  a.seq_offset = L.seq_offset;
+  a.kv_box = L.block_size < pf::TK ? L.block_size : pf::TK;
+  const int64_t rows = (int64_t)L.num_blocks * L.nkv * L.block_size;
+  a.kv_rows = (int)rows;
+  a.scale_log2 = L.softmax_scale * LOG2E;
+  CUtensorMap qm, km, vm;
+  if (!q_map(&qm, L.q, total_q, L.nq, G) || !kv_map_tc(&km, L.k_cache, rows, a.kv_box) ||
+      !kv_map_tc(&vm, L.v_cache, rows, a.kv_box))
+    return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> done{0};
+  cudaError_t e = smem_opt_in(done, attn_prefill_tc_kernel, prefill_tc_smem());
+  if (e != cudaSuccess) return e;
+  const int TQ = pf::TQ_ROWS / G;
+  dim3 grid((max_q_len + TQ - 1) / TQ, L.nkv, L.num_seqs);
+  launch_pdl(attn_prefill_tc_kernel, grid, dim3(pf::THREADS), prefill_tc_smem(), stream, qm, km, vm, a);
+  NVB_LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
 // 2-D view [num_blocks * nkv * block_size rows, 128 dims] of one layer's K or V pool.
 static bool kv_map(CUtensorMap* m, const void* base, int64_t rows, bool fp8, int box_rows) {
   auto enc = attn_encode();
@@ -1120,8 +1565,13 @@ int attn_error_code(int reset) {
 }
 
 cudaError_t launch_attn_prefill(const AttnLaunch& L, int max_q_len, cudaStream_t stream) {
+  return launch_attn_prefill_ex(L, max_q_len, -1, 1, stream);
+}
+
+cudaError_t launch_attn_prefill_ex(const AttnLaunch& L, int max_q_len, int total_q, int use_tc, cudaStream_t stream) {
   if (L.num_seqs == 0 || max_q_len == 0) return cudaSuccess;
   if (L.head_dim != AD || L.nq % L.nkv) return cudaErrorInvalidValue;
+  if (use_tc && total_q > 0 && prefill_tc_ok(L)) return launch_attn_prefill_tc(L, max_q_len, total_q, stream);
   AttnArgs a;
   a.q = static_cast<const __nv_bfloat16*>(L.q);
   a.k_cache = L.k_cache;

@@ -141,12 +141,13 @@ void attn_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tenso
 void attn_prefill(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                   const c10::optional<at::Tensor>& k_scale, const c10::optional<at::Tensor>& v_scale,
                   const at::Tensor& block_tables, const at::Tensor& cu_q, const at::Tensor& ctx_lens, at::Tensor& out,
-                  int64_t nq, int64_t nkv, int64_t seq_offset, int64_t num_seqs, int64_t max_q_len, double scale) {
+                  int64_t nq, int64_t nkv, int64_t seq_offset, int64_t num_seqs, int64_t max_q_len, double scale,
+                  int64_t use_tc) {
   auto L = attn_args(q, k_cache, v_cache, k_scale, v_scale, block_tables, cu_q, ctx_lens, out, nq, nkv, seq_offset,
                      num_seqs, scale);
   L.splits = 1;
   at::cuda::CUDAGuard g(q.device());
-  check(nvb::launch_attn_prefill(L, (int)max_q_len, stream()), "attn_prefill");
+  check(nvb::launch_attn_prefill_ex(L, (int)max_q_len, (int)q.size(0), (int)use_tc, stream()), "attn_prefill");
 }
 
 int64_t decode_splits(int64_t num_seqs, int64_t nkv, int64_t max_ctx, int64_t num_sms) {
@@ -187,7 +188,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &embedding);
   m.def("qkv_post", &qkv_post);
   m.def("attn_decode", &attn_decode);
-  m.def("attn_prefill", &attn_prefill);
+  m.def("attn_prefill", &attn_prefill, pybind11::arg("q"), pybind11::arg("k_cache"), pybind11::arg("v_cache"),
+        pybind11::arg("k_scale"), pybind11::arg("v_scale"), pybind11::arg("block_tables"), pybind11::arg("cu_q"),
+        pybind11::arg("ctx_lens"), pybind11::arg("out"), pybind11::arg("nq"), pybind11::arg("nkv"),
+        pybind11::arg("seq_offset"), pybind11::arg("num_seqs"), pybind11::arg("max_q_len"), pybind11::arg("scale"),
+        pybind11::arg("use_tc") = 1);
   m.def("decode_splits", &decode_splits);
   m.def("attn_error", &attn_error, pybind11::arg("reset") = false);
   m.def("sample_chunks", &sample_chunks);

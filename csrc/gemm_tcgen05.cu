@@ -1232,6 +1232,7 @@ constexpr int DEC_SMEM_MAX = 232448;  // opt-in dynamic shared memory per block 
 struct DecCfg {
   int mt, bn, splits, kb_per_split, w_stages, a_stages, smem, tiles;
   double cost;
+  double traffic = 0.0;  // waves x bytes one CTA moves through its shared memory (see dec_candidates)
 };
 
 template <int MT>
@@ -1269,8 +1270,11 @@ int dec_capacity(int splits, int smem) {
 
 // All decode-kernel shapes for C[m, n] (m <= 256), cheapest first by a bytes-per-CTA model:
 // waves x (weight + activation bytes one CTA streams + its share of the reduction + a fixed
-// pipeline-fill cost).
-std::vector<DecCfg> dec_candidates(int m, int n, int k) {
+// pipeline-fill cost).  `traffic` is a second ranking: waves x (bytes one CTA loads into shared
+// memory: its weight slice AND all m activation rows of its K range, plus the fp32 partial it
+// exports and reads back in a split-K reduction).  At m >= 128 the activation rows, re-read by
+// every CTA, outweigh the weights unless the slice is wide, which the first model ignores.
+std::vector<DecCfg> dec_candidates(int m, int n, int k, bool by_traffic = false) {
   std::vector<DecCfg> out;
   if (m <= 0 || m > 2 * BM || k % BK) return out;
   const int mt = m > BM ? 2 : 1;
@@ -1300,11 +1304,16 @@ std::vector<DecCfg> dec_candidates(int m, int n, int k) {
         const double inflight = (double)(w_st < kbs ? w_st : kbs) * w_bytes;
         const double red = s_eff > 1 ? 0.5 * mt * BM * bn * 4 / 65536.0 : 0.0;
         DecCfg c{mt, bn, s_eff, kbs, w_st, a_st, smem, tiles, waves * (w_cta / inflight + red + 2.0)};
+        const double red_bytes = s_eff > 1 ? 2.0 * mt * BM * bn * 4 : 0.0;
+        c.traffic = waves * ((double)kbs * (w_bytes + a_bytes) + red_bytes);
         out.push_back(c);
       }
     }
   }
-  std::sort(out.begin(), out.end(), [](const DecCfg& a, const DecCfg& b) { return a.cost < b.cost; });
+  if (by_traffic)
+    std::sort(out.begin(), out.end(), [](const DecCfg& a, const DecCfg& b) { return a.traffic < b.traffic; });
+  else
+    std::sort(out.begin(), out.end(), [](const DecCfg& a, const DecCfg& b) { return a.cost < b.cost; });
   return out;
 }
 
@@ -1370,10 +1379,35 @@ cudaError_t gemm_dec_explicit(const void* x, int64_t ldx, const void* w, int64_t
   return cudaErrorInvalidValue;
 }
 
+static GemmPlan dec_to_plan(const DecCfg& d, int k);
+
 bool gemm_dec_plan(int m, int n, int k, int rank, GemmPlan* plan) {
   const auto cands = dec_candidates(m, n, k);
   if (rank < 0 || rank >= (int)cands.size()) return false;
-  const DecCfg& d = cands[rank];
+  *plan = dec_to_plan(cands[rank], k);
+  return true;
+}
+
+// Decode-kernel plans worth timing: the `each` cheapest by either model (deduplicated).
+static std::vector<GemmPlan> dec_plans_for_tuning(int m, int n, int k, int each, int act) {
+  std::vector<GemmPlan> out;
+  for (int by_traffic = 0; by_traffic < 2; ++by_traffic) {
+    int taken = 0;
+    for (const auto& d : dec_candidates(m, n, k, by_traffic != 0)) {
+      if (taken >= each) break;
+      if (act && d.bn % 32) continue;
+      bool dup = false;
+      for (const auto& p : out)
+        dup |= p.bn == d.bn && p.splits == d.splits && p.a_stages == d.a_stages && p.stages == d.w_stages;
+      if (dup) continue;
+      out.push_back(dec_to_plan(d, k));
+      ++taken;
+    }
+  }
+  return out;
+}
+
+static GemmPlan dec_to_plan(const DecCfg& d, int k) {
   GemmPlan pl{};
   pl.dec = 1;
   pl.mt = d.mt;
@@ -1388,8 +1422,7 @@ bool gemm_dec_plan(int m, int n, int k, int rank, GemmPlan* plan) {
   pl.tiles_p = 1;
   pl.tiles_q = d.tiles;
   pl.grid = d.tiles * d.splits;
-  *plan = pl;
-  return true;
+  return pl;
 }
 
 GemmPlan gemm_plan(int m, int n, int k, int force_swap, int force_bn, int force_splits) {
@@ -1599,15 +1632,8 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
     const int bq = m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256;
     for (int sp : {1, 2, 3, 4}) cands.push_back(gemm_plan(m, n, k, 1, bq, sp));
   }
-  if (m <= 2 * BM && k % BK == 0) {
-    GemmPlan d;
-    int taken = 0;
-    for (int r = 0; taken < 8 && gemm_dec_plan(m, n, k, r, &d); ++r)
-      if (!act || d.bn % 32 == 0) {
-        cands.push_back(d);
-        ++taken;
-      }
-  }
+  if (m <= 2 * BM && k % BK == 0)
+    for (const auto& d : dec_plans_for_tuning(m, n, k, 6, act)) cands.push_back(d);
   if (ws && counters) {
     for (int bn : {256, 128}) {
       cands.push_back(gemm_plan(m, n, k, 0, bn, -1));
@@ -1682,9 +1708,7 @@ cudaError_t gemm_bf16_rs(const void* x, int64_t ldx, const void* w, int64_t ldw,
     }
   }
   if (!have) {
-    std::vector<GemmPlan> cands;
-    GemmPlan d;
-    for (int r = 0; cands.size() < 8 && gemm_dec_plan(m, n, k, r, &d); ++r) cands.push_back(d);
+    std::vector<GemmPlan> cands = dec_plans_for_tuning(m, n, k, 6, 0);
     if (cands.empty()) return cudaErrorNotSupported;
     best = cands[0];
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;

@@ -40,6 +40,9 @@ struct AttnLaunch {
 int attn_decode_splits(int num_seqs, int nkv, int max_ctx, int num_sms);
 cudaError_t launch_attn_decode(const AttnLaunch& L, cudaStream_t stream);
 cudaError_t launch_attn_prefill(const AttnLaunch& L, int max_q_len, cudaStream_t stream);
+// total_q: rows of q (tokens of the whole launch's q tensor, for its tensor map; <= 0 forces the
+// mma.sync kernel); use_tc: 1 = tcgen05 kernel where it applies (bf16 KV), 0 = mma.sync kernel.
+cudaError_t launch_attn_prefill_ex(const AttnLaunch& L, int max_q_len, int total_q, int use_tc, cudaStream_t stream);
 // Error word set by an attention kernel that gave up on a bounded wait (0 = none).
 int attn_error_code(int reset);
 

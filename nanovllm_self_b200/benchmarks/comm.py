@@ -3,7 +3,10 @@
 Launch one process per GPU::
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
-        -m nanovllm_self_b200.benchmarks.comm
+        -m nanovllm_self_b200.benchmarks.comm [--gemm]
+
+``--gemm`` times the whole row-parallel GEMM + reduction + norm per call instead (see
+``main_gemm``), the GEMM -> reduce-scatter path against the all-reduce kernel and NCCL.
 
 For each token count T (hidden 4096, bf16) every variant is captured 20 times into one
 CUDA graph and replayed; the time per call is the device time of the replays divided by the
@@ -93,5 +96,85 @@ def main(hidden: int = 4096, tokens=(1, 16, 64, 256, 512, 1024, 4096)):
     dist.destroy_process_group()
 
 
+def main_gemm(hidden: int = 4096, inter: int = 12288, heads: int = 32, tokens=(1, 16, 64, 128, 256)):
+    """Row-parallel GEMM + reduction + residual + RMSNorm, per call, for Qwen3-8B's o_proj and down_proj.
+
+    Variants: ``gemm_rs`` (the reduce-scatter in the GEMM epilogue, then the owner-side sum +
+    norm + all-gather kernel: the product path for decode steps), ``gemm_allreduce`` (GEMM into
+    the symmetric buffer, then the all-reduce + norm kernel), ``gemm_nccl`` (GEMM, NCCL
+    all_reduce, add + RMSNorm kernel: the reference's structure) and ``gemm_only`` (no
+    reduction).  The weights rotate over enough copies to exceed the L2, as in a forward pass.
+    ``roofline_us`` = max(weight bytes / HBM, FLOPs / bf16 peak, NVLink bytes / link) with the
+    NVLink bytes of reduce-scatter + all-gather, 2 (N-1)/N T H 2 per rank.
+    """
+    tp = init_tensor_parallel(int(os.environ["WORLD_SIZE"]), "cuda")
+    ops = CudaOps()
+    symm = SymmetricWorkspace(tp, rows=max(tokens), hidden=hidden)
+    dev = tp.device
+    wn = torch.ones(hidden, device=dev, dtype=torch.bfloat16)
+    peaks = _peaks()
+    for name, k in (("o_proj", heads * 128 // tp.size), ("down_proj", inter // tp.size)):
+        wbytes = hidden * k * 2
+        copies = max(2, min(CALLS, (256 << 20) // wbytes + 1))
+        ws = [(torch.randn(hidden, k, device=dev) * 0.02).to(torch.bfloat16) for _ in range(copies)]
+        for T in tokens:
+            x = torch.randn(T, k, device=dev).to(torch.bfloat16)
+            # residual stream for the reduce-scatter path (its owner rows live in RES)
+            symm.allreduce_add_rmsnorm(symm.input_buffer(T), None, wn, 1e-6, ops)
+            hh = torch.empty(T, hidden, device=dev, dtype=torch.bfloat16)
+            rr = torch.randn(T, hidden, device=dev).to(torch.bfloat16)
+            it = [0]
+
+            def nxt():
+                it[0] = (it[0] + 1) % copies
+                return ws[it[0]]
+
+            def gemm_rs():
+                symm.linear_rs(x, nxt(), ops)
+                return symm.rs_add_rmsnorm(T, wn, 1e-6, ops)
+
+            def gemm_allreduce():
+                ops.linear(x, nxt(), out=symm.input_buffer(T))
+                return symm.allreduce_add_rmsnorm(symm.input_buffer(T), symm.RES[:T], wn, 1e-6, ops)
+
+            def gemm_nccl():
+                ops.linear(x, nxt(), out=hh)
+                dist.all_reduce(hh)
+                return ops.add_rmsnorm(hh, rr, wn, 1e-6)
+
+            def gemm_only():
+                return ops.linear(x, nxt(), out=hh)
+
+            times = {f.__name__: _graph_time(f, dev) for f in (gemm_rs, gemm_allreduce, gemm_nccl, gemm_only)}
+            link = 2 * (tp.size - 1) / tp.size * T * hidden * 2 / (LINK_GBS * 1e3)
+            hbm = wbytes / (peaks["hbm_gbs"] * 1e3)
+            mma = 2 * T * hidden * k / (peaks["bf16_tflops"] * 1e6)
+            roof = max(link, hbm, mma)
+            if tp.rank == 0:
+                print(json.dumps({"world": tp.size, "op": name, "T": T, "k": k,
+                                  **{f"{n}_us": round(t, 2) for n, t in times.items()},
+                                  "roofline_us": round(roof, 2), "link_us": round(link, 2), "hbm_us": round(hbm, 2),
+                                  "frac_roofline_rs": round(roof / times["gemm_rs"], 3),
+                                  "error_word": symm.error()}), flush=True)
+    symm.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _peaks() -> dict:
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"])}
+    except (OSError, ValueError, KeyError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
 if __name__ == "__main__":
-    main()
+    import sys
+    if "--gemm" in sys.argv:
+        main_gemm()
+    else:
+        main()

@@ -26,8 +26,12 @@ import torch
 from ..ops.cuda_ops import CudaOps
 
 NQ, NKV, D, HID, INTER, VOCAB = 32, 8, 128, 4096, 12288, 151936
-CASES = ("attn_decode", "attn_decode_fp8", "attn_prefill", "attn_prefill_fp8", "gemm_prefill", "gemm_decode",
-         "gemm_decode256", "gemm_gate_up_silu256", "qkv_post", "qkv_post_fp8", "add_rmsnorm", "silu_mul", "sample")
+CASES = ("attn_decode", "attn_decode_fp8", "attn_prefill", "attn_prefill_mma", "attn_prefill_fp8",
+         "attn_prefill_flash_attn", "gemm_prefill", "gemm_decode", "gemm_decode256", "gemm_gate_up_silu256", "qkv_post",
+         "qkv_post_fp8", "add_rmsnorm", "silu_mul", "sample")
+# Qwen3-8B decode GEMM shapes (n, k) for gemm_sweep: qkv, o_proj, gate_up, down_proj, lm_head
+DECODE_SHAPES = {"qkv": ((NQ + 2 * NKV) * D, HID), "o_proj": (HID, NQ * D), "gate_up": (2 * INTER, HID),
+                 "down_proj": (HID, INTER), "lm_head": (VOCAB, HID)}
 
 
 class _Ctx:
@@ -65,10 +69,21 @@ def build_case(name: str, ops: CudaOps, dev="cuda"):
         kv_bytes = 2 * B * NKV * L * D * kc.element_size()
         return (lambda: ops.attention(q, kc, vc, c, D ** -0.5, ks, vs)), kv_bytes + 2 * q.numel() * 2, \
             4 * B * NQ * L * D
+    if name == "attn_prefill_flash_attn":
+        # the reference's prefill kernel (flash_attn_varlen_func, causal, contiguous K/V), same shape
+        from flash_attn import flash_attn_varlen_func
+        B, L = 8, 2048
+        q = torch.randn(B * L, NQ, D, device=dev).to(torch.bfloat16)
+        k = torch.randn(B * L, NKV, D, device=dev).to(torch.bfloat16)
+        v = torch.randn_like(k)
+        cu = torch.arange(0, B * L + 1, L, device=dev, dtype=torch.int32)
+        return (lambda: flash_attn_varlen_func(q, k, v, cu, cu, L, L, causal=True, softmax_scale=D ** -0.5)), None, \
+            2 * B * NQ * L * L * D
     if name.startswith("attn_prefill"):
         fp8 = name.endswith("fp8")
         B, L = 8, 2048
         q, kc, vc, ks, vs, c = _paged(B, L, L, fp8, dev)
+        ops.prefill_tc = name != "attn_prefill_mma"
         return (lambda: ops.attention(q, kc, vc, c, D ** -0.5, ks, vs)), None, 2 * B * NQ * L * L * D
     if name == "gemm_gate_up_silu256":
         from ..ops.torch_ref import interleave_gate_up
@@ -159,12 +174,57 @@ def time_case(name: str, iters: int = 20) -> dict:
     return out
 
 
+def gemm_sweep(ms=(1, 16, 64, 128, 256), iters: int = 20) -> None:
+    """Our tcgen05 GEMM (autotuned) against cuBLAS (torch.matmul) on the Qwen3-8B decode shapes.
+
+    One JSON line per (shape, m): median CUDA-event time of each over `iters` launches, every
+    launch after a 256 MiB read (cold L2, as when a layer's weights are used in a forward).
+    """
+    ops = CudaOps()
+    flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+    hbm, tfl, src = _peaks()
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            flush.sum()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(ts)
+
+    for name, (n, k) in DECODE_SHAPES.items():
+        w = (torch.randn(n, k, device="cuda") * 0.02).to(torch.bfloat16)
+        for m in ms:
+            x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+            out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+            ours = timed(lambda: ops.linear(x, w, out))
+            plan = dict(zip(("swap", "bn", "tiles_p", "tiles_q", "splits", "grid"), ops.last_plan))
+            cublas = timed(lambda: torch.matmul(x, w.t(), out=out))
+            nbytes = 2 * (m * k + n * k + m * n)
+            roof = max(nbytes / (hbm * 1e3), 2 * m * n * k / (tfl * 1e6))
+            print(json.dumps({"shape": name, "m": m, "n": n, "k": k, "ours_us": round(ours, 2),
+                              "cublas_us": round(cublas, 2), "ours_vs_cublas": round(cublas / ours, 3),
+                              "roofline_us": round(roof, 2), "frac_roofline": round(roof / ours, 3), "plan": plan,
+                              "l2": "256 MiB read before each launch", "peaks": src}), flush=True)
+        del w
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("case", choices=CASES + ("all",))
+    p.add_argument("case", choices=CASES + ("all", "gemm_sweep"))
     p.add_argument("--mode", choices=("time", "profile"), default="time")
     p.add_argument("--iters", type=int, default=20)
     a = p.parse_args(argv)
+    if a.case == "gemm_sweep":
+        gemm_sweep(iters=a.iters)
+        return
     names = CASES if a.case == "all" else (a.case,)
     for n in names:
         if a.mode == "profile":

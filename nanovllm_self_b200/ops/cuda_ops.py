@@ -38,6 +38,8 @@ class CudaOps:
         self.launches = 0
         self._plans: dict = {}
         self.last_plan = None
+        # prefill attention on the tcgen05 kernel (bf16 KV); False: the mma.sync kernel
+        self.prefill_tc = True
 
     def scratch(self, device) -> _Scratch:
         key = torch.device(device).index
@@ -137,7 +139,8 @@ class CudaOps:
             self.launches += 2 if splits > 1 else 1
         if B > nd:
             self.C.attn_prefill(q, k_cache, v_cache, k_scale, v_scale, ctx.block_tables, ctx.cu_seqlens_q,
-                                ctx.context_lens, out, nq, nkv, nd, B - nd, max(1, ctx.max_seqlen_q), float(scale))
+                                ctx.context_lens, out, nq, nkv, nd, B - nd, max(1, ctx.max_seqlen_q), float(scale),
+                                int(self.prefill_tc))
             self.launches += 1
         return out
 

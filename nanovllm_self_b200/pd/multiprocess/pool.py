@@ -62,6 +62,7 @@ class PDPool:
         self.dwd = [WorkDir(self.root / f"decode_{i}") for i in range(num_decode)]
         self.submitted = {}
         self.results = {}
+        self._seq = 0
 
     # ------------------------------------------------------------- lifecycle
     def _launch(self, role, idx, device, wd, rank):
@@ -128,7 +129,8 @@ class PDPool:
         est = estimate(row, index, int(row["max_tokens"]), RouterConfig())
         pm = self.p_router.route(est, now_s)
         dm = self.d_router.route(est, now_s)
-        base = f"r{index:06d}"
+        base = f"r{self._seq:06d}"  # unique over the pool's lifetime (several runs may share it)
+        self._seq += 1
         req = {"request_id": row.get("id", base), "prompt_ids": row["prompt_ids"], "max_tokens": row["max_tokens"],
                "temperature": row.get("temperature", 0.0), "ignore_eos": row.get("ignore_eos", True),
                "session_id": est.session_id, "decode_work_dir": str(self.dwd[dm["worker_id"]].path),
@@ -162,8 +164,43 @@ class PDPool:
                     done.append(base)
         return done
 
+    def dead_workers(self) -> list:
+        """(role, index, exit code) of every worker process that has exited."""
+        dead = []
+        roles = [("prefill", i) for i in range(self.P)] + [("decode", i) for i in range(self.D)]
+        for (role, idx), p in zip(roles, self.procs):
+            rc = p.poll()
+            if rc is not None:
+                dead.append((role, idx, rc))
+        return dead
+
+    def _fail_stuck(self, inflight: set, request_timeout_s: float | None) -> list:
+        """Mark in-flight requests routed to an exited worker, or older than the request
+        timeout (a lost control message), as failed; returns their bases."""
+        failed = []
+        dead = self.dead_workers() if self.procs else []
+        dead_p = {i for role, i, _ in dead if role == "prefill"}
+        dead_d = {i for role, i, _ in dead if role == "decode"}
+        now = time.time()
+        for base in list(inflight):
+            info = self.submitted[base]
+            why = None
+            if info["p"]["worker_id"] in dead_p:
+                why = f"prefill worker {info['p']['worker_id']} exited"
+            elif info["d"]["worker_id"] in dead_d:
+                why = f"decode worker {info['d']['worker_id']} exited"
+            elif request_timeout_s is not None and now - info["submit_time"] > request_timeout_s:
+                why = f"no completion within {request_timeout_s} s"
+            if why is not None and base not in self.results:
+                self.results[base] = {"error": why}
+                failed.append(base)
+        return failed
+
     def run(self, rows: list, concurrency: int | None = 4, rate: float | None = None, timeout_s: float = 3600.0,
-            seed: int = 0) -> dict:
+            seed: int = 0, request_timeout_s: float | None = None) -> dict:
+        """Drive `rows` through the pool.  A request whose worker exits, or (with
+        `request_timeout_s`) that does not complete in time, is recorded as an error instead of
+        stalling the run; `timeout_s` bounds the whole run."""
         rng = random.Random(seed)
         t0 = time.time()
         next_arrival = 0.0
@@ -181,6 +218,8 @@ class PDPool:
                     inflight.add(self.submit(rows[i], i, now))
                     i += 1
             for b in self._collect():
+                inflight.discard(b)
+            for b in self._fail_stuck(inflight, request_timeout_s):
                 inflight.discard(b)
             if time.time() - t0 > timeout_s:
                 raise TimeoutError("P/D pool run timed out")

@@ -159,6 +159,32 @@ def test_attention_decode_and_prefill(ops, kv_dtype, nq, nkv, bs):
     _close(out, ref, 0.02, 0.03)
 
 
+@pytest.mark.parametrize("nq,nkv,bs", [(32, 8, 256), (16, 8, 16), (64, 8, 256), (8, 8, 32), (16, 1, 256)])
+def test_prefill_tcgen05_matches_fp32(ops, nq, nkv, bs):
+    """The tcgen05 prefill kernel (bf16 KV): long prompts, prefix offsets, ragged tails."""
+    q_lens = [1000, 300, 129, 7, 512]
+    k_lens = [1000, 1300, 129, 700, 2100]
+    q, kc, vc, ks, vs, bt, cu, cl, tables = _paged_case(q_lens, k_lens, nq, nkv, bs, torch.bfloat16, seed=3)
+    ctx = _Ctx()
+    ctx.num_decode_seqs, ctx.num_seqs = 0, len(q_lens)
+    ctx.block_tables, ctx.cu_seqlens_q, ctx.context_lens = bt, cu, cl
+    ctx.max_seqlen_q, ctx.max_seqlen_k = max(q_lens), max(k_lens)
+    scale = 1 / math.sqrt(128)
+    ops.C.attn_error(True)
+    out = ops.attention(q.view(q.shape[0], -1), kc, vc, ctx, scale).view_as(q)
+    torch.cuda.synchronize()
+    assert ops.C.attn_error(True) == 0
+    ref = R.paged_attention(q.float(), kc, vc, q_lens, k_lens, tables, scale)
+    _close(out, ref, 0.02, 0.03)
+    # same answer as the mma.sync kernel
+    ops.prefill_tc = False
+    try:
+        out2 = ops.attention(q.view(q.shape[0], -1), kc, vc, ctx, scale).view_as(q)
+    finally:
+        ops.prefill_tc = True
+    _close(out, out2, 0.02, 0.03)
+
+
 def test_sample_greedy_and_temperature(ops):
     torch.manual_seed(0)
     V = 151936
