@@ -17,7 +17,9 @@ struct GemmPlan {
   int prefetch_w;    // stream the weights through an L2 prefetch lookahead
   int streamk;       // 1: stream-K (even split of tiles x k-blocks over the grid; needs ws + counters)
   int mt;            // 128-row sub-tiles of the token operand per output tile (1 or 2)
-  int dec;           // 1: decode kernel (all m <= 256 tokens per CTA, runtime bn, cluster split-K)
+  int dec;           // 1: decode kernel (all m <= 256 tokens per CTA, runtime bn, cluster split-K);
+                     // 2: skinny kernel (weights on the MMA's M side, mt = tokens per tile,
+                     //    bn = weight rows per CTA, cluster split-K)
   int stages, smem;  // decode kernel: weight-ring depth and dynamic shared memory
   int a_stages;      // decode kernel: activation-ring depth
 };
@@ -29,6 +31,10 @@ GemmPlan gemm_plan(int m, int n, int k, int force_swap, int force_bn, int force_
 // The rank-th cheapest decode-kernel configuration for C[m, n] (m <= 256) by the cost
 // model; false if there is none.
 bool gemm_dec_plan(int m, int n, int k, int rank, GemmPlan* plan);
+
+// The rank-th skinny-kernel configuration (fewest bytes per CTA first) for C[m, n], m <= 256;
+// false if there is none.
+bool gemm_skinny_plan(int m, int n, int k, int rank, int act, GemmPlan* plan);
 
 // Decode kernel with an explicit (bn, splits, activation-ring depth) configuration.
 cudaError_t gemm_dec_explicit(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m,

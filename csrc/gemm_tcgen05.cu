@@ -1369,6 +1369,361 @@ cudaError_t run_dec(const DecCfg& d, const void* x, int64_t ldx, const void* w, 
   return cudaLaunchKernelEx(&cfg, gemm_dec_kernel<1>, mx, mw, p);
 }
 
+
+// ------------------------------------------------------------------ skinny decode GEMM
+// Decode-sized GEMM with the WEIGHTS on the MMA's M side (tensor-core "swap" form):
+// D[i, j] = sum_k W[i, k] X[j, k] on tiles of MW x 128 weight rows (one M = 128 MMA each)
+// by NP tokens (the MMA's N: m rounded up to a multiple of 16, <= 256), so a 1-token step
+// moves 16 activation rows per k-block instead of 128 and every shared-memory byte but
+// those few is a weight byte.  The K range of a tile is split over the `splits` CTAs of a
+// thread-block cluster; every CTA exports its fp32 accumulator transposed ([token][feature])
+// into its idle stage ring and, after a cluster barrier, CTA r sums its share of the
+// features over the peers through distributed shared memory and stores whole 16-byte runs
+// of C rows (optionally SiLU-and-mul of interleaved gate/up rows, or the tensor-parallel
+// reduce-scatter destinations of GemmRsEpilogue).  Warps: 0 TMA (weights are loaded before
+// griddepcontrol.wait: they do not depend on the previous kernel), 1 TMEM + MMA, 2-5
+// TMEM export; all six warps reduce and store.
+struct SkParams {
+  int m, n, k;
+  int np;            // MMA N (tokens per tile, multiple of 16)
+  int mw;            // 128-row weight sub-tiles per CTA (1 or 2)
+  int splits, kb_per_split, num_kb, stages;
+  int act;           // 1: SiLU-and-mul epilogue (gate/up rows interleaved in groups of 16)
+  uint32_t idesc;
+  __nv_bfloat16* c;
+  int64_t ldc;
+  GemmRsEpilogue rs;
+};
+
+__device__ __forceinline__ __nv_bfloat16* sk_row(const SkParams& p, int j) {
+  if (p.rs.rows > 0) {
+    const int o = j / p.rs.rows;
+    return static_cast<__nv_bfloat16*>(p.rs.dst[o]) + (int64_t)(j - o * p.rs.rows) * p.ldc;
+  }
+  return p.c + (int64_t)j * p.ldc;
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+constexpr int SK_XLD = BM + 4;  // export row stride (floats): [token][128 features + pad]
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_skinny_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                       SkParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int W_BYTES = p.mw * BM * BK * 2;
+  const int X_BYTES = p.np * BK * 2;
+  const int STAGE = W_BYTES + X_BYTES;  // multiple of 2 KB: every operand tile stays 1024-aligned
+  const int S = p.stages;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * STAGE);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * S + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 2);
+  const uint32_t bar0 = smem_u32(bars);
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto empty = [&](int s) { return bar0 + 8u * (S + s); };
+  const uint32_t tfull = bar0 + 8u * (2 * S);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t tmem_cols = 32;
+  while (tmem_cols < (uint32_t)(p.mw * p.np)) tmem_cols <<= 1;
+
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const int split = (int)rank;
+  const int tq = blockIdx.x / p.splits;
+  const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+  const int nkb = kb1 > kb0 ? kb1 - kb0 : 0;
+  const int wrow0 = tq * p.mw * BM;  // first weight row (output feature) of this tile
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    mbar_init(tfull, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();  // the whole grid is resident (one wave): the next kernel may launch
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------------ producer
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_x)) : "memory");
+    const int pre = nkb < S ? nkb : S;
+    for (int i = 0; i < pre; ++i) {  // weights first: independent of the previous kernel
+      const int kb = kb0 + i;
+      mbar_arrive_expect_tx(full(i), (uint32_t)STAGE);
+      for (int w = 0; w < p.mw; ++w)
+        tma_load_2d(smem_u32(smem + i * STAGE + w * BM * BK * 2), &map_w, full(i), kb * BK, wrow0 + w * BM);
+    }
+    pdl_wait();  // the activations come from the previous kernel
+    for (int i = 0; i < pre; ++i) tma_load_2d(smem_u32(smem + i * STAGE + W_BYTES), &map_x, full(i), (kb0 + i) * BK, 0);
+    bool ok = true;
+    uint32_t it = pre;
+    for (int i = pre; i < nkb; ++i, ++it) {
+      const int s = i % S;
+      if (!mbar_wait(empty(s), ((i / S) & 1) ^ 1, abort_flag, 20)) {
+        ok = false;
+        break;
+      }
+      const int kb = kb0 + i;
+      mbar_arrive_expect_tx(full(s), (uint32_t)STAGE);
+      for (int w = 0; w < p.mw; ++w)
+        tma_load_2d(smem_u32(smem + s * STAGE + w * BM * BK * 2), &map_w, full(s), kb * BK, wrow0 + w * BM);
+      tma_load_2d(smem_u32(smem + s * STAGE + W_BYTES), &map_x, full(s), kb * BK, 0);
+    }
+    if (!ok) {
+      const uint32_t n = it < (uint32_t)S ? it : (uint32_t)S;
+      for (uint32_t j = it - n; j < it; ++j) mbar_drain(full(j % S), (j / S) & 1);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------------ MMA issuer
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % S;
+      if (!mbar_wait(full(s), (i / S) & 1, abort_flag, 21)) break;
+      tc_fence_after();
+      const uint32_t st = smem_u32(smem + s * STAGE);
+      const uint64_t xd = sdesc(st + W_BYTES);
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k)
+        for (int w = 0; w < p.mw; ++w)
+          tc_mma(tmem_base + w * p.np, sdesc(st + w * BM * BK * 2) + 2 * k, xd + 2 * k, p.idesc,
+                 (i > 0 || k > 0) ? 1u : 0u);
+      tc_commit(empty(s));
+    }
+    tc_commit(tfull);
+  }
+  __syncwarp();
+  bool acc_ok = true;
+  if (warp >= 2) {
+    acc_ok = (warp == 2 ? mbar_wait : mbar_wait_sleep)(tfull, 0, abort_flag, 22);
+    tc_fence_after();
+  }
+  pdl_wait();  // C (or a peer's receive slot) may still be read by the previous kernel
+  float* xp = reinterpret_cast<float*>(smem);  // export [token][SK_XLD] over the idle ring
+  const uint32_t xbase = smem_u32(xp);
+  const int fpr = ((BM / p.splits + 7) / 8) * 8;  // features per CTA in the reduction (multiple of 8)
+  const int f0 = split * fpr, f1 = min(BM, f0 + fpr);
+  for (int w = 0; w < p.mw; ++w) {
+    if (warp >= 2 && acc_ok) {
+      const int q4 = warp & 3;
+      const int r = q4 * 32 + lane;  // feature row of this thread inside sub-tile w
+      for (int c0 = 0; c0 < p.np; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem_base + ((uint32_t)(q4 * 32) << 16) + w * p.np + c0, v);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) xp[(c0 + e) * SK_XLD + r] = __uint_as_float(v[e]);
+      }
+    }
+    if (warp >= 2) tc_fence_before();
+    cluster_sync_all();  // every CTA's export of sub-tile w is visible cluster-wide
+    const int fbase = wrow0 + w * BM;  // output feature of row 0 of this sub-tile
+    if (p.act) {
+      // outputs: 16 per 32 rows (rows 32g..32g+15 gates, +16 the ups); items = 8 outputs
+      const int g0 = f0 / 32, g1 = (f1 + 31) / 32;
+      const int per_tok = (g1 - g0) * 2;
+      for (int it = threadIdx.x; it < p.m * per_tok; it += NUM_THREADS) {
+        const int j = it / per_tok, q = it % per_tok;
+        const int g = g0 + q / 2, half = q % 2;
+        const int rg = g * 32 + half * 8;  // gate rows rg..rg+7, up rows rg+16..rg+23
+        if (rg < f0 || rg >= f1 || fbase + rg >= p.n) continue;
+        float gv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, uv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int s2 = 0; s2 < p.splits; ++s2) {
+          const uint32_t a = xbase + (uint32_t)(j * SK_XLD + rg) * 4u;
+          float4 x0 = ld_dsmem_f32x4(a, s2), x1 = ld_dsmem_f32x4(a + 16u, s2);
+          float4 y0 = ld_dsmem_f32x4(a + 64u, s2), y1 = ld_dsmem_f32x4(a + 80u, s2);
+          gv[0] += x0.x; gv[1] += x0.y; gv[2] += x0.z; gv[3] += x0.w;
+          gv[4] += x1.x; gv[5] += x1.y; gv[6] += x1.z; gv[7] += x1.w;
+          uv[0] += y0.x; uv[1] += y0.y; uv[2] += y0.z; uv[3] += y0.w;
+          uv[4] += y1.x; uv[5] += y1.y; uv[6] += y1.z; uv[7] += y1.w;
+        }
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = silu_f(gv[e]) * uv[e];
+        const int oc = (fbase + g * 32) / 2 + half * 8;
+        *reinterpret_cast<uint4*>(sk_row(p, j) + oc) = f32_to_bf16x8(o);
+      }
+    } else {
+      const int per_tok = (f1 - f0 + 7) / 8;
+      for (int it = threadIdx.x; it < p.m * per_tok; it += NUM_THREADS) {
+        const int j = it / per_tok, f = f0 + (it % per_tok) * 8;
+        const int feat = fbase + f;
+        if (f >= f1 || feat >= p.n) continue;
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int s2 = 0; s2 < p.splits; ++s2) {
+          const uint32_t a = xbase + (uint32_t)(j * SK_XLD + f) * 4u;
+          const float4 x0 = ld_dsmem_f32x4(a, s2), x1 = ld_dsmem_f32x4(a + 16u, s2);
+          acc[0] += x0.x; acc[1] += x0.y; acc[2] += x0.z; acc[3] += x0.w;
+          acc[4] += x1.x; acc[5] += x1.y; acc[6] += x1.z; acc[7] += x1.w;
+        }
+        __nv_bfloat16* dst = sk_row(p, j) + feat;
+        if (feat + 8 <= p.n) {
+          *reinterpret_cast<uint4*>(dst) = f32_to_bf16x8(acc);
+        } else {
+          for (int e = 0; e < 8 && feat + e < p.n; ++e) dst[e] = __float2bfloat16(acc[e]);
+        }
+      }
+    }
+    cluster_sync_all();  // peers are done reading this CTA's export before it is overwritten / freed
+  }
+  if (p.rs.rows > 0) {
+    __syncthreads();
+    if (threadIdx.x == 0) dec_rs_arrive(p.rs);
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
+  }
+}
+
+struct SkCfg {
+  int np, mw, splits, kb_per_split, stages, smem, tiles;
+};
+
+int sk_smem(int np, int mw, int stages) {
+  const int stage = mw * BM * BK * 2 + np * BK * 2;
+  const int ring = stages * stage;
+  const int exportb = np * SK_XLD * 4;
+  return 1024 + (ring > exportb ? ring : exportb) + 8 * (2 * stages + 4);
+}
+
+int sk_capacity(int splits, int smem) {
+  // CTAs of `splits`-wide clusters of this shape that can be resident at once (cached)
+  static std::map<std::pair<int, int>, int> cache;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  auto key = std::make_pair(splits, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaFuncSetAttribute(gemm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM_MAX);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(splits * 64, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_skinny_kernel, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = num_sms() / splits;
+  }
+  cache[key] = n * splits;
+  return n * splits;
+}
+
+// Skinny-kernel configurations for C[m, n] (m <= 256) that run in ONE wave, fewest bytes per
+// CTA first: (weight slice + activation rows of its K range) per CTA, plus its fp32 export.
+std::vector<SkCfg> sk_candidates(int m, int n, int k, int act) {
+  std::vector<SkCfg> out;
+  if (m <= 0 || m > 256 || k % BK || (act && n % 32)) return out;
+  const int np = ((m + 15) / 16) * 16;
+  const int num_kb = k / BK;
+  std::vector<std::pair<double, SkCfg>> scored;
+  for (int mw = 1; mw <= 2; ++mw) {
+    if (mw * np > 512) continue;
+    const int tiles = (n + mw * BM - 1) / (mw * BM);
+    const int stage = mw * BM * BK * 2 + np * BK * 2;
+    int prev = 0;
+    for (int sp = 1; sp <= 8; ++sp) {
+      const int kbs = (num_kb + sp - 1) / sp;
+      const int s_eff = (num_kb + kbs - 1) / kbs;
+      if (s_eff == prev) continue;
+      prev = s_eff;
+      // deepest ring that fits one CTA per SM, and the deepest that fits two
+      for (int two = 0; two < 2; ++two) {
+        const int budget = two ? DEC_SMEM_MAX / 2 - 2048 : DEC_SMEM_MAX;
+        int st = (budget - 1024 - 8 * 20) / stage;
+        if (st > 12) st = 12;
+        if (st > kbs) st = kbs < 2 ? 2 : kbs;
+        if (st < 2) continue;
+        const int smem = sk_smem(np, mw, st);
+        if (smem > budget) continue;
+        const int cap = sk_capacity(s_eff, smem);
+        const int units = tiles * s_eff;
+        if (units > cap) continue;  // one wave only
+        SkCfg c{np, mw, s_eff, kbs, st, smem, tiles};
+        const double bytes = (double)kbs * stage + (s_eff > 1 ? 2.0 * np * BM * 4 * mw : 0.0);
+        scored.push_back({bytes, c});
+      }
+    }
+  }
+  std::sort(scored.begin(), scored.end(), [](const auto& a, const auto& b) { return a.first < b.first; });
+  for (auto& s : scored) out.push_back(s.second);
+  return out;
+}
+
+cudaError_t run_skinny(const SkCfg& d, const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc,
+                       int m, int n, int k, cudaStream_t stream, int act = 0, const GemmRsEpilogue* rs = nullptr) {
+  if (m > 256 || k % BK || (act && n % 32) || ldc % 8) return cudaErrorInvalidValue;
+  CUtensorMap mx, mw;
+  if (!make_map(&mx, x, m, k, ldx, d.np) || !make_map(&mw, w, n, k, ldw, BM)) return cudaErrorInvalidValue;
+  SkParams p;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.np = d.np;
+  p.mw = d.mw;
+  p.splits = d.splits;
+  p.kb_per_split = d.kb_per_split;
+  p.num_kb = k / BK;
+  p.stages = d.stages;
+  p.act = act;
+  // D f32, A bf16 (weights), B bf16 (tokens), N = np, M = 128
+  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(d.np >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  p.c = static_cast<__nv_bfloat16*>(c);
+  p.ldc = ldc;
+  if (rs) {
+    if (act || rs->rows <= 0 || rs->world < 1 || rs->world > 8 || !rs->calls || !rs->ctas_done ||
+        (int64_t)rs->rows * rs->world < m)
+      return cudaErrorInvalidValue;
+    for (int r = 0; r < rs->world; ++r)
+      if (!rs->dst[r] || !rs->flag[r] || ((uintptr_t)rs->dst[r] & 15)) return cudaErrorInvalidValue;
+    p.rs = *rs;
+  } else if (!c || ((uintptr_t)c & 15)) {
+    return cudaErrorInvalidValue;
+  }
+  static std::atomic<uint64_t> done{0};
+  cudaError_t e = smem_opt_in(done, gemm_skinny_kernel, DEC_SMEM_MAX);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(d.tiles * d.splits, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = d.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = d.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, gemm_skinny_kernel, mw, mx, p);
+}
+
 }  // namespace
 
 cudaError_t gemm_dec_explicit(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m,
@@ -1405,6 +1760,40 @@ static std::vector<GemmPlan> dec_plans_for_tuning(int m, int n, int k, int each,
     }
   }
   return out;
+}
+
+// Skinny-kernel plans (dec = 2): mt = tokens per tile (MMA N), bn = weight rows per CTA.
+static std::vector<GemmPlan> skinny_plans_for_tuning(int m, int n, int k, int each, int act) {
+  std::vector<GemmPlan> out;
+  for (const auto& d : sk_candidates(m, n, k, act)) {
+    if ((int)out.size() >= each) break;
+    GemmPlan pl{};
+    pl.dec = 2;
+    pl.mt = d.np;
+    pl.bn = d.mw * BM;
+    pl.splits = d.splits;
+    pl.kb_per_split = d.kb_per_split;
+    pl.num_kb = k / BK;
+    pl.stages = d.stages;
+    pl.smem = d.smem;
+    pl.tiles = d.tiles;
+    pl.tiles_p = 1;
+    pl.tiles_q = d.tiles;
+    pl.grid = d.tiles * d.splits;
+    out.push_back(pl);
+  }
+  return out;
+}
+
+bool gemm_skinny_plan(int m, int n, int k, int rank, int act, GemmPlan* plan) {
+  const auto v = skinny_plans_for_tuning(m, n, k, rank + 1, act);
+  if (rank < 0 || rank >= (int)v.size()) return false;
+  *plan = v[rank];
+  return true;
+}
+
+static SkCfg plan_to_skinny(const GemmPlan& pl) {
+  return SkCfg{pl.mt, pl.bn / BM, pl.splits, pl.kb_per_split, pl.stages, pl.smem, pl.tiles};
 }
 
 static GemmPlan dec_to_plan(const DecCfg& d, int k) {
@@ -1509,6 +1898,10 @@ cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, vo
   if (k % 8 || ldx % 8 || ldw % 8) return cudaErrorInvalidValue;
   if (((uintptr_t)x & 15) || ((uintptr_t)w & 15)) return cudaErrorMisalignedAddress;
   if (!pl.swap && (ldc % 8 || ((uintptr_t)c & 15))) return cudaErrorInvalidValue;
+  if (pl.dec == 2) {
+    if (m > pl.mt || k % BK) return cudaErrorInvalidValue;
+    return run_skinny(plan_to_skinny(pl), x, ldx, w, ldw, c, ldc, m, n, k, stream, act);
+  }
   if (pl.dec) {
     if (m > pl.mt * BM || k % BK) return cudaErrorInvalidValue;
     DecCfg d{pl.mt, pl.bn, pl.splits, pl.kb_per_split, pl.stages, pl.a_stages, pl.smem, pl.tiles, 0.0};
@@ -1632,8 +2025,10 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
     const int bq = m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256;
     for (int sp : {1, 2, 3, 4}) cands.push_back(gemm_plan(m, n, k, 1, bq, sp));
   }
-  if (m <= 2 * BM && k % BK == 0)
+  if (m <= 2 * BM && k % BK == 0) {
     for (const auto& d : dec_plans_for_tuning(m, n, k, 6, act)) cands.push_back(d);
+    for (const auto& d : skinny_plans_for_tuning(m, n, k, 6, act)) cands.push_back(d);
+  }
   if (ws && counters) {
     for (int bn : {256, 128}) {
       cands.push_back(gemm_plan(m, n, k, 0, bn, -1));
@@ -1709,6 +2104,7 @@ cudaError_t gemm_bf16_rs(const void* x, int64_t ldx, const void* w, int64_t ldw,
   }
   if (!have) {
     std::vector<GemmPlan> cands = dec_plans_for_tuning(m, n, k, 6, 0);
+    for (const auto& d : skinny_plans_for_tuning(m, n, k, 6, 0)) cands.push_back(d);
     if (cands.empty()) return cudaErrorNotSupported;
     best = cands[0];
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
@@ -1727,8 +2123,7 @@ cudaError_t gemm_bf16_rs(const void* x, int64_t ldx, const void* w, int64_t ldw,
       cudaEventCreate(&e1);
       float best_ms = 1e30f;
       for (const auto& pl : cands) {
-        DecCfg dc{pl.mt, pl.bn, pl.splits, pl.kb_per_split, pl.stages, pl.a_stages, pl.smem, pl.tiles, 0.0};
-        if (run_dec(dc, x, ldx, w, ldw, tune_c, tune_ldc, m, n, k, stream) != cudaSuccess) {
+        if (gemm_bf16(x, ldx, w, ldw, tune_c, tune_ldc, m, n, k, pl, nullptr, nullptr, stream, 0) != cudaSuccess) {
           cudaGetLastError();
           continue;
         }
@@ -1739,7 +2134,7 @@ cudaError_t gemm_bf16_rs(const void* x, int64_t ldx, const void* w, int64_t ldw,
             l2_evict_kernel<<<num_sms() * 4, 256, 0, stream>>>(static_cast<const uint4*>(flush), flush_bytes / 16 - 16,
                                                               static_cast<int*>(flush) + (flush_bytes / 4 - 1));
           cudaEventRecord(e0, stream);
-          good = run_dec(dc, x, ldx, w, ldw, tune_c, tune_ldc, m, n, k, stream) == cudaSuccess;
+          good = gemm_bf16(x, ldx, w, ldw, tune_c, tune_ldc, m, n, k, pl, nullptr, nullptr, stream, 0) == cudaSuccess;
           cudaEventRecord(e1, stream);
           cudaEventSynchronize(e1);
           float ms = 0.f;
@@ -1759,6 +2154,7 @@ cudaError_t gemm_bf16_rs(const void* x, int64_t ldx, const void* w, int64_t ldw,
     }
   }
   if (chosen) *chosen = best;
+  if (best.dec == 2) return run_skinny(plan_to_skinny(best), x, ldx, w, ldw, nullptr, ldc, m, n, k, stream, 0, &rs);
   DecCfg dc{best.mt, best.bn, best.splits, best.kb_per_split, best.stages, best.a_stages, best.smem, best.tiles, 0.0};
   return run_dec(dc, x, ldx, w, ldw, nullptr, ldc, m, n, k, stream, 0, &rs);
 }

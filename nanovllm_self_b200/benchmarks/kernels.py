@@ -216,14 +216,69 @@ def gemm_sweep(ms=(1, 16, 64, 128, 256), iters: int = 20) -> None:
         del w
 
 
+def gemm_one(m: int, n: int, k: int, impl: str, mode: str, iters: int = 20) -> None:
+    """One GEMM shape with one implementation: ``tuned`` (the autotuner's pick), ``cublas``
+    (torch.matmul), ``skinny:R`` / ``dec:R`` (the R-th configuration of that kernel's model)."""
+    ops = CudaOps()
+    x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(n, k, device="cuda") * 0.02).to(torch.bfloat16)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    kind, _, rank = impl.partition(":")
+    info = {}
+    if kind == "tuned":
+        def fn():
+            ops.linear(x, w, out)
+    elif kind == "cublas":
+        def fn():
+            torch.matmul(x, w.t(), out=out)
+    elif kind == "skinny":
+        def fn():
+            info["cfg"] = ops.C.linear_skinny(x, w, out, int(rank or 0), 0)
+    elif kind == "dec":
+        def fn():
+            info["cfg"] = ops.C.linear_dec(x, w, out, int(rank or 0), 0)
+    else:
+        raise ValueError(impl)
+    fn()
+    torch.cuda.synchronize()
+    ref = x.float() @ w.float().t()
+    err = ((out.float() - ref).abs().max() / ref.abs().max()).item()
+    if mode == "profile":
+        torch.cuda.profiler.start()
+        fn()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"gemm": [m, n, k], "impl": impl, "profiled_launches": 1, "rel_err": err, **info}))
+        return
+    flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+    ts = []
+    for _ in range(iters):
+        flush.sum()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    print(json.dumps({"gemm": [m, n, k], "impl": impl, "us": round(statistics.median(ts), 2), "rel_err": err,
+                      "plan": ops.last_plan if kind == "tuned" else info.get("cfg")}))
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("case", choices=CASES + ("all", "gemm_sweep"))
+    p.add_argument("case", choices=CASES + ("all", "gemm_sweep", "gemm_one"))
+    p.add_argument("--m", type=int, default=1)
+    p.add_argument("--n", type=int, default=6144)
+    p.add_argument("--k", type=int, default=4096)
+    p.add_argument("--impl", default="tuned")
     p.add_argument("--mode", choices=("time", "profile"), default="time")
     p.add_argument("--iters", type=int, default=20)
     a = p.parse_args(argv)
     if a.case == "gemm_sweep":
         gemm_sweep(iters=a.iters)
+        return
+    if a.case == "gemm_one":
+        gemm_one(a.m, a.n, a.k, a.impl, a.mode, a.iters)
         return
     names = CASES if a.case == "all" else (a.case,)
     for n in names:

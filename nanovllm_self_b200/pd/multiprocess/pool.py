@@ -32,7 +32,8 @@ def _pct(xs, q):
 class PDPool:
     def __init__(self, work_root, num_prefill=1, num_decode=1, backend="shared_memory", model="tiny",
                  prefill_devices=None, decode_devices=None, policy="load_aware", worker_args=None,
-                 handshake_timeout_s=120.0, nccl_port=29650, python=sys.executable, tp=1, device_kind="cuda"):
+                 handshake_timeout_s=120.0, nccl_port=29650, python=sys.executable, tp=1, device_kind="cuda",
+                 gpu_base=0):
         self.root = Path(work_root)
         self.root.mkdir(parents=True, exist_ok=True)
         self.P, self.D = num_prefill, num_decode
@@ -42,6 +43,7 @@ class PDPool:
         # (prefill group i on GPUs [i tp, (i+1) tp), decode group j after all prefill groups)
         self.tp = tp
         self.device_kind = device_kind
+        self.gpu_base = gpu_base  # tp > 1: first GPU of this pool's groups
         if tp > 1 and backend == "sync_gpu":
             raise ValueError("sync_gpu P/D workers are TP=1; use ipc_push or shared_memory with tp > 1")
         if tp > 1:
@@ -71,7 +73,7 @@ class PDPool:
                 "--handshake-timeout-s", str(self.timeout)] + self.worker_args
         if self.tp > 1:
             # one torchrun per group; its ranks form the group's TP world
-            offset = rank * self.tp if self.device_kind == "cuda" else 0
+            offset = self.gpu_base + rank * self.tp if self.device_kind == "cuda" else 0
             cmd = [self.python, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={self.tp}",
                    "--master-addr=127.0.0.1", f"--master-port={self.nccl_port + 1 + rank}",
                    "-m", "nanovllm_self_b200.pd.multiprocess.workers"] + args + \

@@ -220,6 +220,33 @@ def test_gemm_tcgen05(ops, m, n, k):
     assert ops.C.gemm_error(True) == 0
 
 
+@pytest.mark.parametrize("m,n,k,act", [
+    (1, 6144, 4096, 0), (7, 4096, 512, 0), (16, 4096, 12288, 0), (33, 1536, 2048, 0), (64, 24576, 4096, 1),
+    (100, 4096, 4096, 0), (200, 2304, 1024, 0), (256, 6144, 4096, 0), (5, 3072, 1024, 1), (129, 768, 4096, 1),
+])
+def test_gemm_skinny_configs(ops, m, n, k, act):
+    """The skinny kernel (weights on the MMA's M side, cluster split-K) over its top configurations."""
+    from nanovllm_self_b200.ops.torch_ref import interleave_gate_up
+    g = torch.Generator(device=DEV).manual_seed(m * 13 + n)
+    x = (torch.randn(m, k, device=DEV, generator=g) * 0.5).bfloat16()
+    w = (torch.randn(n, k, device=DEV, generator=g) * 0.02).bfloat16()
+    ref = x.float() @ w.float().t()
+    if act:
+        gate, up = ref[:, : n // 2], ref[:, n // 2:]
+        ref = torch.nn.functional.silu(gate) * up
+        w = interleave_gate_up(w[: n // 2], w[n // 2:]).contiguous()
+    ran = 0
+    for rank in range(4):
+        out = torch.full((m, n // 2 if act else n), float("nan"), device=DEV, dtype=torch.bfloat16)
+        cfg = ops.C.linear_skinny(x, w, out, rank, act)
+        if not cfg:
+            break
+        ran += 1
+        _close(out, ref, 0.01 * math.sqrt(k / 1024) * 0.5, 0.02)
+    assert ran > 0
+    assert ops.C.gemm_error(True) == 0
+
+
 @pytest.mark.parametrize("swap,bn,splits", [(0, 256, 1), (0, 128, 3), (1, 32, 1), (1, 64, 4), (1, 256, 2), (0, 64, 1)])
 def test_gemm_forced_configs(ops, swap, bn, splits):
     m, n, k = 200, 1280, 2048
