@@ -176,6 +176,44 @@ void sample(const at::Tensor& logits, int64_t col_offset, const at::Tensor& temp
         "sample");
 }
 
+// Row-parallel sampler (greedy / temperature / top-p); with xbases / fbases (every rank's
+// exchange and flag areas of the symmetric buffer, as integers) the vocabulary shards of a
+// tensor-parallel group are combined inside the kernel.
+void sample_rows(const at::Tensor& logits, int64_t col_offset, const at::Tensor& temps,
+                 const c10::optional<at::Tensor>& top_p, const at::Tensor& seed_step, at::Tensor& out_tok,
+                 const c10::optional<at::Tensor>& out_val, std::vector<int64_t> xbases, std::vector<int64_t> fbases,
+                 int64_t rank, int64_t rows_cap, int64_t timeout_ns) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits [rows, V]");
+  TORCH_CHECK(temps.scalar_type() == at::kFloat, "temps fp32");
+  TORCH_CHECK(!top_p.has_value() || top_p->scalar_type() == at::kFloat, "top_p fp32");
+  TORCH_CHECK(seed_step.scalar_type() == at::kLong && seed_step.numel() >= 2, "seed_step int64[2]");
+  TORCH_CHECK(xbases.size() == fbases.size() && xbases.size() <= 8, "exchange areas");
+  int bf16 = logits.scalar_type() == at::kBFloat16;
+  TORCH_CHECK(bf16 || logits.scalar_type() == at::kFloat, "logits bf16 or fp32");
+  nvb::SampleX X;
+  if (xbases.size() > 1) {
+    X.world = (int)xbases.size();
+    X.rank = (int)rank;
+    X.rows_cap = (int)rows_cap;
+    for (size_t p = 0; p < xbases.size(); ++p) {
+      X.x[p] = reinterpret_cast<float*>(xbases[p]);
+      X.f[p] = reinterpret_cast<uint32_t*>(fbases[p]);
+    }
+    X.ctrl = X.f[rank] + 4LL * rows_cap * X.world;
+    if (timeout_ns > 0) X.timeout_ns = (uint64_t)timeout_ns;
+  }
+  at::cuda::CUDAGuard g(logits.device());
+  check(nvb::launch_sample_rows(logits.data_ptr(), bf16, logits.stride(0), (int)logits.size(0), (int)logits.size(1),
+                                col_offset, temps.data_ptr<float>(), ptr_or_null<float>(top_p),
+                                seed_step.data_ptr<int64_t>(), out_tok.data_ptr<int>(), ptr_or_null<float>(out_val), X,
+                                stream()),
+        "sample_rows");
+}
+
+int64_t sample_x_floats(int64_t world, int64_t rows_cap) { return nvb::sample_x_floats((int)world, (int)rows_cap); }
+int64_t sample_f_words(int64_t world, int64_t rows_cap) { return nvb::sample_f_words((int)world, (int)rows_cap); }
+int64_t sample_error(bool reset) { return nvb::sample_error_code(reset ? 1 : 0); }
+
 }  // namespace
 
 void register_gemm(pybind11::module& m);
@@ -197,6 +235,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_error", &attn_error, pybind11::arg("reset") = false);
   m.def("sample_chunks", &sample_chunks);
   m.def("sample", &sample);
+  m.def("sample_rows", &sample_rows, pybind11::arg("logits"), pybind11::arg("col_offset"), pybind11::arg("temps"),
+        pybind11::arg("top_p"), pybind11::arg("seed_step"), pybind11::arg("out_tok"), pybind11::arg("out_val"),
+        pybind11::arg("xbases") = std::vector<int64_t>{}, pybind11::arg("fbases") = std::vector<int64_t>{},
+        pybind11::arg("rank") = 0, pybind11::arg("rows_cap") = 0, pybind11::arg("timeout_ns") = 0);
+  m.def("sample_x_floats", &sample_x_floats);
+  m.def("sample_f_words", &sample_f_words);
+  m.def("sample_rows_capacity", &nvb::sample_rows_capacity);
+  m.def("sample_error", &sample_error, pybind11::arg("reset") = false);
   register_gemm(m);
   register_comm(m);
 }

@@ -35,6 +35,9 @@ bool gemm_dec_plan(int m, int n, int k, int rank, GemmPlan* plan);
 // The rank-th skinny-kernel configuration (fewest bytes per CTA first) for C[m, n], m <= 256;
 // false if there is none.
 bool gemm_skinny_plan(int m, int n, int k, int rank, int act, GemmPlan* plan);
+// Skinny kernel with W in the blocked layout [n / 128][k / 64][128][64] (blocked = 1) or row-major.
+cudaError_t gemm_skinny_run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n,
+                            int k, const GemmPlan& plan, int act, int blocked, cudaStream_t stream);
 
 // Decode kernel with an explicit (bn, splits, activation-ring depth) configuration.
 cudaError_t gemm_dec_explicit(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m,

@@ -153,18 +153,23 @@ std::vector<int64_t> linear_rs(const at::Tensor& x, const at::Tensor& w, std::ve
 // Skinny kernel (weights on the MMA's M side) with the rank-th configuration by its traffic
 // model; returns (tokens per tile, weight rows per CTA, splits, stages), empty if none.
 std::vector<int64_t> linear_skinny(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, int64_t rank,
-                                   int64_t act) {
+                                   int64_t act, int64_t blocked) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
                   out.scalar_type() == at::kBFloat16, "bf16 required");
   TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "unit inner stride required");
-  const int m = (int)x.size(0), k = (int)x.size(1), n = (int)w.size(0);
-  TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == (act ? n / 2 : n), "shape mismatch");
+  const int m = (int)x.size(0), k = (int)x.size(1);
+  // blocked: w is [n / 128, k / 64, 128, 64]; otherwise [n, k]
+  const int n = blocked ? (int)(w.size(0) * 128) : (int)w.size(0);
+  TORCH_CHECK(blocked ? (w.dim() == 4 && w.size(1) * 64 == k && w.size(2) == 128 && w.size(3) == 64 && w.is_contiguous())
+                      : w.size(1) == k, "weight shape");
+  TORCH_CHECK(out.size(0) == m && out.size(1) == (act ? n / 2 : n), "shape mismatch");
   nvb::GemmPlan pl{};
   if (!nvb::gemm_skinny_plan(m, n, k, (int)rank, (int)act, &pl)) return {};
   at::cuda::CUDAGuard g(x.device());
-  cudaError_t e = nvb::gemm_bf16(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0),
-                                 m, n, k, pl, nullptr, nullptr, at::cuda::getCurrentCUDAStream().stream(), (int)act);
+  cudaError_t e = nvb::gemm_skinny_run(x.data_ptr(), x.stride(0), w.data_ptr(), blocked ? 64 : w.stride(0),
+                                       out.data_ptr(), out.stride(0), m, n, k, pl, (int)act, (int)blocked,
+                                       at::cuda::getCurrentCUDAStream().stream());
   TORCH_CHECK(e == cudaSuccess, "gemm_bf16 (skinny) failed: ", cudaGetErrorString(e));
   return {pl.mt, pl.bn, pl.splits, pl.stages};
 }
@@ -187,7 +192,8 @@ void register_gemm(pybind11::module& m) {
         pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("rank"), pybind11::arg("act") = 0);
   m.def("linear_dec_cfg", &linear_dec_cfg, "decode-sized tcgen05 GEMM with an explicit configuration");
   m.def("linear_skinny", &linear_skinny, "skinny tcgen05 GEMM (weights on M) with a ranked configuration",
-        pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("rank"), pybind11::arg("act") = 0);
+        pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("rank"), pybind11::arg("act") = 0,
+        pybind11::arg("blocked") = 0);
   m.def("linear_rs", &linear_rs, "tcgen05 decode GEMM whose rows are stored at their owner rank (reduce-scatter)");
   m.def("gemm_error", &error_code, pybind11::arg("reset") = false);
 }

@@ -1389,11 +1389,23 @@ struct SkParams {
   int mw;            // 128-row weight sub-tiles per CTA (1 or 2)
   int splits, kb_per_split, num_kb, stages;
   int act;           // 1: SiLU-and-mul epilogue (gate/up rows interleaved in groups of 16)
+  int blocked;       // 1: W stored as [n / 128][k / 64][128][64] (every TMA box one contiguous 16 KB)
   uint32_t idesc;
   __nv_bfloat16* c;
   int64_t ldc;
   GemmRsEpilogue rs;
 };
+
+// TMA coordinates of the weight box (128 rows from `row`, k-block kb).
+__device__ __forceinline__ void sk_wcoord(const SkParams& p, int row, int kb, int& x, int& y) {
+  if (p.blocked) {
+    x = 0;
+    y = ((row / BM) * p.num_kb + kb) * BM;
+  } else {
+    x = kb * BK;
+    y = row;
+  }
+}
 
 __device__ __forceinline__ __nv_bfloat16* sk_row(const SkParams& p, int j) {
   if (p.rs.rows > 0) {
@@ -1470,8 +1482,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int i = 0; i < pre; ++i) {  // weights first: independent of the previous kernel
       const int kb = kb0 + i;
       mbar_arrive_expect_tx(full(i), (uint32_t)STAGE);
-      for (int w = 0; w < p.mw; ++w)
-        tma_load_2d(smem_u32(smem + i * STAGE + w * BM * BK * 2), &map_w, full(i), kb * BK, wrow0 + w * BM);
+      for (int w = 0; w < p.mw; ++w) {
+        int wx, wy;
+        sk_wcoord(p, wrow0 + w * BM, kb, wx, wy);
+        tma_load_2d(smem_u32(smem + i * STAGE + w * BM * BK * 2), &map_w, full(i), wx, wy);
+      }
     }
     pdl_wait();  // the activations come from the previous kernel
     for (int i = 0; i < pre; ++i) tma_load_2d(smem_u32(smem + i * STAGE + W_BYTES), &map_x, full(i), (kb0 + i) * BK, 0);
@@ -1485,8 +1500,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       const int kb = kb0 + i;
       mbar_arrive_expect_tx(full(s), (uint32_t)STAGE);
-      for (int w = 0; w < p.mw; ++w)
-        tma_load_2d(smem_u32(smem + s * STAGE + w * BM * BK * 2), &map_w, full(s), kb * BK, wrow0 + w * BM);
+      for (int w = 0; w < p.mw; ++w) {
+        int wx, wy;
+        sk_wcoord(p, wrow0 + w * BM, kb, wx, wy);
+        tma_load_2d(smem_u32(smem + s * STAGE + w * BM * BK * 2), &map_w, full(s), wx, wy);
+      }
       tma_load_2d(smem_u32(smem + s * STAGE + W_BYTES), &map_x, full(s), kb * BK, 0);
     }
     if (!ok) {
@@ -1675,10 +1693,13 @@ std::vector<SkCfg> sk_candidates(int m, int n, int k, int act) {
 }
 
 cudaError_t run_skinny(const SkCfg& d, const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc,
-                       int m, int n, int k, cudaStream_t stream, int act = 0, const GemmRsEpilogue* rs = nullptr) {
+                       int m, int n, int k, cudaStream_t stream, int act = 0, const GemmRsEpilogue* rs = nullptr,
+                       int blocked = 0) {
   if (m > 256 || k % BK || (act && n % 32) || ldc % 8) return cudaErrorInvalidValue;
+  if (blocked && n % BM) return cudaErrorInvalidValue;
   CUtensorMap mx, mw;
-  if (!make_map(&mx, x, m, k, ldx, d.np) || !make_map(&mw, w, n, k, ldw, BM)) return cudaErrorInvalidValue;
+  const bool wok = blocked ? make_map(&mw, w, n * (k / BK), BK, BK, BM) : make_map(&mw, w, n, k, ldw, BM);
+  if (!make_map(&mx, x, m, k, ldx, d.np) || !wok) return cudaErrorInvalidValue;
   SkParams p;
   p.m = m;
   p.n = n;
@@ -1690,6 +1711,7 @@ cudaError_t run_skinny(const SkCfg& d, const void* x, int64_t ldx, const void* w
   p.num_kb = k / BK;
   p.stages = d.stages;
   p.act = act;
+  p.blocked = blocked;
   // D f32, A bf16 (weights), B bf16 (tokens), N = np, M = 128
   p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(d.np >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
   p.c = static_cast<__nv_bfloat16*>(c);
@@ -1794,6 +1816,12 @@ bool gemm_skinny_plan(int m, int n, int k, int rank, int act, GemmPlan* plan) {
 
 static SkCfg plan_to_skinny(const GemmPlan& pl) {
   return SkCfg{pl.mt, pl.bn / BM, pl.splits, pl.kb_per_split, pl.stages, pl.smem, pl.tiles};
+}
+
+cudaError_t gemm_skinny_run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n,
+                            int k, const GemmPlan& plan, int act, int blocked, cudaStream_t stream) {
+  if (plan.dec != 2) return cudaErrorInvalidValue;
+  return run_skinny(plan_to_skinny(plan), x, ldx, w, ldw, c, ldc, m, n, k, stream, act, nullptr, blocked);
 }
 
 static GemmPlan dec_to_plan(const DecCfg& d, int k) {

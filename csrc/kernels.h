@@ -51,4 +51,26 @@ cudaError_t launch_sample(const void* logits, int logits_is_bf16, int64_t ld, in
                           const float* temps, const int64_t* seed_step, float* part_val, int* part_idx, int nchunk,
                           int* out_tok, float* out_val, cudaStream_t stream);
 
+// Row-parallel sampler (one CTA per row): greedy / temperature / top-p over a vocabulary
+// shard, with the cross-rank combination inside the kernel when world > 1 (see sampling.cu).
+constexpr int SAMPLE_NB = 1024;  // histogram bins per level of the top-p threshold search
+struct SampleX {
+  int world = 1, rank = 0, rows_cap = 0;
+  float* x[8] = {};        // every rank's exchange area (floats; regions of rounds 1-4)
+  uint32_t* f[8] = {};     // every rank's flag words [4 rounds][rows_cap][world]
+  uint32_t* ctrl = nullptr;  // this rank's [0] completed calls, [1] finished CTAs
+  uint64_t timeout_ns = 10000000000ull;
+};
+// Floats of one rank's exchange area / words of its flag area for `rows_cap` rows.
+inline int64_t sample_x_floats(int world, int rows_cap) {
+  const int64_t wr = (int64_t)world * rows_cap;
+  return wr + wr * (SAMPLE_NB + 1) + wr * SAMPLE_NB + wr * 2;
+}
+inline int64_t sample_f_words(int world, int rows_cap) { return 4LL * rows_cap * world + 2; }
+int sample_rows_capacity();
+cudaError_t launch_sample_rows(const void* logits, int logits_is_bf16, int64_t ld, int rows, int V, int64_t col_offset,
+                               const float* temps, const float* top_p, const int64_t* seed_step, int* out_tok,
+                               float* out_val, const SampleX& X, cudaStream_t stream);
+int sample_error_code(int reset);
+
 }  // namespace nvb

@@ -234,6 +234,11 @@ def gemm_one(m: int, n: int, k: int, impl: str, mode: str, iters: int = 20) -> N
     elif kind == "skinny":
         def fn():
             info["cfg"] = ops.C.linear_skinny(x, w, out, int(rank or 0), 0)
+    elif kind == "skinnyb":  # weights in the blocked [n/128, k/64, 128, 64] layout
+        wb = w.view(n // 128, 128, k // 64, 64).permute(0, 2, 1, 3).contiguous()
+
+        def fn():
+            info["cfg"] = ops.C.linear_skinny(x, wb, out, int(rank or 0), 0, 1)
     elif kind == "dec":
         def fn():
             info["cfg"] = ops.C.linear_dec(x, w, out, int(rank or 0), 0)

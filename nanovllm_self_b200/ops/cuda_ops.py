@@ -149,7 +149,13 @@ class CudaOps:
                generator=None, use_top_p=False, col_offset=0):
         rows, V = logits.shape
         if use_top_p:
-            return R.sample(logits, temperatures, top_p, generator, batch_greedy_compat).to(torch.int32)
+            # one CTA per row: nucleus threshold by a two-level mass histogram, then Gumbel-max
+            # over the nucleus (no sort, no host sync); batch_greedy_compat is applied by the runner
+            tok = torch.empty(rows, dtype=torch.int32, device=logits.device)
+            tp = top_p.float() if top_p is not None else None
+            self.C.sample_rows(logits, int(col_offset), temperatures, tp, step, tok, None)
+            self.launches += 1
+            return tok
         sc = self.scratch(logits.device)
         nchunk = int(self.C.sample_chunks(rows, V))
         tok = torch.empty(rows, dtype=torch.int32, device=logits.device)

@@ -16,9 +16,10 @@ Here every reduction is fused with what follows it:
   buffers, see :mod:`nanovllm_self_b200.parallel.symm`); backend ``"nccl"`` is the
   reference's behaviour (NCCL all-reduce, then the local add+norm kernel) and is kept
   as the measured baseline.
-* ``vocab_parallel_sample``: each rank holds ``V / tp`` logits; the sampler reduces
-  its shard to one (score, token) pair per row (greedy or Gumbel-max with a shared
-  counter-based noise stream) and only those pairs cross the link.
+* ``vocab_parallel_sample``: each rank holds ``V / tp`` logits; one sampler kernel per
+  step reduces the shard and combines it with the other ranks' inside the kernel (per-row
+  (score, token) pairs, and for top-p the maxima and mass histograms, by peer stores into
+  the symmetric buffer); greedy, temperature and top-p, graph-capturable, no NCCL.
 """
 from __future__ import annotations
 
@@ -47,7 +48,8 @@ class TPComm:
             from .symm import SymmetricWorkspace
             c = runner.config
             rows = max(c.max_num_batched_tokens, c.cuda_graph_max_bs, c.max_num_seqs)
-            self.symm = SymmetricWorkspace(self.tp, rows=rows, hidden=runner.model.hidden_size)
+            self.symm = SymmetricWorkspace(self.tp, rows=rows, hidden=runner.model.hidden_size,
+                                           sample_rows=max(c.cuda_graph_max_bs, c.max_num_seqs))
         elif self.backend == "fused":
             self.backend = "nccl"  # CPU / gloo: no peer memory
 
@@ -88,8 +90,17 @@ class TPComm:
 
     # ------------------------------------------------------------- sampling
     def vocab_parallel_sample(self, logits, temps, topp, model, runner):
+        """Tokens of every row sampled over the whole vocabulary from this rank's shard.
+
+        Fused backend: one kernel per step; the per-row partials (maxima, top-p mass histograms,
+        (score, token) pairs) cross the ranks by peer stores into the symmetric buffer, so the
+        decode graph holds no NCCL call and no eager op.  NCCL backend (the baseline): the
+        (score, token) pairs are all-gathered, or for top-p the whole logits."""
         n = self.tp.size
         use_top_p = getattr(runner, "_use_top_p", False)
+        if self.symm is not None and logits.shape[0] <= self.symm.sample_cap:
+            return self.symm.sample_rows(logits, temps, topp if use_top_p else None, runner._step_tensor(),
+                                         model.vocab_start, self.ops)
         if runner.is_cuda and not use_top_p:
             val, tok = self.ops.sample_partial(logits, temps, runner._step_tensor(), model.vocab_start)
             pair = torch.stack([val, tok.float()], dim=1)  # token ids < 2^24 are exact in fp32
@@ -97,7 +108,7 @@ class TPComm:
             dist.all_gather_into_tensor(out, pair.contiguous(), group=self.tp.group)
             best = out[:, :, 0].argmax(dim=0)
             return out[best, torch.arange(pair.shape[0], device=pair.device), 1].to(torch.int32)
-        # top-p (or CPU): gather the full logits; every rank samples identically
+        # top-p on the NCCL baseline (or CPU): gather the full logits; every rank samples identically
         parts = [torch.empty_like(logits) for _ in range(n)]
         dist.all_gather(parts, logits.contiguous(), group=self.tp.group)
         full = torch.cat(parts, dim=1)[:, :model.vocab_size]

@@ -34,7 +34,8 @@ class SymmetricWorkspace:
     # stay below this; beyond it the two-shot kernel moves 2 (world - 1) / world of that
     ONESHOT_PEER_BYTES = 4 << 20
 
-    def __init__(self, tp, rows: int, hidden: int, oneshot_rows: int | None = None, timeout_s: float = 10.0):
+    def __init__(self, tp, rows: int, hidden: int, oneshot_rows: int | None = None, timeout_s: float = 10.0,
+                 sample_rows: int = 0):
         self.C = load()
         # bound of every peer wait inside the kernels; on expiry they record an error word
         # (``error()``) and return instead of waiting for ever
@@ -58,7 +59,13 @@ class SymmetricWorkspace:
         self.res_off = row_bytes + 3 * small
         self.out_off = 2 * row_bytes + 3 * small
         self.rs_off = 3 * row_bytes + 3 * small
-        self.flag_off = self.rs_off + rs_bytes
+        # sampler exchange (vocab-parallel sampling): SX floats, SF flag words
+        self.sample_cap = int(sample_rows)
+        sx = int(self.C.sample_x_floats(tp.size, self.sample_cap)) * 4 if self.sample_cap else 0
+        sf = int(self.C.sample_f_words(tp.size, self.sample_cap)) * 4 if self.sample_cap else 0
+        self.sx_off = self.rs_off + rs_bytes
+        self.sf_off = self.sx_off + ((sx + 255) // 256) * 256
+        self.flag_off = self.sf_off + ((sf + 255) // 256) * 256
         self.nbytes = self.flag_off + int(self.C.COMM_FLAG_BYTES)
         torch.cuda.set_device(tp.device)
         self.base, handle = self.C.symm_alloc(self.nbytes)
@@ -161,6 +168,24 @@ class SymmetricWorkspace:
         if ops is not None and hasattr(ops, "launches"):
             ops.launches += 1
         return self.OUT[:T], self.RES[:T]
+
+    # ------------------------------------------------------- vocab-parallel sampling
+    def sample_rows(self, logits, temps, top_p, step, col_offset: int, ops=None):
+        """Sample every row over the whole vocabulary from this rank's shard of the logits: the
+        kernel combines the shards with the other ranks through the symmetric buffer (per-row
+        maxima, top-p mass histograms and (score, token) pairs, by NVLink peer stores).  Every
+        rank returns the same tokens."""
+        rows = logits.shape[0]
+        if rows > self.sample_cap:
+            raise ValueError(f"{rows} rows exceed the sampler exchange capacity ({self.sample_cap})")
+        tok = torch.empty(rows, dtype=torch.int32, device=logits.device)
+        xb = [b + self.sx_off for b in self.bases]
+        fb = [b + self.sf_off for b in self.bases]
+        self.C.sample_rows(logits, int(col_offset), temps, top_p, step, tok, None, xb, fb, self.tp.rank,
+                           self.sample_cap, self.timeout_ns)
+        if ops is not None and hasattr(ops, "launches"):
+            ops.launches += 1
+        return tok
 
     def error(self, reset: bool = False) -> int:
         return int(self.C.comm_error(reset))

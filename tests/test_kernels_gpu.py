@@ -206,6 +206,35 @@ def test_sample_greedy_and_temperature(ops):
     assert torch.allclose(freq, torch.tensor([0.1, 0.2, 0.3, 0.4]), atol=0.02), freq
 
 
+def test_sample_top_p_on_gpu(ops):
+    """Nucleus sampling in one kernel: only the nucleus is drawn, in its renormalised proportions."""
+    V, rows = 151936, 4096
+    base = torch.full((V,), -30.0, device=DEV)
+    probs = torch.tensor([0.4, 0.3, 0.2, 0.1], device=DEV)
+    base[[11, 5000, 70000, 151935]] = torch.log(probs)
+    logits = base.repeat(rows, 1)
+    temps = torch.ones(rows, device=DEV)
+    counts = {0.6: torch.zeros(4), 0.95: torch.zeros(4), 1.0: torch.zeros(4)}
+    cols = torch.tensor([11, 5000, 70000, 151935], device=DEV)
+    for p in counts:
+        for s in range(3):
+            tok = ops.sample(logits, temps, torch.full((rows,), p, device=DEV),
+                             step=torch.tensor([5, s], dtype=torch.int64, device=DEV), use_top_p=True)
+            hit = (tok.long()[:, None] == cols[None]).float()
+            assert bool((hit.sum(1) == 1).all()), "a token outside the four live columns was drawn"
+            counts[p] += hit.sum(0).cpu()
+    f = {p: c / c.sum() for p, c in counts.items()}
+    assert torch.allclose(f[0.6], torch.tensor([4 / 7, 3 / 7, 0, 0]), atol=0.02), f[0.6]
+    assert torch.allclose(f[0.95], torch.tensor([0.4, 0.3, 0.2, 0.1]), atol=0.02), f[0.95]
+    assert torch.allclose(f[1.0], torch.tensor([0.4, 0.3, 0.2, 0.1]), atol=0.02), f[1.0]
+    # greedy rows in the same launch take the argmax; a row at T -> 0+ with p < 1 too
+    t2 = torch.tensor([0.0, 1e-4, 1.0], device=DEV)
+    tok = ops.sample(logits[:3], t2, torch.tensor([0.5, 0.5, 1.0], device=DEV),
+                     step=torch.tensor([1, 2], dtype=torch.int64, device=DEV), use_top_p=True)
+    assert tok[0].item() == 11 and tok[1].item() == 11
+    assert ops.C.sample_error(True) == 0
+
+
 @pytest.mark.parametrize("m,n,k", [
     (1, 1024, 1024), (5, 6144, 4096), (64, 4096, 4096), (130, 24576, 1024), (256, 512, 3072),
     (300, 1024, 1024), (1000, 3072, 1024), (4096, 4096, 4096), (77, 151936, 1024), (2, 768, 4096),

@@ -216,6 +216,51 @@ def _rs_worker(rank, world, port, out_path):
     dist.destroy_process_group()
 
 
+def _sample_worker(rank, world, port, out_path):
+    """Vocab-parallel sampling in one kernel per step equals sampling the full logits on one GPU."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from nanovllm_self_b200.ops.cuda_ops import CudaOps
+    from nanovllm_self_b200.parallel.state import init_tensor_parallel
+    from nanovllm_self_b200.parallel.symm import SymmetricWorkspace
+    tp = init_tensor_parallel(world, "cuda")
+    dev = tp.device
+    ops = CudaOps()
+    symm = SymmetricWorkspace(tp, rows=64, hidden=256, timeout_s=5.0, sample_rows=64)
+    V, rows = 151936, 48
+    per = (V + world - 1) // world
+    g = torch.Generator().manual_seed(4)
+    logits = (torch.randn(rows, V, generator=g) * 3).to(dev)
+    temps = torch.tensor([0.0, 1.0, 0.7, 1.3] * (rows // 4), device=dev)
+    top_p = torch.tensor([1.0, 0.9, 0.5, 1.0] * (rows // 4), device=dev)
+    res = {}
+    for s in range(3):
+        step = torch.tensor([3, s], dtype=torch.int64, device=dev)
+        shard = logits[:, rank * per:min(V, (rank + 1) * per)].contiguous()
+        tok_tp = symm.sample_rows(shard, temps, top_p, step, rank * per, ops)
+        tok_one = torch.empty(rows, dtype=torch.int32, device=dev)
+        ops.C.sample_rows(logits, 0, temps, top_p, step, tok_one, None)
+        torch.cuda.synchronize()
+        res[s] = (tok_tp.cpu(), tok_one.cpu())
+    err = ops.C.sample_error(False)
+    dist.barrier()
+    if rank == 0:
+        torch.save({"res": res, "err": err}, out_path)
+    symm.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_vocab_parallel_sampler_matches_one_gpu(tmp_path):
+    out = tmp_path / "sample.pt"
+    mp.spawn(_sample_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    res = torch.load(out)
+    assert res["err"] == 0
+    for s, (a, b) in res["res"].items():
+        assert torch.equal(a, b), f"step {s}: {(a != b).sum().item()} rows differ"
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_gemm_reduce_scatter_norm_allgather_matches_fp32(tmp_path):
     out = tmp_path / "rs.pt"
