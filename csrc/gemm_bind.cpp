@@ -157,7 +157,7 @@ std::vector<int64_t> linear_skinny(const at::Tensor& x, const at::Tensor& w, at:
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
                   out.scalar_type() == at::kBFloat16, "bf16 required");
-  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "unit inner stride required");
+  TORCH_CHECK(x.stride(1) == 1 && (blocked || w.stride(1) == 1) && out.stride(1) == 1, "unit inner stride required");
   const int m = (int)x.size(0), k = (int)x.size(1);
   // blocked: w is [n / 128, k / 64, 128, 64]; otherwise [n, k]
   const int n = blocked ? (int)(w.size(0) * 128) : (int)w.size(0);

@@ -68,55 +68,100 @@ __device__ __forceinline__ void load_head(const QkvPostArgs& a, int t, int head,
   }
 }
 
+constexpr int QKV_HPW = 8;  // heads per warp: their loads are all issued before any is used
+
+// Normalise (nw) and rotate (at pos) the 4 elements x of one head held by this lane.
+__device__ __forceinline__ void norm_rope(const QkvPostArgs& a, const __nv_bfloat16* nw, bool rope, const float* cs,
+                                          int lane, float* x) {
+  if (nw) {
+    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / (float)HD + a.eps);
+    float w[4];
+    bf16x4_to_f32(*reinterpret_cast<const uint2*>(nw + lane * 4), w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = x[i] * inv * w[i];
+  }
+  if (rope) {
+    const int f = (lane * 4) & 63;
+    float p[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[i] = __shfl_xor_sync(FULL_MASK, x[i], 16);
+    const bool lo = lane < 16;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float c = cs[f + i], sn = cs[64 + f + i];
+      x[i] = lo ? (x[i] * c - p[i] * sn) : (x[i] * c + p[i] * sn);
+    }
+  }
+}
+
+// One warp per (token, group of QKV_HPW heads): every head's 256-byte row is requested before
+// the first one is processed, so each warp keeps QKV_HPW loads in flight (one load per warp
+// left the kernel latency-bound at a third of the copy bandwidth).
 __global__ void __launch_bounds__(128) qkv_post_kernel(QkvPostArgs a) {
   pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
   const int lane = threadIdx.x & 31;
   const int heads = a.nq + 2 * a.nkv;
+  const int groups = (heads + QKV_HPW - 1) / QKV_HPW;
   const int64_t gw = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (gw >= (int64_t)a.T * heads) return;
-  const int t = (int)(gw / heads);
-  const int j = (int)(gw - (int64_t)t * heads);
-  float x[4];
-  if (j < a.nq) {
-    load_head(a, t, j, a.q_norm, true, lane, x);
-    *reinterpret_cast<uint2*>(a.q_out + (int64_t)t * a.nq * HD + j * HD + lane * 4) = f32_to_bf16x4(x);
-    return;
-  }
-  const bool is_k = j < a.nq + a.nkv;
-  const int h = is_k ? j - a.nq : j - a.nq - a.nkv;
-  const __nv_bfloat16* nw = is_k ? a.k_norm : nullptr;
-  load_head(a, t, j, nw, is_k, lane, x);
-  const int slot = a.slots[t];
-  if (slot < 0) return;
-  const int blk = slot / a.block_size, off = slot - blk * a.block_size;
-  const int64_t dst = (((int64_t)blk * a.nkv + h) * a.block_size + off) * HD + lane * 4;
-  if (!a.kv_fp8) {
-    __nv_bfloat16* cache = static_cast<__nv_bfloat16*>(is_k ? a.k_cache : a.v_cache);
-    *reinterpret_cast<uint2*>(cache + dst) = f32_to_bf16x4(x);
-    return;
-  }
-  float* scales = is_k ? a.k_scale : a.v_scale;
-  float scale;
-  const int first_t = t - off;
-  if (off == 0 || (first_t >= 0 && a.slots[first_t] == slot - off)) {
-    float y[4];
-    if (off == 0) {
-      y[0] = x[0]; y[1] = x[1]; y[2] = x[2]; y[3] = x[3];
-    } else {
-      load_head(a, first_t, j, nw, is_k, lane, y);
+  if (gw >= (int64_t)a.T * groups) return;
+  const int t = (int)(gw / groups);
+  const int j0 = (int)(gw - (int64_t)t * groups) * QKV_HPW;
+  const __nv_bfloat16* row = a.qkv + (int64_t)t * a.qkv_stride + lane * 4;
+  uint2 raw[QKV_HPW];
+#pragma unroll
+  for (int i = 0; i < QKV_HPW; ++i)
+    if (j0 + i < heads) raw[i] = *reinterpret_cast<const uint2*>(row + (j0 + i) * HD);
+  const bool any_rope = j0 < a.nq + a.nkv;
+  const float* cs = any_rope ? a.cos_sin + (int64_t)a.positions[t] * HD : nullptr;
+  const int slot = j0 + QKV_HPW > a.nq ? a.slots[t] : -1;
+#pragma unroll
+  for (int i = 0; i < QKV_HPW; ++i) {
+    const int j = j0 + i;
+    if (j >= heads) break;
+    float x[4];
+    bf16x4_to_f32(raw[i], x);
+    if (j < a.nq) {
+      norm_rope(a, a.q_norm, true, cs, lane, x);
+      *reinterpret_cast<uint2*>(a.q_out + (int64_t)t * a.nq * HD + j * HD + lane * 4) = f32_to_bf16x4(x);
+      continue;
     }
-    float m = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
-    m = warp_max(m);
-    scale = fmaxf(m * (4.0f / 448.0f), 1e-8f);
-    if (off == 0 && lane == 0) scales[(int64_t)blk * a.nkv + h] = scale;
-  } else {
-    scale = scales[(int64_t)blk * a.nkv + h];
+    const bool is_k = j < a.nq + a.nkv;
+    const int h = is_k ? j - a.nq : j - a.nq - a.nkv;
+    const __nv_bfloat16* nw = is_k ? a.k_norm : nullptr;
+    norm_rope(a, nw, is_k, cs, lane, x);
+    if (slot < 0) continue;
+    const int blk = slot / a.block_size, off = slot - blk * a.block_size;
+    const int64_t dst = (((int64_t)blk * a.nkv + h) * a.block_size + off) * HD + lane * 4;
+    if (!a.kv_fp8) {
+      __nv_bfloat16* cache = static_cast<__nv_bfloat16*>(is_k ? a.k_cache : a.v_cache);
+      *reinterpret_cast<uint2*>(cache + dst) = f32_to_bf16x4(x);
+      continue;
+    }
+    float* scales = is_k ? a.k_scale : a.v_scale;
+    float scale;
+    const int first_t = t - off;
+    if (off == 0 || (first_t >= 0 && a.slots[first_t] == slot - off)) {
+      float y[4];
+      if (off == 0) {
+        y[0] = x[0]; y[1] = x[1]; y[2] = x[2]; y[3] = x[3];
+      } else {
+        load_head(a, first_t, j, nw, is_k, lane, y);
+      }
+      float m = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
+      m = warp_max(m);
+      scale = fmaxf(m * (4.0f / 448.0f), 1e-8f);
+      if (off == 0 && lane == 0) scales[(int64_t)blk * a.nkv + h] = scale;
+    } else {
+      scale = scales[(int64_t)blk * a.nkv + h];
+    }
+    const float inv = 1.0f / scale;
+    float q[4] = {x[0] * inv, x[1] * inv, x[2] * inv, x[3] * inv};
+    uint8_t* cache = static_cast<uint8_t*>(is_k ? a.k_cache : a.v_cache);
+    *reinterpret_cast<uint32_t*>(cache + dst) = f32x4_to_e4m3(q);
   }
-  const float inv = 1.0f / scale;
-  float q[4] = {x[0] * inv, x[1] * inv, x[2] * inv, x[3] * inv};
-  uint8_t* cache = static_cast<uint8_t*>(is_k ? a.k_cache : a.v_cache);
-  *reinterpret_cast<uint32_t*>(cache + dst) = f32x4_to_e4m3(q);
 }
 
 cudaError_t launch_qkv_post(const void* qkv, int64_t qkv_stride, void* q_out, const void* q_norm, const void* k_norm,
@@ -144,7 +189,7 @@ cudaError_t launch_qkv_post(const void* qkv, int64_t qkv_stride, void* q_out, co
   a.nkv = nkv;
   a.block_size = block_size;
   a.kv_fp8 = kv_fp8;
-  int64_t warps = (int64_t)T * (nq + 2 * nkv);
+  int64_t warps = (int64_t)T * ((nq + 2 * nkv + QKV_HPW - 1) / QKV_HPW);
   int64_t blocks = (warps + 3) / 4;
   launch_pdl(qkv_post_kernel, dim3((unsigned)blocks), dim3(128), 0, stream, a);
   NVB_LAUNCH_CHECK();

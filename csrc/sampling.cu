@@ -22,7 +22,10 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 __device__ __forceinline__ float gumbel(uint64_t seed, uint64_t step, int row, int64_t col) {
   uint64_t h = mix64(seed + 0x9E3779B97F4A7C15ull * (step + 1));
   h = mix64(h ^ ((uint64_t)row << 40) ^ (uint64_t)col);
-  float u = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
+  // 23 random bits: (k + 0.5) / 2^23 is exact in fp32 and lies in [2^-24, 1 - 2^-24], so u < 1 and
+  // the noise is finite (24 bits would round the top value up to u = 1 and give g = +inf,
+  // letting a random column win about once per 2^24 columns)
+  const float u = ((float)(h >> 41) + 0.5f) * (1.0f / 8388608.0f);
   return -logf(-logf(u));
 }
 

@@ -275,7 +275,8 @@ def main(argv=None):
     p.add_argument("--m", type=int, default=1)
     p.add_argument("--n", type=int, default=6144)
     p.add_argument("--k", type=int, default=4096)
-    p.add_argument("--impl", default="tuned")
+    p.add_argument("--impl", default="tuned", help="comma-separated: tuned, cublas, skinny:R, skinnyb:R, dec:R")
+    p.add_argument("--ms", default=None, help="comma-separated m values (gemm_one), instead of --m")
     p.add_argument("--mode", choices=("time", "profile"), default="time")
     p.add_argument("--iters", type=int, default=20)
     a = p.parse_args(argv)
@@ -283,7 +284,9 @@ def main(argv=None):
         gemm_sweep(iters=a.iters)
         return
     if a.case == "gemm_one":
-        gemm_one(a.m, a.n, a.k, a.impl, a.mode, a.iters)
+        for impl in a.impl.split(","):
+            for m in (a.ms.split(",") if a.ms else [a.m]):
+                gemm_one(int(m), a.n, a.k, impl, a.mode, a.iters)
         return
     names = CASES if a.case == "all" else (a.case,)
     for n in names:

@@ -7,18 +7,50 @@
 * ``kv_dtype``     - the same workload with bf16 and fp8 KV caches (``benchmark_kv_cache_dtype.py``);
 * ``prefix``       - the multi-turn agent prefix workload (config 4): prefix-hit rate and tok/s;
 * ``pd``           - P/D pool with Poisson arrivals (config 5): p50/p99 TTFT and TPOT.
-Every driver prints one JSON line.
+Every driver prints one JSON line (rank 0 under ``torch.distributed.run`` for ``--tp`` > 1), with the
+SM clocks and throttle reasons sampled during its timed part.  Warm-up runs use different prompt
+token ids than the timed runs (same lengths), so no timed prefill is served from the prefix cache;
+the line reports the timed prefix-cache hits.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import os
 import time
 
 import torch
 
 from .. import LLM, SamplingParams
+from ..utils.clocks import ClockSampler
 from . import datasets
+
+WARMUP_SEED = 10_000  # added to a workload's seed for its warm-up copy (same lengths, other token ids)
+
+
+def _fresh(rows, vocab, seed):
+    """Same lengths as `rows`, new token ids."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    return [dict(r, prompt_ids=rng.integers(0, vocab, len(r["prompt_ids"])).tolist()) for r in rows]
+
+
+class _Timed:
+    """Clock samples and prefix-cache hits over one timed region."""
+
+    def __init__(self, llm):
+        self.llm = llm
+
+    def __enter__(self):
+        dev = self.llm.model_runner.device
+        self.clk = ClockSampler(dev.index or 0 if dev.type == "cuda" else 0)
+        self.hits0 = self.llm.block_manager.num_prefix_hit_blocks
+        self.clk.start()
+        return self
+
+    def __exit__(self, *a):
+        self.clocks = self.clk.stop()
+        self.prefix_hits = self.llm.block_manager.num_prefix_hit_blocks - self.hits0
 
 
 def _llm(args, **kw):
@@ -36,26 +68,34 @@ def runtime(args) -> dict:
     llm = _llm(args)
     vocab = llm.model_runner.arch.vocab_size
     rows = datasets.uniform_serving(args.batch, vocab, (args.prompt_len, args.prompt_len), (args.gen, args.gen))
-    llm.generate([r["prompt_ids"] for r in rows], _sp(rows))
-    m = llm.generate([r["prompt_ids"] for r in rows], _sp(rows), return_metrics=True)["metrics"]
+    warm = _fresh(rows, vocab, WARMUP_SEED)
+    llm.generate([r["prompt_ids"] for r in warm], _sp(warm))
+    with _Timed(llm) as t:
+        m = llm.generate([r["prompt_ids"] for r in rows], _sp(rows), return_metrics=True)["metrics"]
     prefill_s = m["ttft_ms_p50"] / 1e3
-    return {"bench": "runtime", "batch": args.batch, "prompt_len": args.prompt_len, "gen": args.gen,
+    return {"bench": "runtime", "model": args.model, "tp": args.tp, "batch": args.batch,
+            "prompt_len": args.prompt_len, "gen": args.gen,
             "ttft_ms": m["ttft_ms_p50"], "itl_ms": m["tpot_ms_p50"],
             "prefill_tok_s": args.batch * args.prompt_len / prefill_s if prefill_s > 0 else 0.0,
             "decode_tok_s": args.batch / (m["tpot_ms_p50"] / 1e3) if m["tpot_ms_p50"] > 0 else 0.0,
-            "e2e_tok_s": m["e2e_throughput_tok_s"], "device_tok_s": m["throughput_tok_s"]}
+            "e2e_tok_s": m["e2e_throughput_tok_s"], "device_tok_s": m["throughput_tok_s"],
+            "prefix_hit_blocks_timed": t.prefix_hits, "clocks": t.clocks}
 
 
 def decode_sweep(args) -> dict:
     llm = _llm(args)
     vocab = llm.model_runner.arch.vocab_size
-    out = {"bench": "decode_sweep", "context": args.context, "kv": args.kv, "points": []}
+    out = {"bench": "decode_sweep", "model": args.model, "tp": args.tp, "context": args.context, "kv": args.kv,
+           "gen": args.gen, "points": []}
     for bs in [int(b) for b in args.batches.split(",")]:
         rows = datasets.uniform_serving(bs, vocab, (args.context, args.context), (args.gen, args.gen), seed=bs)
-        llm.generate([r["prompt_ids"] for r in rows], _sp(rows))
-        m = llm.generate([r["prompt_ids"] for r in rows], _sp(rows), return_metrics=True)["metrics"]
+        warm = _fresh(rows, vocab, WARMUP_SEED + bs)
+        llm.generate([r["prompt_ids"] for r in warm], _sp(warm))
+        with _Timed(llm) as t:
+            m = llm.generate([r["prompt_ids"] for r in rows], _sp(rows), return_metrics=True)["metrics"]
         out["points"].append({"batch": bs, "tpot_ms": m["tpot_ms_p50"],
-                              "decode_tok_s": bs / (m["tpot_ms_p50"] / 1e3) if m["tpot_ms_p50"] > 0 else 0.0})
+                              "decode_tok_s": bs / (m["tpot_ms_p50"] / 1e3) if m["tpot_ms_p50"] > 0 else 0.0,
+                              "prefix_hit_blocks_timed": t.prefix_hits, "clocks": t.clocks})
     return out
 
 
@@ -66,10 +106,13 @@ def kv_dtype(args) -> dict:
         llm = _llm(args)
         vocab = llm.model_runner.arch.vocab_size
         rows = datasets.uniform_serving(args.batch, vocab, (100, 1024), (100, 1024))
-        llm.generate([r["prompt_ids"] for r in rows], _sp(rows))
-        m = llm.generate([r["prompt_ids"] for r in rows], _sp(rows), return_metrics=True)["metrics"]
+        warm = _fresh(rows, vocab, WARMUP_SEED)
+        llm.generate([r["prompt_ids"] for r in warm], _sp(warm))
+        with _Timed(llm) as t:
+            m = llm.generate([r["prompt_ids"] for r in rows], _sp(rows), return_metrics=True)["metrics"]
         res["runs"].append({"kv": kv, "device_tok_s": m["throughput_tok_s"], "e2e_tok_s": m["e2e_throughput_tok_s"],
-                            "tpot_ms": m["tpot_ms_p50"], "kv_blocks": llm.model_runner.num_blocks})
+                            "tpot_ms": m["tpot_ms_p50"], "kv_blocks": llm.model_runner.num_blocks,
+                            "prefix_hit_blocks_timed": t.prefix_hits, "clocks": t.clocks})
         llm.shutdown()
         del llm
         torch.cuda.empty_cache()
@@ -83,25 +126,33 @@ def prefix(args) -> dict:
     by_turn = {}
     for r in rows:
         by_turn.setdefault(r["step_id"], []).append(r)
+    # warm-up: one short unrelated batch (compiles graphs, tunes GEMMs; shares no prefix)
+    warm = datasets.uniform_serving(4, vocab, (256, 256), (8, 8), seed=WARMUP_SEED)
+    llm.generate([r["prompt_ids"] for r in warm], _sp(warm))
+    snap0 = llm.block_manager.get_block_usage_snapshot()
     t0 = time.perf_counter()
-    gen = 0
-    for t in sorted(by_turn):
-        batch = by_turn[t]
-        out = llm.generate([r["prompt_ids"] for r in batch], _sp(batch), return_metrics=True)
-        gen += out["metrics"]["generated_tokens"]
+    gen, dev_s = 0, 0.0
+    with _Timed(llm) as tm:
+        for t in sorted(by_turn):
+            batch = by_turn[t]
+            out = llm.generate([r["prompt_ids"] for r in batch], _sp(batch), return_metrics=True)
+            gen += out["metrics"]["generated_tokens"]
+            dev_s += out["metrics"]["total_time_s"]
     wall = time.perf_counter() - t0
     snap = llm.block_manager.get_block_usage_snapshot()
-    return {"bench": "prefix", "sessions": args.sessions, "turns": len(by_turn), "wall_s": wall,
-            "output_tok_s": gen / wall, "prefix_hit_blocks": snap["prefix_hit_blocks"],
-            "prefix_query_blocks": snap["prefix_query_blocks"],
-            "prefix_hit_rate": snap["prefix_hit_blocks"] / max(1, snap["prefix_query_blocks"])}
+    hits = snap["prefix_hit_blocks"] - snap0["prefix_hit_blocks"]
+    queries = snap["prefix_query_blocks"] - snap0["prefix_query_blocks"]
+    return {"bench": "prefix", "model": args.model, "tp": args.tp, "sessions": args.sessions, "turns": len(by_turn),
+            "wall_s": wall, "output_tok_s": gen / wall, "device_output_tok_s": gen / dev_s if dev_s else 0.0,
+            "prefix_hit_blocks": hits, "prefix_query_blocks": queries, "prefix_hit_rate": hits / max(1, queries),
+            "clocks": tm.clocks}
 
 
 def pd(args) -> dict:
     from ..pd.multiprocess.pool import PDPool
     rows = datasets.pd_lognormal(args.num_requests)
     pool = PDPool(args.work_root, args.num_prefill, args.num_decode, args.pd_backend, args.model,
-                  policy="affinity_load_aware",
+                  policy="affinity_load_aware", tp=args.tp,
                   worker_args=["--max-model-len", str(args.max_model_len), "--block-size", str(args.block_size),
                                "--kv-cache-quant-mode", args.kv])
     pool.start()
@@ -109,7 +160,8 @@ def pd(args) -> dict:
         s = pool.run(rows, concurrency=None, rate=args.rate)
     finally:
         pool.shutdown()
-    s["bench"] = "pd"
+    s.update(bench="pd", model=args.model, tp_per_worker=args.tp, kv=args.kv, rate=args.rate,
+             num_prefill=args.num_prefill, num_decode=args.num_decode, backend=args.pd_backend)
     return s
 
 
@@ -136,7 +188,13 @@ def main(argv=None):
     ap.add_argument("--pd-backend", default="ipc_push")
     ap.add_argument("--work-root", default="/tmp/nvb_pd")
     args = ap.parse_args(argv)
-    print(json.dumps(globals()[args.name](args)))
+    if args.name == "pd":
+        # the pool launches its own worker processes (TP groups via torchrun): run it from one process
+        print(json.dumps(pd(args)), flush=True)
+        return
+    res = globals()[args.name](args)
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps(res), flush=True)
 
 
 if __name__ == "__main__":

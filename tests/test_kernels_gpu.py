@@ -206,6 +206,19 @@ def test_sample_greedy_and_temperature(ops):
     assert torch.allclose(freq, torch.tensor([0.1, 0.2, 0.3, 0.4]), atol=0.02), freq
 
 
+def test_temperature_sampling_never_leaves_the_live_columns(ops):
+    """Full-vocabulary rows at T = 1 with 4 live columns: the noise stays finite for every column
+    (a noise value of +inf would let a dead column win about once per 2^24 columns)."""
+    V, rows = 151936, 4096
+    base = torch.full((V,), -30.0, device=DEV)
+    cols = torch.tensor([11, 5000, 70000, 151935], device=DEV)
+    base[cols] = torch.log(torch.tensor([0.4, 0.3, 0.2, 0.1], device=DEV))
+    logits = base.repeat(rows, 1)
+    for s in range(3):
+        tok = ops.sample(logits, torch.ones(rows, device=DEV), step=torch.tensor([9, s], dtype=torch.int64, device=DEV))
+        assert bool((tok.long()[:, None] == cols[None]).any(1).all())
+
+
 def test_sample_top_p_on_gpu(ops):
     """Nucleus sampling in one kernel: only the nucleus is drawn, in its renormalised proportions."""
     V, rows = 151936, 4096
