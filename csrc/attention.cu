@@ -1049,7 +1049,7 @@ namespace pf {
 constexpr int TQ_ROWS = 128;  // MMA M: (query token, query head) rows per CTA
 constexpr int TK = 128;       // keys per tile (MMA N of S, K of P V)
 constexpr int NSTAGE = 2;     // K/V ring depth
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;  // 10 warps: TMA, MMA, 8 softmax (two per TMEM lane quarter)
 constexpr int HALF = TQ_ROWS * 64 * 2;  // bytes of one 64-dim half of a 128-row tile (16 KB)
 constexpr int TILE = 2 * HALF;          // 32 KB: a 128 x 128 bf16 tile
 constexpr float RESCALE_LOG2 = 8.f;
@@ -1202,7 +1202,7 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
       bar_init(v_full(s), 1);
       bar_init(v_empty(s), 1);
       bar_init(s_full(s), 1);
-      bar_init(p_ready(s), 128);
+      bar_init(p_ready(s), 256);
       bar_init(s_free(s), 1);
     }
     bar_init(o_done, 1);
@@ -1306,82 +1306,102 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
     commit(o_final);
   } else if (warp >= 2) {
     // ------------------------------------------------------------------ softmax / output
+    // Two warps per TMEM lane quarter: warp w serves rows 32 (w & 3) .. +31 and the key (and
+    // head-dim) half `half` of them; the pair exchanges its row maxima through shared memory
+    // (named barrier 1 + quarter, 64 threads) so both halves scale by the same maximum.
     const int q4 = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = q4 * 32 + lane;
     const int t = t0 + r / G, g = r % G;
     const int pos = off + t;
     const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
+    const int c0 = half * 64;  // this thread's first key column of a tile / first head dim
+    __shared__ float xmax[2][2][TQ_ROWS];  // [tile parity][half][row]
+    __shared__ int xok[2][2][TQ_ROWS];
+    __shared__ float xsum[2][TQ_ROWS];
+    // Both warps of a pair pass the same sequence of pair barriers on every path (errors
+    // included): the decision to stop is taken from the exchanged flags, identically by both.
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + q4) : "memory"); };
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int s = j & 1;
-      if (!wait(s_full(s), (j >> 1) & 1, 46)) {
-        ok = false;
-        break;
-      }
+      if (ok) ok = wait(s_full(s), (j >> 1) & 1, 46);
       fence_after();
-      uint32_t raw[TK];
-#pragma unroll
-      for (int c = 0; c < TK; c += 32) tmem_ld32(lane_base + s_col(s) + c, raw + c);
-      tmem_ld_wait();
-      const int key0 = j * TK;
-      const int lim = min(pos + 1, k_len) - key0;  // keys [0, lim) of this tile are visible
-      float x[TK];
+      uint32_t raw[64];
+      if (ok) {
+        tmem_ld32(lane_base + s_col(s) + c0, raw);
+        tmem_ld32(lane_base + s_col(s) + c0 + 32, raw + 32);
+        tmem_ld_wait();
+      }
+      const int lim = ok ? min(pos + 1, k_len) - j * TK - c0 : 0;  // keys [0, lim) of this half are visible
+      float x[64];
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < TK; ++c) {
+      for (int c = 0; c < 64; ++c) {
         x[c] = c < lim ? __uint_as_float(raw[c]) * a.scale_log2 : -INFINITY;
         mx = fmaxf(mx, x[c]);
       }
+      xmax[s][half][r] = mx;
+      xok[s][half][r] = ok ? 1 : 0;
+      pair_sync();
+      mx = fmaxf(xmax[s][0][r], xmax[s][1][r]);
+      ok = xok[s][0][r] && xok[s][1][r];
+      if (!ok) break;  // identical in both warps of the pair
       if (mx > m_used + RESCALE_LOG2 || m_used == -INFINITY) {
-        // raise the running maximum; O (if any) must be rescaled first
+        // raise the running maximum; O (if any) must be rescaled first (each half its 64 dims)
         const float m_new = mx;
         if (j > 0 && m_used != -INFINITY) {
           if (!wait(o_done, (j - 1) & 1, 47)) {
-            ok = false;
-            break;
-          }
-          fence_after();
-          const float f = exp2f(m_used - m_new);
+            ok = false;  // reported to the partner at the next exchange
+          } else {
+            fence_after();
+            const float f = exp2f(m_used - m_new);
 #pragma unroll 1
-          for (int c = 0; c < 128; c += 32) {
-            uint32_t o[32];
-            tmem_ld32(lane_base + O_COL + c, o);
-            tmem_ld_wait();
+            for (int c = 0; c < 64; c += 32) {
+              uint32_t o[32];
+              tmem_ld32(lane_base + O_COL + c0 + c, o);
+              tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-            tmem_st32(lane_base + O_COL + c, o);
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+              tmem_st32(lane_base + O_COL + c0 + c, o);
+            }
+            tmem_st_wait();
+            l *= f;
           }
-          tmem_st_wait();
-          l *= f;
         }
         if (m_new != -INFINITY) m_used = m_new;
       }
       const float base = m_used == -INFINITY ? 0.f : m_used;
-      uint32_t p[TK / 2];
+      uint32_t p[32];
       float rs = 0.f;
 #pragma unroll
-      for (int c = 0; c < TK; c += 2) {
+      for (int c = 0; c < 64; c += 2) {
         const float p0 = exp2f(x[c] - base), p1 = exp2f(x[c + 1] - base);
         rs += p0 + p1;
         p[c / 2] = pack_bf16(p0, p1);
       }
       l += rs;
-      tmem_st32(lane_base + s_col(s), p);
-      tmem_st32(lane_base + s_col(s) + 32, p + 32);
+      tmem_st32(lane_base + s_col(s) + half * 32, p);  // keys c0.. -> packed columns 32 half ..
       tmem_st_wait();
       fence_before();
       arrive(p_ready(s));
     }
+    // row sum over both halves (both warps of the pair reach this barrier on every path)
+    xsum[half][r] = l;
+    xok[0][half][r] = ok ? 1 : 0;
+    pair_sync();
+    const float lt = xsum[0][r] + xsum[1][r];
+    ok = xok[0][0][r] && xok[0][1][r];
     if (ok && wait(o_final, 0, 48)) {
       fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = a.out + ((int64_t)(qs + t) * a.nq + h * G + g) * 128;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      __nv_bfloat16* dst = a.out + ((int64_t)(qs + t) * a.nq + h * G + g) * 128 + c0;
       const bool valid = t < q_len;
 #pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
+      for (int c = 0; c < 64; c += 32) {
         uint32_t o[32];
-        tmem_ld32(lane_base + O_COL + c, o);
+        tmem_ld32(lane_base + O_COL + c0 + c, o);
         tmem_ld_wait();
         if (valid) {
           float f[32];

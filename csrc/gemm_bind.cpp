@@ -153,7 +153,7 @@ std::vector<int64_t> linear_rs(const at::Tensor& x, const at::Tensor& w, std::ve
 // Skinny kernel (weights on the MMA's M side) with the rank-th configuration by its traffic
 // model; returns (tokens per tile, weight rows per CTA, splits, stages), empty if none.
 std::vector<int64_t> linear_skinny(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, int64_t rank,
-                                   int64_t act, int64_t blocked) {
+                                   int64_t act, int64_t blocked, const c10::optional<at::Tensor>& trace) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
                   out.scalar_type() == at::kBFloat16, "bf16 required");
@@ -169,7 +169,8 @@ std::vector<int64_t> linear_skinny(const at::Tensor& x, const at::Tensor& w, at:
   at::cuda::CUDAGuard g(x.device());
   cudaError_t e = nvb::gemm_skinny_run(x.data_ptr(), x.stride(0), w.data_ptr(), blocked ? 64 : w.stride(0),
                                        out.data_ptr(), out.stride(0), m, n, k, pl, (int)act, (int)blocked,
-                                       at::cuda::getCurrentCUDAStream().stream());
+                                       at::cuda::getCurrentCUDAStream().stream(),
+                                       trace.has_value() ? reinterpret_cast<uint64_t*>(trace->data_ptr()) : nullptr);
   TORCH_CHECK(e == cudaSuccess, "gemm_bf16 (skinny) failed: ", cudaGetErrorString(e));
   return {pl.mt, pl.bn, pl.splits, pl.stages};
 }
@@ -193,7 +194,7 @@ void register_gemm(pybind11::module& m) {
   m.def("linear_dec_cfg", &linear_dec_cfg, "decode-sized tcgen05 GEMM with an explicit configuration");
   m.def("linear_skinny", &linear_skinny, "skinny tcgen05 GEMM (weights on M) with a ranked configuration",
         pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("rank"), pybind11::arg("act") = 0,
-        pybind11::arg("blocked") = 0);
+        pybind11::arg("blocked") = 0, pybind11::arg("trace") = c10::nullopt);
   m.def("linear_rs", &linear_rs, "tcgen05 decode GEMM whose rows are stored at their owner rank (reduce-scatter)");
   m.def("gemm_error", &error_code, pybind11::arg("reset") = false);
 }

@@ -916,6 +916,8 @@ struct DecParams {
   int bn, splits, kb_per_split, num_kb;
   int w_stages, a_stages;
   int act;               // 1: SiLU-and-mul epilogue (interleaved gate/up rows, see act_silu_store)
+  int a_rows;            // rows of each activation TMA box: m rounded up to 16 when m < 128 (the
+                         // accumulator rows past it see stale shared memory and are never stored)
   uint32_t idesc;
   __nv_bfloat16* c;
   int64_t ldc;
@@ -1016,7 +1018,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const CUtensorMap* map = is_w ? &map_w : &map_x;
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
     const int S = is_w ? SW : SA;
-    const uint32_t bytes = is_w ? (uint32_t)W_BYTES : (uint32_t)A_BYTES;
+    const uint32_t bytes = is_w ? (uint32_t)W_BYTES : (uint32_t)(MT * p.a_rows * BK * 2);
     // the weights do not depend on the previous kernel: their ring fills while it finishes
     if (!is_w) pdl_wait();
     uint32_t it = 0;
@@ -1321,7 +1323,8 @@ cudaError_t run_dec(const DecCfg& d, const void* x, int64_t ldx, const void* w, 
                     int m, int n, int k, cudaStream_t stream, int act = 0, const GemmRsEpilogue* rs = nullptr) {
   if (act && (d.bn % 32 || n % 32)) return cudaErrorInvalidValue;
   CUtensorMap mx, mw;
-  if (!make_map(&mx, x, m, k, ldx, BM) || !make_map(&mw, w, n, k, ldw, d.bn)) return cudaErrorInvalidValue;
+  const int a_rows = d.mt == 1 && m < BM ? ((m + 15) / 16) * 16 : BM;
+  if (!make_map(&mx, x, m, k, ldx, a_rows) || !make_map(&mw, w, n, k, ldw, d.bn)) return cudaErrorInvalidValue;
   DecParams p;
   p.m = m;
   p.n = n;
@@ -1332,6 +1335,7 @@ cudaError_t run_dec(const DecCfg& d, const void* x, int64_t ldx, const void* w, 
   p.num_kb = k / BK;
   p.w_stages = d.w_stages;
   p.act = act;
+  p.a_rows = a_rows;
   p.a_stages = d.a_stages;
   p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(d.bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
   p.c = static_cast<__nv_bfloat16*>(c);
@@ -1390,6 +1394,8 @@ struct SkParams {
   int splits, kb_per_split, num_kb, stages;
   int act;           // 1: SiLU-and-mul epilogue (gate/up rows interleaved in groups of 16)
   int blocked;       // 1: W stored as [n / 128][k / 64][128][64] (every TMA box one contiguous 16 KB)
+  uint64_t* trace;   // optional: per CTA 8 %globaltimer stamps (start, weights issued, first stage full,
+                     // MMAs done, export done, reduce done, end, unused)
   uint32_t idesc;
   __nv_bfloat16* c;
   int64_t ldc;
@@ -1426,7 +1432,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
 
 constexpr int SK_XLD = BM + 4;  // export row stride (floats): [token][128 features + pad]
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their rings fit
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                        SkParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1473,6 +1479,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_trigger();  // the whole grid is resident (one wave): the next kernel may launch
+  uint64_t* tr = p.trace ? p.trace + (int64_t)blockIdx.x * 8 : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = globaltimer();
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------------ producer
@@ -1488,6 +1496,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tma_load_2d(smem_u32(smem + i * STAGE + w * BM * BK * 2), &map_w, full(i), wx, wy);
       }
     }
+    if (tr) tr[1] = globaltimer();
     pdl_wait();  // the activations come from the previous kernel
     for (int i = 0; i < pre; ++i) tma_load_2d(smem_u32(smem + i * STAGE + W_BYTES), &map_x, full(i), (kb0 + i) * BK, 0);
     bool ok = true;
@@ -1516,6 +1525,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int i = 0; i < nkb; ++i) {
       const int s = i % S;
       if (!mbar_wait(full(s), (i / S) & 1, abort_flag, 21)) break;
+      if (tr && i == 0) tr[2] = globaltimer();
       tc_fence_after();
       const uint32_t st = smem_u32(smem + s * STAGE);
       const uint64_t xd = sdesc(st + W_BYTES);
@@ -1533,78 +1543,110 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp >= 2) {
     acc_ok = (warp == 2 ? mbar_wait : mbar_wait_sleep)(tfull, 0, abort_flag, 22);
     tc_fence_after();
+    if (tr && threadIdx.x == 64) tr[3] = globaltimer();
   }
   pdl_wait();  // C (or a peer's receive slot) may still be read by the previous kernel
-  float* xp = reinterpret_cast<float*>(smem);  // export [token][SK_XLD] over the idle ring
-  const uint32_t xbase = smem_u32(xp);
+  float* xp0 = reinterpret_cast<float*>(smem);  // export [sub-tile][token][SK_XLD] over the idle ring
   const int fpr = ((BM / p.splits + 7) / 8) * 8;  // features per CTA in the reduction (multiple of 8)
   const int f0 = split * fpr, f1 = min(BM, f0 + fpr);
-  for (int w = 0; w < p.mw; ++w) {
+  // every sub-tile's export at once when the ring holds them all (one pair of cluster barriers),
+  // otherwise one sub-tile at a time
+  const int per_pass = (int64_t)p.mw * p.np * SK_XLD * 4 <= (int64_t)S * STAGE ? p.mw : 1;
+  for (int w0 = 0; w0 < p.mw; w0 += per_pass) {
     if (warp >= 2 && acc_ok) {
       const int q4 = warp & 3;
-      const int r = q4 * 32 + lane;  // feature row of this thread inside sub-tile w
-      for (int c0 = 0; c0 < p.np; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem_base + ((uint32_t)(q4 * 32) << 16) + w * p.np + c0, v);
+      const int r = q4 * 32 + lane;  // feature row of this thread inside a sub-tile
+      for (int w = w0; w < w0 + per_pass; ++w) {
+        float* xp = xp0 + (w - w0) * p.np * SK_XLD;
+        for (int c0 = 0; c0 < p.np; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(tmem_base + ((uint32_t)(q4 * 32) << 16) + w * p.np + c0, v);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) xp[(c0 + e) * SK_XLD + r] = __uint_as_float(v[e]);
+          for (int e = 0; e < 16; ++e) xp[(c0 + e) * SK_XLD + r] = __uint_as_float(v[e]);
+        }
       }
     }
     if (warp >= 2) tc_fence_before();
-    cluster_sync_all();  // every CTA's export of sub-tile w is visible cluster-wide
-    const int fbase = wrow0 + w * BM;  // output feature of row 0 of this sub-tile
-    if (p.act) {
-      // outputs: 16 per 32 rows (rows 32g..32g+15 gates, +16 the ups); items = 8 outputs
-      const int g0 = f0 / 32, g1 = (f1 + 31) / 32;
-      const int per_tok = (g1 - g0) * 2;
-      for (int it = threadIdx.x; it < p.m * per_tok; it += NUM_THREADS) {
-        const int j = it / per_tok, q = it % per_tok;
-        const int g = g0 + q / 2, half = q % 2;
-        const int rg = g * 32 + half * 8;  // gate rows rg..rg+7, up rows rg+16..rg+23
-        if (rg < f0 || rg >= f1 || fbase + rg >= p.n) continue;
-        float gv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, uv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int s2 = 0; s2 < p.splits; ++s2) {
+    cluster_sync_all();  // every CTA's export of these sub-tiles is visible cluster-wide
+    if (tr && threadIdx.x == 0 && w0 == 0) tr[4] = globaltimer();
+    for (int w = w0; w < w0 + per_pass; ++w) {
+      const uint32_t xbase = smem_u32(xp0 + (w - w0) * p.np * SK_XLD);
+      const int fbase = wrow0 + w * BM;  // output feature of row 0 of this sub-tile
+      if (p.act) {
+        // outputs: 16 per 32 rows (rows 32g..32g+15 gates, +16 the ups); items = 8 outputs
+        const int g0 = f0 / 32, g1 = (f1 + 31) / 32;
+        const int per_tok = (g1 - g0) * 2;
+        for (int it = threadIdx.x; it < p.m * per_tok; it += NUM_THREADS) {
+          const int j = it / per_tok, q = it % per_tok;
+          const int g = g0 + q / 2, half = q % 2;
+          const int rg = g * 32 + half * 8;  // gate rows rg..rg+7, up rows rg+16..rg+23
+          if (rg < f0 || rg >= f1 || fbase + rg >= p.n) continue;
+          float gv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, uv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
           const uint32_t a = xbase + (uint32_t)(j * SK_XLD + rg) * 4u;
-          float4 x0 = ld_dsmem_f32x4(a, s2), x1 = ld_dsmem_f32x4(a + 16u, s2);
-          float4 y0 = ld_dsmem_f32x4(a + 64u, s2), y1 = ld_dsmem_f32x4(a + 80u, s2);
-          gv[0] += x0.x; gv[1] += x0.y; gv[2] += x0.z; gv[3] += x0.w;
-          gv[4] += x1.x; gv[5] += x1.y; gv[6] += x1.z; gv[7] += x1.w;
-          uv[0] += y0.x; uv[1] += y0.y; uv[2] += y0.z; uv[3] += y0.w;
-          uv[4] += y1.x; uv[5] += y1.y; uv[6] += y1.z; uv[7] += y1.w;
-        }
-        float o[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = silu_f(gv[e]) * uv[e];
-        const int oc = (fbase + g * 32) / 2 + half * 8;
-        *reinterpret_cast<uint4*>(sk_row(p, j) + oc) = f32_to_bf16x8(o);
-      }
-    } else {
-      const int per_tok = (f1 - f0 + 7) / 8;
-      for (int it = threadIdx.x; it < p.m * per_tok; it += NUM_THREADS) {
-        const int j = it / per_tok, f = f0 + (it % per_tok) * 8;
-        const int feat = fbase + f;
-        if (f >= f1 || feat >= p.n) continue;
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int s2 = 0; s2 < p.splits; ++s2) {
-          const uint32_t a = xbase + (uint32_t)(j * SK_XLD + f) * 4u;
-          const float4 x0 = ld_dsmem_f32x4(a, s2), x1 = ld_dsmem_f32x4(a + 16u, s2);
-          acc[0] += x0.x; acc[1] += x0.y; acc[2] += x0.z; acc[3] += x0.w;
-          acc[4] += x1.x; acc[5] += x1.y; acc[6] += x1.z; acc[7] += x1.w;
+          for (int sb = 0; sb < 8; sb += 4) {  // 4 peers' loads in flight at a time
+            float4 x0[4], x1[4], y0[4], y1[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (sb + q < p.splits) {
+                x0[q] = ld_dsmem_f32x4(a, sb + q);
+                x1[q] = ld_dsmem_f32x4(a + 16u, sb + q);
+                y0[q] = ld_dsmem_f32x4(a + 64u, sb + q);
+                y1[q] = ld_dsmem_f32x4(a + 80u, sb + q);
+              }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (sb + q < p.splits) {
+                gv[0] += x0[q].x; gv[1] += x0[q].y; gv[2] += x0[q].z; gv[3] += x0[q].w;
+                gv[4] += x1[q].x; gv[5] += x1[q].y; gv[6] += x1[q].z; gv[7] += x1[q].w;
+                uv[0] += y0[q].x; uv[1] += y0[q].y; uv[2] += y0[q].z; uv[3] += y0[q].w;
+                uv[4] += y1[q].x; uv[5] += y1[q].y; uv[6] += y1[q].z; uv[7] += y1[q].w;
+              }
+          }
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] = silu_f(gv[e]) * uv[e];
+          const int oc = (fbase + g * 32) / 2 + half * 8;
+          *reinterpret_cast<uint4*>(sk_row(p, j) + oc) = f32_to_bf16x8(o);
         }
-        __nv_bfloat16* dst = sk_row(p, j) + feat;
-        if (feat + 8 <= p.n) {
-          *reinterpret_cast<uint4*>(dst) = f32_to_bf16x8(acc);
-        } else {
-          for (int e = 0; e < 8 && feat + e < p.n; ++e) dst[e] = __float2bfloat16(acc[e]);
+      } else {
+        const int per_tok = (f1 - f0 + 7) / 8;
+        for (int it = threadIdx.x; it < p.m * per_tok; it += NUM_THREADS) {
+          const int j = it / per_tok, f = f0 + (it % per_tok) * 8;
+          const int feat = fbase + f;
+          if (f >= f1 || feat >= p.n) continue;
+          float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          const uint32_t a = xbase + (uint32_t)(j * SK_XLD + f) * 4u;
+          float4 x0[8], x1[8];
+#pragma unroll
+          for (int s2 = 0; s2 < 8; ++s2)  // every peer's loads in flight before the first is used
+            if (s2 < p.splits) {
+              x0[s2] = ld_dsmem_f32x4(a, s2);
+              x1[s2] = ld_dsmem_f32x4(a + 16u, s2);
+            }
+#pragma unroll
+          for (int s2 = 0; s2 < 8; ++s2)
+            if (s2 < p.splits) {
+              acc[0] += x0[s2].x; acc[1] += x0[s2].y; acc[2] += x0[s2].z; acc[3] += x0[s2].w;
+              acc[4] += x1[s2].x; acc[5] += x1[s2].y; acc[6] += x1[s2].z; acc[7] += x1[s2].w;
+            }
+          __nv_bfloat16* dst = sk_row(p, j) + feat;
+          if (feat + 8 <= p.n) {
+            *reinterpret_cast<uint4*>(dst) = f32_to_bf16x8(acc);
+          } else {
+            for (int e = 0; e < 8 && feat + e < p.n; ++e) dst[e] = __float2bfloat16(acc[e]);
+          }
         }
       }
     }
     cluster_sync_all();  // peers are done reading this CTA's export before it is overwritten / freed
+    if (tr && threadIdx.x == 0 && w0 == 0) tr[5] = globaltimer();
   }
   if (p.rs.rows > 0) {
     __syncthreads();
     if (threadIdx.x == 0) dec_rs_arrive(p.rs);
   }
+  if (tr && threadIdx.x == 0) tr[6] = globaltimer();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
@@ -1631,6 +1673,16 @@ int sk_capacity(int splits, int smem) {
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
   cudaFuncSetAttribute(gemm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM_MAX);
+  if (splits == 1) {  // no cluster: CTAs per SM x SMs
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_skinny_kernel, NUM_THREADS, smem) != cudaSuccess ||
+        per_sm <= 0) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
+    cache[key] = per_sm * num_sms();
+    return cache[key];
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(splits * 64, 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
@@ -1694,7 +1746,7 @@ std::vector<SkCfg> sk_candidates(int m, int n, int k, int act) {
 
 cudaError_t run_skinny(const SkCfg& d, const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc,
                        int m, int n, int k, cudaStream_t stream, int act = 0, const GemmRsEpilogue* rs = nullptr,
-                       int blocked = 0) {
+                       int blocked = 0, uint64_t* trace = nullptr) {
   if (m > 256 || k % BK || (act && n % 32) || ldc % 8) return cudaErrorInvalidValue;
   if (blocked && n % BM) return cudaErrorInvalidValue;
   CUtensorMap mx, mw;
@@ -1712,6 +1764,7 @@ cudaError_t run_skinny(const SkCfg& d, const void* x, int64_t ldx, const void* w
   p.stages = d.stages;
   p.act = act;
   p.blocked = blocked;
+  p.trace = trace;
   // D f32, A bf16 (weights), B bf16 (tokens), N = np, M = 128
   p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(d.np >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
   p.c = static_cast<__nv_bfloat16*>(c);
@@ -1765,9 +1818,28 @@ bool gemm_dec_plan(int m, int n, int k, int rank, GemmPlan* plan) {
   return true;
 }
 
-// Decode-kernel plans worth timing: the `each` cheapest by either model (deduplicated).
+// Decode-kernel plans worth timing: the `each` cheapest by either model, plus the two narrowest
+// single-split shapes that fill the GPU in one wave (no split-K reduction at all), deduplicated.
 static std::vector<GemmPlan> dec_plans_for_tuning(int m, int n, int k, int each, int act) {
   std::vector<GemmPlan> out;
+  {
+    auto all = dec_candidates(m, n, k);
+    std::vector<DecCfg> one;
+    for (const auto& d : all)
+      if (d.splits == 1 && d.tiles <= num_sms() && (!act || d.bn % 32 == 0)) one.push_back(d);
+    std::sort(one.begin(), one.end(), [](const DecCfg& a, const DecCfg& b) {
+      return a.bn != b.bn ? a.bn < b.bn : a.w_stages > b.w_stages;
+    });
+    int taken = 0;
+    int last_bn = -1;
+    for (const auto& d : one) {
+      if (taken >= 2) break;
+      if (d.bn == last_bn) continue;
+      last_bn = d.bn;
+      out.push_back(dec_to_plan(d, k));
+      ++taken;
+    }
+  }
   for (int by_traffic = 0; by_traffic < 2; ++by_traffic) {
     int taken = 0;
     for (const auto& d : dec_candidates(m, n, k, by_traffic != 0)) {
@@ -1819,9 +1891,9 @@ static SkCfg plan_to_skinny(const GemmPlan& pl) {
 }
 
 cudaError_t gemm_skinny_run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n,
-                            int k, const GemmPlan& plan, int act, int blocked, cudaStream_t stream) {
+                            int k, const GemmPlan& plan, int act, int blocked, cudaStream_t stream, uint64_t* trace) {
   if (plan.dec != 2) return cudaErrorInvalidValue;
-  return run_skinny(plan_to_skinny(plan), x, ldx, w, ldw, c, ldc, m, n, k, stream, act, nullptr, blocked);
+  return run_skinny(plan_to_skinny(plan), x, ldx, w, ldw, c, ldc, m, n, k, stream, act, nullptr, blocked, trace);
 }
 
 static GemmPlan dec_to_plan(const DecCfg& d, int k) {

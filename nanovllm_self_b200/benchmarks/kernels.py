@@ -216,6 +216,60 @@ def gemm_sweep(ms=(1, 16, 64, 128, 256), iters: int = 20) -> None:
         del w
 
 
+def gemm_chain(ms=(1, 16, 64, 128, 256), calls: int = 24) -> None:
+    """Decode GEMMs as the engine runs them: `calls` back-to-back launches captured in one CUDA
+    graph (programmatic dependent launch lets each GEMM's weight stream start while the previous
+    kernel finishes), weights rotating over enough copies to exceed the L2.  Per-call time =
+    graph replay time / calls; ours (autotuned) against cuBLAS (torch.matmul) in the same form."""
+    ops = CudaOps()
+    hbm, tfl, src = _peaks()
+    for name, (n, k) in DECODE_SHAPES.items():
+        if name == "lm_head":
+            continue
+        wbytes = n * k * 2
+        copies = max(2, min(calls, (384 << 20) // wbytes + 1))
+        ws = [(torch.randn(n, k, device="cuda") * 0.02).to(torch.bfloat16) for _ in range(copies)]
+        for m in ms:
+            x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+            out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+            res = {}
+            for impl in ("ours", "cublas"):
+                def body():
+                    for i in range(calls):
+                        if impl == "ours":
+                            ops.linear(x, ws[i % copies], out)
+                        else:
+                            torch.matmul(x, ws[i % copies].t(), out=out)
+                s = torch.cuda.Stream()
+                s.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(s):
+                    body()  # tunes outside the capture
+                torch.cuda.current_stream().wait_stream(s)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    body()
+                for _ in range(3):
+                    g.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(5):
+                    g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                res[impl] = e0.elapsed_time(e1) * 1e3 / (5 * calls)
+                del g
+            roof = max(2 * (m * k + n * k + m * n) / (hbm * 1e3), 2 * m * n * k / (tfl * 1e6))
+            print(json.dumps({"shape": name, "m": m, "n": n, "k": k, "ours_us": round(res["ours"], 2),
+                              "cublas_us": round(res["cublas"], 2), "ours_vs_cublas": round(res["cublas"] / res["ours"], 3),
+                              "roofline_us": round(roof, 2), "frac_roofline": round(roof / res["ours"], 3),
+                              "plan": dict(zip(("swap", "bn", "tiles_p", "tiles_q", "splits", "grid"), ops.last_plan)),
+                              "timing": f"CUDA graph of {calls} calls, weights rotating over {copies} copies",
+                              "peaks": src}), flush=True)
+        del ws
+
+
 def gemm_one(m: int, n: int, k: int, impl: str, mode: str, iters: int = 20) -> None:
     """One GEMM shape with one implementation: ``tuned`` (the autotuner's pick), ``cublas``
     (torch.matmul), ``skinny:R`` / ``dec:R`` (the R-th configuration of that kernel's model)."""
@@ -271,7 +325,7 @@ def gemm_one(m: int, n: int, k: int, impl: str, mode: str, iters: int = 20) -> N
 
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("case", choices=CASES + ("all", "gemm_sweep", "gemm_one"))
+    p.add_argument("case", choices=CASES + ("all", "gemm_sweep", "gemm_one", "gemm_chain"))
     p.add_argument("--m", type=int, default=1)
     p.add_argument("--n", type=int, default=6144)
     p.add_argument("--k", type=int, default=4096)
@@ -282,6 +336,9 @@ def main(argv=None):
     a = p.parse_args(argv)
     if a.case == "gemm_sweep":
         gemm_sweep(iters=a.iters)
+        return
+    if a.case == "gemm_chain":
+        gemm_chain()
         return
     if a.case == "gemm_one":
         for impl in a.impl.split(","):
