@@ -38,7 +38,7 @@ void add_rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual_
   at::cuda::CUDAGuard g(x.device());
   check(nvb::launch_add_rmsnorm(x.data_ptr(), x.stride(0), ptr_or_null<void>(residual_in),
                                 ptr_or_null<void>(residual_out), w.data_ptr(), out.data_ptr(), rows, H, (float)eps,
-                                ptr_or_null<int>(row_index), stream()),
+                                ptr_or_null<int>(row_index), stream(), (int)x.size(0)),
         "add_rmsnorm");
 }
 
@@ -77,7 +77,7 @@ void qkv_post(const at::Tensor& qkv, at::Tensor& q_out, const at::Tensor& q_norm
                              (float)eps, positions.data_ptr<int>(), cos_sin.data_ptr<float>(), k_cache.data_ptr(),
                              v_cache.data_ptr(), ptr_or_null<float>(k_scale), ptr_or_null<float>(v_scale),
                              slots.data_ptr<int>(), (int)qkv.size(0), (int)nq, (int)nkv, (int)k_cache.size(3),
-                             (int)k_cache.size(2), fp8, stream()),
+                             (int)k_cache.size(2), fp8, stream(), (int)k_cache.size(0)),
         "qkv_post");
 }
 
@@ -214,6 +214,14 @@ int64_t sample_x_floats(int64_t world, int64_t rows_cap) { return nvb::sample_x_
 int64_t sample_f_words(int64_t world, int64_t rows_cap) { return nvb::sample_f_words((int)world, (int)rows_cap); }
 int64_t sample_error(bool reset) { return nvb::sample_error_code(reset ? 1 : 0); }
 
+// First index-check error recorded by the checked kernels (401: gathered norm row out of range,
+// 402: KV slot beyond the pool), 0 if none.
+int64_t bounds_error(bool reset) {
+  const int a = nvb::norm_check_code(reset ? 1 : 0);
+  const int b = nvb::qkv_check_code(reset ? 1 : 0);
+  return a ? a : b;
+}
+
 }  // namespace
 
 void register_gemm(pybind11::module& m);
@@ -243,6 +251,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample_f_words", &sample_f_words);
   m.def("sample_rows_capacity", &nvb::sample_rows_capacity);
   m.def("sample_error", &sample_error, pybind11::arg("reset") = false);
+  m.def("bounds_error", &bounds_error, pybind11::arg("reset") = false);
+  m.attr("BOUNDS_CHECK") = (int64_t)nvb::bounds_check_enabled();
   register_gemm(m);
   register_comm(m);
 }

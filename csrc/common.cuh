@@ -7,9 +7,28 @@
 
 #include <atomic>
 
+// Index checks on the scattered accesses whose indices come from the host (KV slots, gathered
+// rows).  On (the default) every such index is range-checked; a bad one records an error code
+// in the kernel file's check word (read with bounds_error) and the access is skipped, so a bad
+// index never faults the GPU.  Building with -DNVB_BOUNDS_CHECK=0 removes the checks.
+#ifndef NVB_BOUNDS_CHECK
+#define NVB_BOUNDS_CHECK 1
+#endif
+
 namespace nvb {
 
 constexpr unsigned FULL_MASK = 0xffffffffu;
+
+// True when 0 <= i < n; otherwise records `code` in *word (first error wins) and returns false.
+__device__ __forceinline__ bool in_range(long long i, long long n, int* word, int code) {
+#if NVB_BOUNDS_CHECK
+  if (i < 0 || i >= n) {
+    atomicCAS(word, 0, code);
+    return false;
+  }
+#endif
+  return true;
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

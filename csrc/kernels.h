@@ -5,16 +5,20 @@
 
 namespace nvb {
 
+// src_rows: rows of x (and residual_in) that row_index may address (checked, see NVB_BOUNDS_CHECK).
 cudaError_t launch_add_rmsnorm(const void* x, int64_t x_stride, const void* residual_in, void* residual_out,
                                const void* w, void* out, int rows, int H, float eps, const int* row_index,
-                               cudaStream_t stream);
+                               cudaStream_t stream, int src_rows = 0x7fffffff);
+int norm_check_code(int reset);
+int bounds_check_enabled();
+int qkv_check_code(int reset);
 cudaError_t launch_silu_mul(const void* x, void* out, int T, int I, cudaStream_t stream);
 cudaError_t launch_embedding(const int* ids, const void* table, int rows, int vocab_start, void* out, int T, int H,
                              cudaStream_t stream);
 cudaError_t launch_qkv_post(const void* qkv, int64_t qkv_stride, void* q_out, const void* q_norm, const void* k_norm,
                             float eps, const int* positions, const float* cos_sin, void* k_cache, void* v_cache,
                             float* k_scale, float* v_scale, const int* slots, int T, int nq, int nkv, int head_dim,
-                            int block_size, int kv_fp8, cudaStream_t stream);
+                            int block_size, int kv_fp8, cudaStream_t stream, int num_blocks = 0x7fffffff);
 
 struct AttnLaunch {
   const void* q;

@@ -8,6 +8,20 @@
 
 namespace nvb {
 
+__device__ int g_norm_check = 0;  // bounds-check word of this file (401: gathered row out of range)
+
+int bounds_check_enabled() { return NVB_BOUNDS_CHECK; }
+
+int norm_check_code(int reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_norm_check, sizeof(int));
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_norm_check, &z, sizeof(int));
+  }
+  return v;
+}
+
 // One CTA per output row.  residual_out = x + residual_in (rounded to bf16, as an
 // eager bf16 add would be); out = rmsnorm(residual_out) * w.  residual_in == nullptr
 // means the residual is x itself and nothing is written to residual_out.  With
@@ -17,11 +31,13 @@ template <int NI>
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
                                                           const __nv_bfloat16* residual_in, __nv_bfloat16* residual_out,
                                                           const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
-                                                          int H, float eps, const int* __restrict__ row_index) {
+                                                          int H, float eps, const int* __restrict__ row_index,
+                                                          int src_rows) {
   pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
   const int row = blockIdx.x;
   const int src_row = row_index ? row_index[row] : row;
+  if (row_index && !in_range(src_row, src_rows, &g_norm_check, 401)) return;  // uniform over the CTA
   const int nvec = H >> 3;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)src_row * x_stride);
   float v[NI][8];
@@ -71,7 +87,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const __nv_bfloat16* _
 
 cudaError_t launch_add_rmsnorm(const void* x, int64_t x_stride, const void* residual_in, void* residual_out,
                                const void* w, void* out, int rows, int H, float eps, const int* row_index,
-                               cudaStream_t stream) {
+                               cudaStream_t stream, int src_rows) {
   if (rows == 0) return cudaSuccess;
   if (H % 8 != 0 || H > 8 * 256 * 4) return cudaErrorInvalidValue;
   int nvec = H / 8;
@@ -83,10 +99,10 @@ cudaError_t launch_add_rmsnorm(const void* x, int64_t x_stride, const void* resi
   auto W = static_cast<const __nv_bfloat16*>(w);
   auto O = static_cast<__nv_bfloat16*>(out);
   switch (ni) {
-    case 1: launch_pdl(add_rmsnorm_kernel<1>, dim3(rows), dim3(threads), 0, stream, X, x_stride, R, RO, W, O, H, eps, row_index); break;
-    case 2: launch_pdl(add_rmsnorm_kernel<2>, dim3(rows), dim3(threads), 0, stream, X, x_stride, R, RO, W, O, H, eps, row_index); break;
-    case 3: launch_pdl(add_rmsnorm_kernel<3>, dim3(rows), dim3(threads), 0, stream, X, x_stride, R, RO, W, O, H, eps, row_index); break;
-    default: launch_pdl(add_rmsnorm_kernel<4>, dim3(rows), dim3(threads), 0, stream, X, x_stride, R, RO, W, O, H, eps, row_index); break;
+    case 1: launch_pdl(add_rmsnorm_kernel<1>, dim3(rows), dim3(threads), 0, stream, X, x_stride, R, RO, W, O, H, eps, row_index, src_rows); break;
+    case 2: launch_pdl(add_rmsnorm_kernel<2>, dim3(rows), dim3(threads), 0, stream, X, x_stride, R, RO, W, O, H, eps, row_index, src_rows); break;
+    case 3: launch_pdl(add_rmsnorm_kernel<3>, dim3(rows), dim3(threads), 0, stream, X, x_stride, R, RO, W, O, H, eps, row_index, src_rows); break;
+    default: launch_pdl(add_rmsnorm_kernel<4>, dim3(rows), dim3(threads), 0, stream, X, x_stride, R, RO, W, O, H, eps, row_index, src_rows); break;
   }
   NVB_LAUNCH_CHECK();
   return cudaSuccess;

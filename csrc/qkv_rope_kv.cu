@@ -35,7 +35,20 @@ struct QkvPostArgs {
   const int* slots;
   int T, nq, nkv, block_size;
   int kv_fp8;
+  int num_blocks;  // pool blocks: slots must lie in [0, num_blocks * block_size) (-1: skip)
 };
+
+__device__ int g_qkv_check = 0;  // bounds-check word of this file (402: KV slot beyond the pool)
+
+int qkv_check_code(int reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_qkv_check, sizeof(int));
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_qkv_check, &z, sizeof(int));
+  }
+  return v;
+}
 
 // Load 4 lanes' worth (4 elements) of head `head` of token t, optionally normalise with
 // `nw` and rotate at `pos`.  Every lane of the warp must call it (uses shuffles).
@@ -133,6 +146,7 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(QkvPostArgs a) {
     const __nv_bfloat16* nw = is_k ? a.k_norm : nullptr;
     norm_rope(a, nw, is_k, cs, lane, x);
     if (slot < 0) continue;
+    if (!in_range(slot, (long long)a.num_blocks * a.block_size, &g_qkv_check, 402)) continue;
     const int blk = slot / a.block_size, off = slot - blk * a.block_size;
     const int64_t dst = (((int64_t)blk * a.nkv + h) * a.block_size + off) * HD + lane * 4;
     if (!a.kv_fp8) {
@@ -167,7 +181,7 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(QkvPostArgs a) {
 cudaError_t launch_qkv_post(const void* qkv, int64_t qkv_stride, void* q_out, const void* q_norm, const void* k_norm,
                             float eps, const int* positions, const float* cos_sin, void* k_cache, void* v_cache,
                             float* k_scale, float* v_scale, const int* slots, int T, int nq, int nkv, int head_dim,
-                            int block_size, int kv_fp8, cudaStream_t stream) {
+                            int block_size, int kv_fp8, cudaStream_t stream, int num_blocks) {
   if (T == 0) return cudaSuccess;
   if (head_dim != HD) return cudaErrorInvalidValue;
   QkvPostArgs a;
@@ -189,6 +203,7 @@ cudaError_t launch_qkv_post(const void* qkv, int64_t qkv_stride, void* q_out, co
   a.nkv = nkv;
   a.block_size = block_size;
   a.kv_fp8 = kv_fp8;
+  a.num_blocks = num_blocks;
   int64_t warps = (int64_t)T * ((nq + 2 * nkv + QKV_HPW - 1) / QKV_HPW);
   int64_t blocks = (warps + 3) / 4;
   launch_pdl(qkv_post_kernel, dim3((unsigned)blocks), dim3(128), 0, stream, a);
