@@ -85,6 +85,11 @@ cudaError_t gemm_bf16_rs(const void* x, int64_t ldx, const void* w, int64_t ldw,
                          const GemmRsEpilogue& rs, void* tune_c, int64_t tune_ldc, cudaStream_t stream,
                          GemmPlan* chosen);
 
+// Deterministic mode (default: environment NVB_DETERMINISTIC): plans chosen from the shape alone,
+// never by timing, so every process runs a shape with the same kernel and split-K order.
+void gemm_set_deterministic(int on);
+int gemm_deterministic();
+
 // Error word written by a GEMM that gave up on a bounded wait (0 = none).
 int gemm_error_code(int reset);
 

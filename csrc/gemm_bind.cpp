@@ -197,4 +197,6 @@ void register_gemm(pybind11::module& m) {
         pybind11::arg("blocked") = 0, pybind11::arg("trace") = c10::nullopt);
   m.def("linear_rs", &linear_rs, "tcgen05 decode GEMM whose rows are stored at their owner rank (reduce-scatter)");
   m.def("gemm_error", &error_code, pybind11::arg("reset") = false);
+  m.def("gemm_set_deterministic", [](bool on) { nvb::gemm_set_deterministic(on ? 1 : 0); });
+  m.def("gemm_deterministic", []() { return nvb::gemm_deterministic() != 0; });
 }

@@ -2095,12 +2095,31 @@ std::mutex& tune_mutex() {
   return mu;
 }
 int m_bucket(int m) { return m <= 256 ? m : ((m + 511) / 512) * 512; }
+
+// Deterministic mode: plans come from the shape alone (no timing), so every process computes a
+// shape with the same kernel and the same split-K order (bit-identical results across the
+// processes of a P/D pair or a TP group).  Default from the environment (NVB_DETERMINISTIC=1).
+std::atomic<int>& deterministic_flag() {
+  static std::atomic<int> f{[] {
+    const char* e = getenv("NVB_DETERMINISTIC");
+    return e && e[0] && e[0] != '0' ? 1 : 0;
+  }()};
+  return f;
+}
 }  // namespace
+
+void gemm_set_deterministic(int on) { deterministic_flag().store(on ? 1 : 0); }
+int gemm_deterministic() { return deterministic_flag().load(); }
 
 cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n,
                             int k, float* ws, int64_t ws_elems, int* counters, int64_t num_counters,
                             cudaStream_t stream, GemmPlan* chosen, int act) {
   if (m == 0 || n == 0) return cudaSuccess;
+  if (gemm_deterministic()) {  // the shape alone decides, whatever was tuned before
+    const GemmPlan pl = gemm_plan(m, n, k, act ? 0 : -1, 0, 0);
+    if (chosen) *chosen = pl;
+    return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, pl, ws, counters, stream, act);
+  }
   const auto key = std::make_tuple(m_bucket(m), act ? -n : n, k);
   {
     std::lock_guard<std::mutex> g(tune_mutex());
@@ -2113,7 +2132,7 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   cudaStreamIsCapturing(stream, &cap);
   GemmPlan best = gemm_plan(m, n, k, act ? 0 : -1, 0, 0);
-  if (cap != cudaStreamCaptureStatusNone) {  // cannot time inside a capture
+  if (cap != cudaStreamCaptureStatusNone || gemm_deterministic()) {  // no timing: capture or deterministic
     if (chosen) *chosen = best;
     return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, best, ws, counters, stream, act);
   }
@@ -2194,7 +2213,7 @@ cudaError_t gemm_bf16_rs(const void* x, int64_t ldx, const void* w, int64_t ldw,
   const auto key = std::make_tuple(m, n, k);
   GemmPlan best{};
   bool have = false;
-  {
+  if (!gemm_deterministic()) {
     std::lock_guard<std::mutex> g(tune_mutex());
     auto it = cache.find(key);
     if (it != cache.end()) {
@@ -2209,7 +2228,7 @@ cudaError_t gemm_bf16_rs(const void* x, int64_t ldx, const void* w, int64_t ldw,
     best = cands[0];
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(stream, &cap);
-    if (cap == cudaStreamCaptureStatusNone && tune_c && cands.size() > 1) {
+    if (cap == cudaStreamCaptureStatusNone && tune_c && cands.size() > 1 && !gemm_deterministic()) {
       // time the candidates with a plain local output (the reduce-scatter stores and flags
       // must only happen once per reduction), each after a 256 MiB read (cold L2)
       const size_t flush_bytes = (size_t)256 << 20;

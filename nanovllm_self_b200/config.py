@@ -108,6 +108,9 @@ class EngineConfig:
     # Use the hand-written CUDA ops (True) or the torch reference ops (False, CPU/oracle).
     use_custom_kernels: bool | None = None
     enforce_eager: bool = False
+    # GEMM plans from the shape alone instead of timing (identical numerics in every process:
+    # P/D pairs and TP groups reproduce a monolithic run bit for bit); also NVB_DETERMINISTIC=1
+    deterministic: bool = False
     # Allocate the KV pool with cudaMalloc + CUDA IPC so another process can push blocks
     # into it (the decode side of the NVLink P/D push).
     kv_pool_ipc: bool = False

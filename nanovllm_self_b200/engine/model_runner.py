@@ -64,6 +64,8 @@ class ModelRunner:
             else:
                 random_init(self.model, seed=config.seed, std=config.init_std)
         self.ops = get_ops(self.device, config.use_custom_kernels)
+        if config.deterministic and hasattr(self.ops, "C"):
+            self.ops.C.gemm_set_deterministic(True)
         self.comm = comm
         max_pos = max(config.max_model_len + 1, 16)
         self.model.finalize(self.ops, comm, max_position=max(max_pos, self.arch.max_position_embeddings))
