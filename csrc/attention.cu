@@ -1063,6 +1063,8 @@ struct Args {
   int nq, nkv, G, block_size, num_blocks, seq_offset;
   int kv_box;       // rows per K/V TMA box: min(block_size, 128)
   int kv_rows;      // rows of the 2-D [NB * nkv * BS, 128] pool view (an out-of-range row start)
+  int qtiles;       // query tiles of the longest sequence of the launch
+  int num_seqs;     // sequences of the launch (from seq_offset)
   float scale_log2;
 };
 
@@ -1148,15 +1150,19 @@ __device__ __forceinline__ constexpr uint32_t idesc(bool b_mn_major) {
          ((uint32_t)(128 >> 4) << 24);
 }
 
-// TMEM columns: S buffers at 0 and 128, O at 256.
+// TMEM columns: S buffers at 0 and 128, O buffers at 256 and 384.
 __device__ __forceinline__ constexpr uint32_t s_col(int s) { return s ? 128u : 0u; }
-constexpr uint32_t O_COL = 256;
+__device__ __forceinline__ constexpr uint32_t o_col(int s) { return s ? 384u : 256u; }
 
 }  // namespace pf
 
-__global__ void __launch_bounds__(pf::THREADS, 1)
+__global__ void __maxnreg__(200)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                            const __grid_constant__ CUtensorMap vmap, pf::Args a) {
+  // Persistent: one CTA per SM walks the (query tile, KV head, sequence) items round-robin,
+  // heaviest (latest) query tiles first.  Barrier phases and the K/V ring, S buffers and the
+  // P V completion count run on CTA-wide counters across items; O is double-buffered in TMEM
+  // so the softmax warps store one item's output while the MMAs of the next item run.
   using namespace pf;
   pdl_wait();     // inputs come from the previous kernel in the stream
   pdl_trigger();  // the next kernel may start its prologue
@@ -1166,36 +1172,51 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
   uint8_t* sk = sq + TILE;                    // K ring: NSTAGE x TILE
   uint8_t* sv = sk + NSTAGE * TILE;           // V ring: NSTAGE x TILE
   uint64_t* bars = reinterpret_cast<uint64_t*>(sv + NSTAGE * TILE);
-  // bars: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_ready[2], s_free[2], o_done, o_final
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 17);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18);
+  // bars: q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_ready[2], s_free[2],
+  //       o_done, o_final[2], o_empty[2], drain
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 22);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 23);
   const uint32_t b0 = smem_u32(bars);
-  const uint32_t q_full = b0;
-  auto k_full = [&](int s) { return b0 + 8u * (1 + s); };
-  auto k_empty = [&](int s) { return b0 + 8u * (3 + s); };
-  auto v_full = [&](int s) { return b0 + 8u * (5 + s); };
-  auto v_empty = [&](int s) { return b0 + 8u * (7 + s); };
-  auto s_full = [&](int s) { return b0 + 8u * (9 + s); };
-  auto p_ready = [&](int s) { return b0 + 8u * (11 + s); };
-  auto s_free = [&](int s) { return b0 + 8u * (13 + s); };
-  const uint32_t o_done = b0 + 8u * 15, o_final = b0 + 8u * 16;
+  const uint32_t q_full = b0, q_empty = b0 + 8u;
+  auto k_full = [&](int s) { return b0 + 8u * (2 + s); };
+  auto k_empty = [&](int s) { return b0 + 8u * (4 + s); };
+  auto v_full = [&](int s) { return b0 + 8u * (6 + s); };
+  auto v_empty = [&](int s) { return b0 + 8u * (8 + s); };
+  auto s_full = [&](int s) { return b0 + 8u * (10 + s); };
+  auto p_ready = [&](int s) { return b0 + 8u * (12 + s); };
+  auto s_free = [&](int s) { return b0 + 8u * (14 + s); };
+  const uint32_t o_done = b0 + 8u * 16;
+  auto o_final = [&](int s) { return b0 + 8u * (17 + s); };
+  auto o_empty = [&](int s) { return b0 + 8u * (19 + s); };
+  const uint32_t drain = b0 + 8u * 21;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
   const int G = a.G, TQ = TQ_ROWS / G;
-  const int b = blockIdx.z + a.seq_offset;
-  const int h = blockIdx.y;
-  const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest (latest) query tiles first
-  const int qs = a.cu_q[b];
-  const int q_len = a.cu_q[b + 1] - qs;
-  const int t0 = qt * TQ;
-  if (t0 >= q_len) return;  // uniform over the CTA: nothing initialised yet
-  const int k_len = a.ctx_lens[b];
-  const int off = k_len - q_len;
-  const int kmax = min(k_len, off + min(q_len, t0 + TQ));
-  const int n_tiles = (kmax + TK - 1) / TK;
+  const int items = a.qtiles * a.nkv * a.num_seqs;
+
+  // Item i -> (sequence, KV head, query tile) and its extent; false when the tile is empty.
+  struct Item {
+    int b, h, qs, q_len, t0, k_len, off, n_tiles;
+  };
+  auto item = [&](int i, Item& it) -> bool {
+    const int per = a.nkv * a.num_seqs;
+    const int qt = a.qtiles - 1 - i / per;
+    const int rem = i % per;
+    it.h = rem / a.num_seqs;
+    it.b = rem % a.num_seqs + a.seq_offset;
+    it.qs = a.cu_q[it.b];
+    it.q_len = a.cu_q[it.b + 1] - it.qs;
+    it.t0 = qt * TQ;
+    if (it.t0 >= it.q_len) return false;
+    it.k_len = a.ctx_lens[it.b];
+    it.off = it.k_len - it.q_len;
+    const int kmax = min(it.k_len, it.off + min(it.q_len, it.t0 + TQ));
+    it.n_tiles = (kmax + TK - 1) / TK;
+    return it.n_tiles > 0;
+  };
 
   if (threadIdx.x == 0) {
     bar_init(q_full, 1);
+    bar_init(q_empty, 1);
     for (int s = 0; s < 2; ++s) {
       bar_init(k_full(s), 1);
       bar_init(k_empty(s), 1);
@@ -1204,9 +1225,11 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
       bar_init(s_full(s), 1);
       bar_init(p_ready(s), 256);
       bar_init(s_free(s), 1);
+      bar_init(o_final(s), 1);
+      bar_init(o_empty(s), 256);
     }
     bar_init(o_done, 1);
-    bar_init(o_final, 1);
+    bar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1232,78 +1255,120 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
     }
     return true;
   };
+  // Exit path: waits for a phase regardless of the abort flag (bounded), so no copy or MMA
+  // of this CTA is still writing shared memory or TMEM when the CTA frees them.
+  auto settle = [&](uint32_t bar, uint32_t parity) {
+    const uint64_t tstart = att_timer();
+    while (!att_try(bar, parity))
+      if (att_timer() - tstart > ATT_WAIT_NS) {
+        atomicCAS(&g_attn_error, 0, 51);
+        return;
+      }
+  };
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------------ TMA producer
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&qmap)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&vmap)) : "memory");
-    expect_tx(q_full, TILE);
-    for (int half = 0; half < 2; ++half)
-      tma3d(smem_u32(sq + half * HALF), &qmap, q_full, half * 64, h * G, qs + t0);
-    const int* bt = a.block_tables + (int64_t)b * a.W;
     const int boxes = TK / a.kv_box;
     bool ok = true;
-    for (int j = 0; j < n_tiles && ok; ++j) {
-      const int s = j & 1;
-      const uint32_t par = ((j >> 1) & 1) ^ 1;
-      for (int kv = 0; kv < 2 && ok; ++kv) {
-        if (!wait(kv ? v_empty(s) : k_empty(s), par, 40)) {
-          ok = false;
-          break;
-        }
-        const uint32_t full = kv ? v_full(s) : k_full(s);
-        uint8_t* dst = (kv ? sv : sk) + s * TILE;
-        expect_tx(full, TILE);
-        for (int bx = 0; bx < boxes; ++bx) {
-          const int tk = j * TK + bx * a.kv_box;
-          const int bi = tk / a.block_size;
-          int row = a.kv_rows;  // past the end: the box reads as zeros
-          if (tk < k_len && bi < a.W) {
-            const int blk = bt[bi];
-            if (blk >= 0 && blk < a.num_blocks) row = (blk * a.nkv + h) * a.block_size + (tk % a.block_size);
+    int g = 0, n_it = 0;
+    int last[2][2] = {{-1, -1}, {-1, -1}};  // [K/V][stage]: tile of the last load issued there
+    for (int i = blockIdx.x; i < items && ok; i += gridDim.x) {
+      Item it;
+      if (!item(i, it)) continue;
+      // the previous item's S MMAs are done reading Q
+      if (n_it >= 1 && !wait(q_empty, (n_it - 1) & 1, 49)) break;
+      ++n_it;
+      expect_tx(q_full, TILE);
+      for (int half = 0; half < 2; ++half)
+        tma3d(smem_u32(sq + half * HALF), &qmap, q_full, half * 64, it.h * G, it.qs + it.t0);
+      const int* bt = a.block_tables + (int64_t)it.b * a.W;
+      for (int j = 0; j < it.n_tiles && ok; ++j, ++g) {
+        const int s = g & 1;
+        const uint32_t par = ((g >> 1) & 1) ^ 1;
+        for (int kv = 0; kv < 2 && ok; ++kv) {
+          if (!wait(kv ? v_empty(s) : k_empty(s), par, 40)) {
+            ok = false;
+            break;
           }
-          for (int half = 0; half < 2; ++half)
-            tma2d(smem_u32(dst + half * HALF + bx * a.kv_box * 128), kv ? &vmap : &kmap, full, half * 64, row);
+          const uint32_t full = kv ? v_full(s) : k_full(s);
+          uint8_t* dst = (kv ? sv : sk) + s * TILE;
+          last[kv][s] = g;
+          expect_tx(full, TILE);
+          for (int bx = 0; bx < boxes; ++bx) {
+            const int tk = j * TK + bx * a.kv_box;
+            const int bi = tk / a.block_size;
+            int row = a.kv_rows;  // past the end: the box reads as zeros
+            if (tk < it.k_len && bi < a.W) {
+              const int blk = bt[bi];
+              if (blk >= 0 && blk < a.num_blocks) row = (blk * a.nkv + it.h) * a.block_size + (tk % a.block_size);
+            }
+            for (int half = 0; half < 2; ++half)
+              tma2d(smem_u32(dst + half * HALF + bx * a.kv_box * 128), kv ? &vmap : &kmap, full, half * 64, row);
+          }
         }
       }
+    }
+    if (*abort_flag) {  // loads nobody consumed may still be landing
+      if (n_it) settle(q_full, (n_it - 1) & 1);
+      for (int kv = 0; kv < 2; ++kv)
+        for (int s = 0; s < 2; ++s)
+          if (last[kv][s] >= 0) settle(kv ? v_full(s) : k_full(s), (last[kv][s] >> 1) & 1);
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------------ MMA issuer
     const uint32_t id_qk = idesc(false), id_pv = idesc(true);
-    bool ok = wait(q_full, 0, 41);
     const uint32_t qa = smem_u32(sq);
-    for (int j = 0; j <= n_tiles && ok; ++j) {
-      if (j < n_tiles) {
-        const int s = j & 1;
-        if (!wait(k_full(s), (j >> 1) & 1, 42)) break;
-        if (j >= 2 && !wait(s_free(s), ((j - 2) >> 1) & 1, 43)) break;
-        fence_after();
-        const uint32_t kb = smem_u32(sk + s * TILE);
+    bool ok = true;
+    int g = 0, n_it = 0;
+    for (int i = blockIdx.x; i < items && ok; i += gridDim.x) {
+      Item it;
+      if (!item(i, it)) continue;
+      const int ob = n_it & 1;
+      if (!wait(q_full, n_it & 1, 41)) break;
+      const int n = it.n_tiles;
+      for (int j = 0; j <= n && ok; ++j) {
+        if (j < n) {
+          const int gs = g + j, s = gs & 1;
+          if (!wait(k_full(s), (gs >> 1) & 1, 42)) { ok = false; break; }
+          if (gs >= 2 && !wait(s_free(s), ((gs - 2) >> 1) & 1, 43)) { ok = false; break; }
+          fence_after();
+          const uint32_t kb = smem_u32(sk + s * TILE);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t ho = (k >> 2) * HALF + (k & 3) * 32;  // 16-element step inside a 64-dim half
-          mma_ss(tmem + s_col(s), desc_sw128(qa + ho, 16, 1024), desc_sw128(kb + ho, 16, 1024), id_qk, k > 0);
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t ho = (k >> 2) * HALF + (k & 3) * 32;  // 16-element step inside a 64-dim half
+            mma_ss(tmem + s_col(s), desc_sw128(qa + ho, 16, 1024), desc_sw128(kb + ho, 16, 1024), id_qk, k > 0);
+          }
+          commit(s_full(s));
+          commit(k_empty(s));
+          if (j == n - 1) commit(q_empty);  // every S MMA of this item reads Q before this completes
         }
-        commit(s_full(s));
-        commit(k_empty(s));
-      }
-      if (j >= 1) {
-        const int jj = j - 1, s = jj & 1;
-        if (!wait(p_ready(s), (jj >> 1) & 1, 44)) break;
-        if (!wait(v_full(s), (jj >> 1) & 1, 45)) break;
-        fence_after();
-        const uint32_t vb = smem_u32(sv + s * TILE);
+        if (j >= 1) {
+          const int gp = g + j - 1, s = gp & 1;
+          if (!wait(p_ready(s), (gp >> 1) & 1, 44)) { ok = false; break; }
+          if (!wait(v_full(s), (gp >> 1) & 1, 45)) { ok = false; break; }
+          // O[ob] was last used by the item two before this one: its output must have been read
+          if (j == 1 && n_it >= 2 && !wait(o_empty(ob), ((n_it >> 1) - 1) & 1, 50)) { ok = false; break; }
+          fence_after();
+          const uint32_t vb = smem_u32(sv + s * TILE);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)  // 16 keys per step: P columns 8k.., V rows 16k..
-          mma_ts(tmem + O_COL, tmem + s_col(s) + 8 * k, desc_sw128(vb + k * 16 * 128, HALF, 1024), id_pv,
-                 (jj > 0 || k > 0) ? 1u : 0u);
-        commit(o_done);
-        commit(v_empty(s));
-        commit(s_free(s));
+          for (int k = 0; k < 8; ++k)  // 16 keys per step: P columns 8k.., V rows 16k..
+            mma_ts(tmem + o_col(ob), tmem + s_col(s) + 8 * k, desc_sw128(vb + k * 16 * 128, HALF, 1024), id_pv,
+                   (j > 1 || k > 0) ? 1u : 0u);
+          commit(o_done);
+          commit(v_empty(s));
+          commit(s_free(s));
+        }
       }
+      if (!ok) break;
+      commit(o_final(ob));
+      g += n;
+      ++n_it;
     }
-    commit(o_final);
+    commit(drain);  // completes when every MMA this thread issued has completed
+    settle(drain, 0);
   } else if (warp >= 2) {
     // ------------------------------------------------------------------ softmax / output
     // Two warps per TMEM lane quarter: warp w serves rows 32 (w & 3) .. +31 and the key (and
@@ -1312,105 +1377,121 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
     const int q4 = warp & 3;
     const int half = (warp - 2) >> 2;
     const int r = q4 * 32 + lane;
-    const int t = t0 + r / G, g = r % G;
-    const int pos = off + t;
     const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
     const int c0 = half * 64;  // this thread's first key column of a tile / first head dim
     __shared__ float xmax[2][2][TQ_ROWS];  // [tile parity][half][row]
     __shared__ int xok[2][2][TQ_ROWS];
     __shared__ float xsum[2][TQ_ROWS];
+    __shared__ int xokf[2][TQ_ROWS];
     // Both warps of a pair pass the same sequence of pair barriers on every path (errors
-    // included): the decision to stop is taken from the exchanged flags, identically by both.
+    // included): both walk every item, and each decision to stop a tile loop is taken from the
+    // exchanged flags, identically by both.  After an error the remaining items cost one
+    // exchange each and touch no barrier, TMEM or output.
     auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + q4) : "memory"); };
-    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int s = j & 1;
-      if (ok) ok = wait(s_full(s), (j >> 1) & 1, 46);
-      fence_after();
-      uint32_t raw[64];
-      if (ok) {
-        tmem_ld32(lane_base + s_col(s) + c0, raw);
-        tmem_ld32(lane_base + s_col(s) + c0 + 32, raw + 32);
-        tmem_ld_wait();
-      }
-      const int lim = ok ? min(pos + 1, k_len) - j * TK - c0 : 0;  // keys [0, lim) of this half are visible
-      float x[64];
-      float mx = -INFINITY;
+    int g = 0, n_it = 0;
+    for (int i = blockIdx.x; i < items; i += gridDim.x) {
+      Item it;
+      if (!item(i, it)) continue;
+      const int ob = n_it & 1;
+      const int t = it.t0 + r / G, gq = r % G;
+      const int pos = it.off + t;
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < it.n_tiles; ++j) {
+        const int gs = g + j, s = gs & 1;
+        if (ok) ok = wait(s_full(s), (gs >> 1) & 1, 46);
+        fence_after();
+        uint32_t raw[64];
+        if (ok) {
+          tmem_ld32(lane_base + s_col(s) + c0, raw);
+          tmem_ld32(lane_base + s_col(s) + c0 + 32, raw + 32);
+          tmem_ld_wait();
+        }
+        const int lim = ok ? min(pos + 1, it.k_len) - j * TK - c0 : 0;  // keys [0, lim) of this half are visible
+        float x[64];
+        float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        x[c] = c < lim ? __uint_as_float(raw[c]) * a.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, x[c]);
-      }
-      xmax[s][half][r] = mx;
-      xok[s][half][r] = ok ? 1 : 0;
-      pair_sync();
-      mx = fmaxf(xmax[s][0][r], xmax[s][1][r]);
-      ok = xok[s][0][r] && xok[s][1][r];
-      if (!ok) break;  // identical in both warps of the pair
-      if (mx > m_used + RESCALE_LOG2 || m_used == -INFINITY) {
-        // raise the running maximum; O (if any) must be rescaled first (each half its 64 dims)
-        const float m_new = mx;
-        if (j > 0 && m_used != -INFINITY) {
-          if (!wait(o_done, (j - 1) & 1, 47)) {
-            ok = false;  // reported to the partner at the next exchange
-          } else {
-            fence_after();
-            const float f = exp2f(m_used - m_new);
+        for (int c = 0; c < 64; ++c) {
+          x[c] = c < lim ? __uint_as_float(raw[c]) * a.scale_log2 : -INFINITY;
+          mx = fmaxf(mx, x[c]);
+        }
+        xmax[s][half][r] = mx;
+        xok[s][half][r] = ok ? 1 : 0;
+        pair_sync();
+        mx = fmaxf(xmax[s][0][r], xmax[s][1][r]);
+        ok = xok[s][0][r] && xok[s][1][r];
+        if (!ok) break;  // identical in both warps of the pair
+        if (mx > m_used + RESCALE_LOG2 || m_used == -INFINITY) {
+          // raise the running maximum; O (if any) must be rescaled first (each half its 64 dims)
+          const float m_new = mx;
+          if (j > 0 && m_used != -INFINITY) {
+            if (!wait(o_done, (gs - 1) & 1, 47)) {
+              ok = false;  // reported to the partner at the next exchange
+            } else {
+              fence_after();
+              const float f = exp2f(m_used - m_new);
 #pragma unroll 1
-            for (int c = 0; c < 64; c += 32) {
-              uint32_t o[32];
-              tmem_ld32(lane_base + O_COL + c0 + c, o);
-              tmem_ld_wait();
+              for (int c = 0; c < 64; c += 32) {
+                uint32_t o[32];
+                tmem_ld32(lane_base + o_col(ob) + c0 + c, o);
+                tmem_ld_wait();
 #pragma unroll
-              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-              tmem_st32(lane_base + O_COL + c0 + c, o);
+                for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+                tmem_st32(lane_base + o_col(ob) + c0 + c, o);
+              }
+              tmem_st_wait();
+              l *= f;
             }
-            tmem_st_wait();
-            l *= f;
+          }
+          if (m_new != -INFINITY) m_used = m_new;
+        }
+        const float base = m_used == -INFINITY ? 0.f : m_used;
+        uint32_t pk[32];
+        float rs = 0.f;
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) {
+          const float p0 = exp2f(x[c] - base), p1 = exp2f(x[c + 1] - base);
+          rs += p0 + p1;
+          pk[c / 2] = pack_bf16(p0, p1);
+        }
+        l += rs;
+        tmem_st32(lane_base + s_col(s) + half * 32, pk);  // keys c0.. -> packed columns 32 half ..
+        tmem_st_wait();
+        fence_before();
+        arrive(p_ready(s));
+      }
+      // row sum over both halves (both warps of the pair reach this barrier on every path)
+      xsum[half][r] = l;
+      xokf[half][r] = ok ? 1 : 0;
+      pair_sync();
+      const float lt = xsum[0][r] + xsum[1][r];
+      ok = xokf[0][r] && xokf[1][r];
+      pair_sync();  // xsum / xok are rewritten by the next item
+      if (ok && wait(o_final(ob), (n_it >> 1) & 1, 48)) {
+        fence_after();
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+        __nv_bfloat16* dst = a.out + ((int64_t)(it.qs + t) * a.nq + it.h * G + gq) * 128 + c0;
+        const bool valid = t < it.q_len;
+#pragma unroll 1
+        for (int c = 0; c < 64; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(lane_base + o_col(ob) + c0 + c, o);
+          tmem_ld_wait();
+          if (valid) {
+            float f[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(o[e]) * inv;
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) *reinterpret_cast<uint4*>(dst + c + e) = f32_to_bf16x8(f + e);
           }
         }
-        if (m_new != -INFINITY) m_used = m_new;
+        fence_before();
+        arrive(o_empty(ob));
+      } else {
+        ok = false;
       }
-      const float base = m_used == -INFINITY ? 0.f : m_used;
-      uint32_t p[32];
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        const float p0 = exp2f(x[c] - base), p1 = exp2f(x[c + 1] - base);
-        rs += p0 + p1;
-        p[c / 2] = pack_bf16(p0, p1);
-      }
-      l += rs;
-      tmem_st32(lane_base + s_col(s) + half * 32, p);  // keys c0.. -> packed columns 32 half ..
-      tmem_st_wait();
-      fence_before();
-      arrive(p_ready(s));
-    }
-    // row sum over both halves (both warps of the pair reach this barrier on every path)
-    xsum[half][r] = l;
-    xok[0][half][r] = ok ? 1 : 0;
-    pair_sync();
-    const float lt = xsum[0][r] + xsum[1][r];
-    ok = xok[0][0][r] && xok[0][1][r];
-    if (ok && wait(o_final, 0, 48)) {
-      fence_after();
-      const float inv = lt > 0.f ? 1.f / lt : 0.f;
-      __nv_bfloat16* dst = a.out + ((int64_t)(qs + t) * a.nq + h * G + g) * 128 + c0;
-      const bool valid = t < q_len;
-#pragma unroll 1
-      for (int c = 0; c < 64; c += 32) {
-        uint32_t o[32];
-        tmem_ld32(lane_base + O_COL + c0 + c, o);
-        tmem_ld_wait();
-        if (valid) {
-          float f[32];
-#pragma unroll
-          for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(o[e]) * inv;
-#pragma unroll
-          for (int e = 0; e < 32; e += 8) *reinterpret_cast<uint4*>(dst + c + e) = f32_to_bf16x8(f + e);
-        }
-      }
+      g += it.n_tiles;
+      ++n_it;
     }
     fence_before();
   }
@@ -1485,7 +1566,13 @@ static cudaError_t launch_attn_prefill_tc(const AttnLaunch& L, int max_q_len, in
   cudaError_t e = smem_opt_in(done, attn_prefill_tc_kernel, prefill_tc_smem());
   if (e != cudaSuccess) return e;
   const int TQ = pf::TQ_ROWS / G;
-  dim3 grid((max_q_len + TQ - 1) / TQ, L.nkv, L.num_seqs);
+  a.qtiles = (max_q_len + TQ - 1) / TQ;
+  a.num_seqs = L.num_seqs;
+  const int items = a.qtiles * L.nkv * L.num_seqs;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  dim3 grid(items < sms ? items : sms);  // persistent: one CTA per SM (shared memory and TMEM allow one)
   launch_pdl(attn_prefill_tc_kernel, grid, dim3(pf::THREADS), prefill_tc_smem(), stream, qm, km, vm, a);
   NVB_LAUNCH_CHECK();
   return cudaSuccess;

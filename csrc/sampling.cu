@@ -8,6 +8,8 @@
 // The noise for (row, global column) comes from a counter-based hash of (seed, step,
 // row, column) (SplitMix64 finaliser, Steele et al. 2014), so every TP rank draws the
 // same noise for the same column and the whole sampler is CUDA-graph safe.
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -355,7 +357,7 @@ __global__ void __launch_bounds__(1024) sample_rows_kernel(const T* __restrict__
                                                            const float* __restrict__ top_p,
                                                            const int64_t* __restrict__ seed_step,
                                                            int* __restrict__ out_tok, float* __restrict__ out_val,
-                                                           SampleX X) {
+                                                           int rows, SampleX X) {
   pdl_wait();
   pdl_trigger();
   __shared__ float hist[SAMPLE_NB + 1];
@@ -364,19 +366,21 @@ __global__ void __launch_bounds__(1024) sample_rows_kernel(const T* __restrict__
   __shared__ uint32_t s_epoch;
   __shared__ bool s_ok;
   __shared__ float s_cut;
-  const int row = blockIdx.x;
+  const uint64_t seed = (uint64_t)seed_step[0], step = (uint64_t)seed_step[1];
+  const bool multi = X.world > 1;
+  if (threadIdx.x == 0) s_epoch = multi ? sx_ld_acquire(X.ctrl) + 1 : 0u;
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  bool ok = true;  // false after a failed exchange: later rows are sampled from this shard alone
+  // CTA b samples rows b, b + grid, ...: the same rows in the same order on every rank, so with
+  // every CTA resident each exchange finds its peer CTA running
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
   const float t = temps[row];
   const bool greedy = !(t > 0.f);
   const float inv_t = greedy ? 1.f : 1.f / t;
   const float p = top_p ? top_p[row] : 1.f;
   const bool use_p = !greedy && p < 1.f;
-  const uint64_t seed = (uint64_t)seed_step[0], step = (uint64_t)seed_step[1];
   const T* lr = logits + (int64_t)row * ld;
-  const bool multi = X.world > 1;
-  if (threadIdx.x == 0) s_epoch = multi ? sx_ld_acquire(X.ctrl) + 1 : 0u;
-  __syncthreads();
-  const uint32_t epoch = s_epoch;
-  bool ok = true;
   float cut_d = INFINITY, M = 0.f;
   if (use_p) {
     float m = -INFINITY;
@@ -529,14 +533,16 @@ __global__ void __launch_bounds__(1024) sample_rows_kernel(const T* __restrict__
     const int tok = __float_as_int(sval[1]);
     out_tok[row] = tok < 0 ? 0 : tok;
     if (out_val) out_val[row] = sval[0];
-    if (multi) {
-      // the last CTA of this rank advances the call number (every CTA read it at its start)
-      uint32_t prev;
-      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(X.ctrl + 1) : "memory");
-      if (prev == gridDim.x - 1) {
-        X.ctrl[1] = 0;
-        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(X.ctrl), "r"(epoch) : "memory");
-      }
+  }
+  __syncthreads();  // the next row rewrites the shared buffers
+  }
+  if (multi && threadIdx.x == 0) {
+    // the last CTA of this rank advances the call number (every CTA read it at its start)
+    uint32_t prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(X.ctrl + 1) : "memory");
+    if (prev == gridDim.x - 1) {
+      X.ctrl[1] = 0;
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(X.ctrl), "r"(epoch) : "memory");
     }
   }
 }
@@ -544,15 +550,22 @@ __global__ void __launch_bounds__(1024) sample_rows_kernel(const T* __restrict__
 }  // namespace
 
 int sample_rows_capacity() {
+  static std::atomic<int> cached[64];  // per device; 0 = not yet computed
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64) {
+    const int c = cached[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
   int n = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, sample_rows_kernel<__nv_bfloat16>, 1024, 0) != cudaSuccess ||
       n <= 0) {
     cudaGetLastError();
     n = 1;
   }
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
+  int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (dev >= 0 && dev < 64) cached[dev].store(n * sms, std::memory_order_relaxed);
   return n * sms;
 }
 
@@ -560,20 +573,22 @@ cudaError_t launch_sample_rows(const void* logits, int logits_is_bf16, int64_t l
                                const float* temps, const float* top_p, const int64_t* seed_step, int* out_tok,
                                float* out_val, const SampleX& X, cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
+  int grid = rows;
   if (X.world > 1) {
-    // every CTA waits for the same row on the other ranks: all of them must be resident
-    if (X.world > 8 || X.rank < 0 || X.rank >= X.world || rows > X.rows_cap || !X.ctrl ||
-        rows > sample_rows_capacity())
-      return cudaErrorInvalidValue;
+    if (X.world > 8 || X.rank < 0 || X.rank >= X.world || rows > X.rows_cap || !X.ctrl) return cudaErrorInvalidValue;
     for (int p = 0; p < X.world; ++p)
       if (!X.x[p] || !X.f[p]) return cudaErrorInvalidValue;
+    // every CTA waits for its rows on the other ranks: all of them must be resident
+    const int cap = sample_rows_capacity();
+    if (grid > cap) grid = cap;
   }
   if (logits_is_bf16)
-    launch_pdl(sample_rows_kernel<__nv_bfloat16>, dim3(rows), dim3(1024), 0, stream,
-               static_cast<const __nv_bfloat16*>(logits), ld, V, col_offset, temps, top_p, seed_step, out_tok, out_val, X);
+    launch_pdl(sample_rows_kernel<__nv_bfloat16>, dim3(grid), dim3(1024), 0, stream,
+               static_cast<const __nv_bfloat16*>(logits), ld, V, col_offset, temps, top_p, seed_step, out_tok, out_val,
+               rows, X);
   else
-    launch_pdl(sample_rows_kernel<float>, dim3(rows), dim3(1024), 0, stream, static_cast<const float*>(logits), ld, V,
-               col_offset, temps, top_p, seed_step, out_tok, out_val, X);
+    launch_pdl(sample_rows_kernel<float>, dim3(grid), dim3(1024), 0, stream, static_cast<const float*>(logits), ld, V,
+               col_offset, temps, top_p, seed_step, out_tok, out_val, rows, X);
   NVB_LAUNCH_CHECK();
   return cudaSuccess;
 }

@@ -39,7 +39,7 @@ class TPComm:
         self.ops = None
         self.launches = 0
         # GEMM -> reduce-scatter path for decode-sized steps (fused backend only)
-        self.rs_enabled = bool(getattr(config, "fused_reduce_scatter", True)) if config is not None else True
+        self.rs_enabled = bool(getattr(config, "fused_reduce_scatter", False)) if config is not None else False
 
     def bind(self, runner):
         self.runner = runner

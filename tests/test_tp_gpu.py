@@ -39,7 +39,15 @@ def _score(llm, seq):
     from nanovllm_self_b200.sampling_params import SamplingParams
     r = llm.model_runner
     s = Sequence(10 ** 6, seq, SamplingParams(temperature=0, max_tokens=1), r.block_size)
-    r.block_manager.allocate(s)
+    # every position is computed here: no block may come from the prefix cache (the generate
+    # call before left this sequence's prefix blocks in it)
+    bm = r.block_manager
+    saved, bm.enable_prefix_cache = bm.enable_prefix_cache, False
+    try:
+        bm.allocate(s)
+    finally:
+        bm.enable_prefix_cache = saved
+    assert s.num_cached_tokens == 0
     s.num_new_tokens = len(s.token_ids) - s.num_cached_tokens
     pk = r._pack([s])
     ids, pos, ctx, _, _ = r._to_device(pk)
@@ -56,7 +64,12 @@ def _score(llm, seq):
 
 
 def _kw(backend):
-    return dict(max_model_len=2048, max_num_seqs=16, num_blocks=64, cuda_graph_max_bs=16, comm_backend=backend)
+    """``fused``: one-shot / two-shot all-reduce kernels; ``fused_rs``: decode-sized steps take the
+    GEMM -> reduce-scatter path; ``nccl``: the NCCL baseline."""
+    kw = dict(max_model_len=2048, max_num_seqs=16, num_blocks=64, cuda_graph_max_bs=16)
+    if backend == "fused_rs":
+        return dict(kw, comm_backend="fused", fused_reduce_scatter=True)
+    return dict(kw, comm_backend=backend)
 
 
 def _worker(rank, world, port, out_path, backend):
@@ -96,13 +109,14 @@ def test_tp2_fused_matches_nccl_and_tp1(tmp_path):
     from nanovllm_self_b200.engine.sequence import Sequence
     from nanovllm_self_b200.sampling_params import SamplingParams
     res = {}
-    for backend in ("fused", "nccl"):
+    for backend in ("fused", "fused_rs", "nccl"):
         path = str(tmp_path / f"{backend}.pt")
         mp.spawn(_worker, args=(2, _free_port(), path, backend), nprocs=2, join=True)
         res[backend] = torch.load(path)
-    assert res["fused"]["err"] == 0
+    assert res["fused"]["err"] == 0 and res["fused_rs"]["err"] == 0
     lf, ln = res["fused"]["logits"], res["nccl"]["logits"]
     assert torch.nn.functional.cosine_similarity(lf, ln, dim=0).item() > 0.999
+    assert torch.nn.functional.cosine_similarity(res["fused_rs"]["logits"], ln, dim=0).item() > 0.999
     llm = LLM("qwen3-0.6b", device="cuda:0", **_kw("nccl"))
     r = llm.model_runner
     s = Sequence(0, _prompts()[1], SamplingParams(temperature=0, max_tokens=1), r.block_size)
@@ -113,8 +127,9 @@ def test_tp2_fused_matches_nccl_and_tp1(tmp_path):
     with torch.inference_mode():
         l1 = r.model.forward(ids, pos, ctx, r.kv_layers, r.kv_scale_layers)[0].float().cpu()
     assert torch.nn.functional.cosine_similarity(lf, l1, dim=0).item() > 0.995
-    _check_greedy_margin(res["fused"], res["nccl"], "out")
-    _check_greedy_margin(res["fused"], res["nccl"], "short")
+    for fused in ("fused", "fused_rs"):
+        _check_greedy_margin(res[fused], res["nccl"], "out")
+        _check_greedy_margin(res[fused], res["nccl"], "short")
 
 
 def _check_greedy_margin(a, b, key):
@@ -227,15 +242,18 @@ def _sample_worker(rank, world, port, out_path):
     tp = init_tensor_parallel(world, "cuda")
     dev = tp.device
     ops = CudaOps()
-    symm = SymmetricWorkspace(tp, rows=64, hidden=256, timeout_s=5.0, sample_rows=64)
-    V, rows = 151936, 48
+    # 48 rows, and more rows than CTAs that can be resident at once (each CTA then loops)
+    cap = int(ops.C.sample_rows_capacity())
+    big = cap + 20
+    symm = SymmetricWorkspace(tp, rows=64, hidden=256, timeout_s=5.0, sample_rows=big)
+    V = 151936
     per = (V + world - 1) // world
-    g = torch.Generator().manual_seed(4)
-    logits = (torch.randn(rows, V, generator=g) * 3).to(dev)
-    temps = torch.tensor([0.0, 1.0, 0.7, 1.3] * (rows // 4), device=dev)
-    top_p = torch.tensor([1.0, 0.9, 0.5, 1.0] * (rows // 4), device=dev)
     res = {}
-    for s in range(3):
+    for s, rows in enumerate((48, 48, 48, big)):
+        g = torch.Generator().manual_seed(4 + s)
+        logits = (torch.randn(rows, V, generator=g) * 3).to(dev)
+        temps = torch.tensor([0.0, 1.0, 0.7, 1.3], device=dev).repeat((rows + 3) // 4)[:rows].contiguous()
+        top_p = torch.tensor([1.0, 0.9, 0.5, 1.0], device=dev).repeat((rows + 3) // 4)[:rows].contiguous()
         step = torch.tensor([3, s], dtype=torch.int64, device=dev)
         shard = logits[:, rank * per:min(V, (rank + 1) * per)].contiguous()
         tok_tp = symm.sample_rows(shard, temps, top_p, step, rank * per, ops)
@@ -243,6 +261,7 @@ def _sample_worker(rank, world, port, out_path):
         ops.C.sample_rows(logits, 0, temps, top_p, step, tok_one, None)
         torch.cuda.synchronize()
         res[s] = (tok_tp.cpu(), tok_one.cpu())
+        del logits, shard
     err = ops.C.sample_error(False)
     dist.barrier()
     if rank == 0:
