@@ -548,6 +548,61 @@ cudaError_t launch_kv_push(const void* src_pool, void* dst_pool, const int* src_
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------ push completion flags
+// The sender raises a 32-bit sequence number in a flag word that lives in the receiver's
+// exported allocation once its push kernels (earlier in the same stream) have completed; the
+// receiver's stream waits for that number before the pushed blocks are read.
+__device__ int g_push_error = 0;
+
+__global__ void push_signal_kernel(uint32_t* flag, uint32_t epoch) {
+  // the push kernels before this one in the stream have completed; make their peer stores
+  // visible system-wide before the flag
+  fence_acq_rel_sys();
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(epoch) : "memory");
+}
+
+// status (optional): 1 when the flag arrived, 2 when the wait gave up
+__global__ void push_wait_kernel(const uint32_t* flag, uint32_t epoch, uint64_t timeout_ns, int* status) {
+  const uint64_t t0 = comm_timer();
+  for (;;) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (reached(v, epoch)) {
+      if (status) *status = 1;
+      return;
+    }
+    if (comm_timer() - t0 > timeout_ns) {
+      atomicCAS(&g_push_error, 0, 210);  // the sender never signalled: the blocks are not usable
+      if (status) *status = 2;
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
+cudaError_t launch_push_signal(uint32_t* flag, uint32_t epoch, cudaStream_t stream) {
+  if (!flag || ((uintptr_t)flag & 3)) return cudaErrorInvalidValue;
+  push_signal_kernel<<<1, 1, 0, stream>>>(flag, epoch);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_push_wait(const uint32_t* flag, uint32_t epoch, uint64_t timeout_ns, int* status,
+                             cudaStream_t stream) {
+  if (!flag || ((uintptr_t)flag & 3)) return cudaErrorInvalidValue;
+  push_wait_kernel<<<1, 1, 0, stream>>>(flag, epoch, timeout_ns ? timeout_ns : COMM_WAIT_NS, status);
+  return cudaGetLastError();
+}
+
+int push_error_code(int reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_push_error, sizeof(int));
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_push_error, &z, sizeof(int));
+  }
+  return v;
+}
+
 int comm_error_code(int reset) {
   int v = 0;
   cudaMemcpyFromSymbol(&v, g_comm_error, sizeof(int));

@@ -68,6 +68,15 @@ int comm_error_code(int reset);
 cudaError_t launch_kv_push(const void* src_pool, void* dst_pool, const int* src_ids, const int* dst_ids, int n,
                            int planes, int nb_src, int nb_dst, int64_t block_bytes, cudaStream_t stream);
 
+// Push completion: after the pushes of one handoff, raise `flag` (a word of the receiver's
+// exported allocation) to `epoch`; the receiver's stream waits (bounded; error word 210 on
+// expiry, read with push_error_code) until the flag has reached `epoch`.
+constexpr int PUSH_FLAG_SLOTS = 256;  // one word per sending worker
+cudaError_t launch_push_signal(uint32_t* flag, uint32_t epoch, cudaStream_t stream);
+cudaError_t launch_push_wait(const uint32_t* flag, uint32_t epoch, uint64_t timeout_ns, int* status,
+                             cudaStream_t stream);
+int push_error_code(int reset);
+
 cudaError_t symm_alloc(size_t bytes, void** ptr, void* handle_out);  // handle_out: 64 bytes
 cudaError_t symm_open(const void* handle, void** ptr);
 cudaError_t symm_close(void* peer_ptr);

@@ -112,6 +112,29 @@ void kv_push(const at::Tensor& pool, const at::Tensor& src_ids, const at::Tensor
         "kv_push");
 }
 
+// Raise a peer's push flag (raw pointer into its exported allocation) to `epoch`, in stream
+// order after the pushes launched before.
+void kv_push_signal(int64_t flag_ptr, int64_t epoch) {
+  check(nvb::launch_push_signal(reinterpret_cast<uint32_t*>(flag_ptr), (uint32_t)epoch,
+                                at::cuda::getCurrentCUDAStream().stream()),
+        "kv_push_signal");
+}
+
+// Make the current stream wait until this device's push flag word reaches `epoch`; `status`
+// (int32, optional) receives 1 on arrival, 2 when the bounded wait gave up.
+void kv_push_wait(int64_t flag_ptr, int64_t epoch, int64_t timeout_ns, const c10::optional<at::Tensor>& status) {
+  int* st = nullptr;
+  if (status.has_value()) {
+    TORCH_CHECK(status->is_cuda() && status->scalar_type() == at::kInt && status->numel() >= 1, "status int32");
+    st = status->data_ptr<int>();
+  }
+  check(nvb::launch_push_wait(reinterpret_cast<const uint32_t*>(flag_ptr), (uint32_t)epoch, (uint64_t)timeout_ns, st,
+                              at::cuda::getCurrentCUDAStream().stream()),
+        "kv_push_wait");
+}
+
+int64_t push_error(bool reset) { return nvb::push_error_code(reset ? 1 : 0); }
+
 }  // namespace
 
 void register_comm(pybind11::module& m) {
@@ -130,6 +153,11 @@ void register_comm(pybind11::module& m) {
         pybind11::arg("has_residual"), pybind11::arg("eps"), pybind11::arg("ctas"), pybind11::arg("timeout_ns") = 0);
   m.def("comm_error", &comm_error, pybind11::arg("reset") = false);
   m.def("kv_push", &kv_push);
+  m.def("kv_push_signal", &kv_push_signal);
+  m.def("kv_push_wait", &kv_push_wait, pybind11::arg("flag_ptr"), pybind11::arg("epoch"),
+        pybind11::arg("timeout_ns") = 0, pybind11::arg("status") = pybind11::none());
+  m.def("push_error", &push_error, pybind11::arg("reset") = false);
+  m.attr("PUSH_FLAG_SLOTS") = (int64_t)nvb::PUSH_FLAG_SLOTS;
   m.attr("COMM_FLAG_BYTES") = (int64_t)nvb::COMM_FLAG_BYTES;
   m.attr("COMM_MAX_CTAS") = (int64_t)nvb::COMM_MAX_CTAS;
   m.attr("COMM_RS_MAX_ROWS") = (int64_t)nvb::COMM_RS_MAX_ROWS;

@@ -141,22 +141,29 @@ class ModelRunner:
         self._kv_ipc = None
         scale_shape = (2, m.num_layers, self.num_blocks, m.num_kv_heads)
         self._scale_off = 0
+        self._flag_off = 0
+        self.push_flags = None
         if c.kv_pool_ipc and self.is_cuda:
-            # one IPC allocation: the pool, then (fp8) its per-block scales at a 256-byte offset,
-            # so a peer's push kernel reaches both through one handle
+            # one IPC allocation: the pool, then (fp8) its per-block scales, then the push
+            # completion flags (one 32-bit word per sending worker), each at a 256-byte offset,
+            # so a peer's push kernels and its completion signal reach all of it through one handle
             from ..ops._ext import load
             from ..parallel.symm import _DevPtr
             C = load()
             nbytes = int(np.prod(shape)) * torch.empty(0, dtype=c.kv_cache_dtype).element_size()
             self._scale_off = (nbytes + 255) // 256 * 256
-            total = self._scale_off + (int(np.prod(scale_shape)) * 4 if c.kv_cache_quant_mode == "fp8" else 0)
+            scale_end = self._scale_off + (int(np.prod(scale_shape)) * 4 if c.kv_cache_quant_mode == "fp8" else 0)
+            self._flag_off = (scale_end + 255) // 256 * 256
+            total = self._flag_off + int(C.PUSH_FLAG_SLOTS) * 4
             ptr, handle = C.symm_alloc(total)
             self._kv_ipc = (C, ptr, handle)
             raw = torch.as_tensor(_DevPtr(ptr, total), device=self.device)
             self.kv_cache = raw[:nbytes].view(c.kv_cache_dtype).view(shape)
             if c.kv_cache_quant_mode == "fp8":
-                self.kv_scale_cache = raw[self._scale_off:total].view(torch.float32).view(scale_shape)
+                self.kv_scale_cache = raw[self._scale_off:scale_end].view(torch.float32).view(scale_shape)
                 self.kv_scale_cache.fill_(1.0)
+            self.push_flags = raw[self._flag_off:total].view(torch.int32)
+            self.push_flags.zero_()
         else:
             self.kv_cache = torch.zeros(shape, dtype=c.kv_cache_dtype, device=self.device)
         if not (c.kv_pool_ipc and self.is_cuda and c.kv_cache_quant_mode == "fp8"):
@@ -184,6 +191,22 @@ class ModelRunner:
     def kv_scale_offset(self) -> int:
         """Byte offset of the fp8 scales inside the exported allocation (0: no scales)."""
         return self._scale_off if self.kv_scale_cache is not None and self._kv_ipc is not None else 0
+
+    @property
+    def push_flag_offset(self) -> int:
+        """Byte offset of the push completion flags inside the exported allocation (0: none)."""
+        return self._flag_off if self._kv_ipc is not None else 0
+
+    def wait_push(self, slot: int, epoch: int, timeout_s: float = 10.0) -> torch.Tensor:
+        """Make this runner's stream wait until sender `slot` has signalled push `epoch`.
+
+        Bounded: on expiry the stream goes on.  Returns a device int32 status, 1 once the flag
+        arrived and 2 if the wait gave up (the pushed blocks are then not usable)."""
+        C = self._kv_ipc[0]
+        flag = self.push_flags[slot]
+        status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        C.kv_push_wait(int(flag.data_ptr()), int(epoch), int(timeout_s * 1e9), status)
+        return status
 
     def _alloc_staging(self):
         c = self.config

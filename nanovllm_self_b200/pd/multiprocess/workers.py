@@ -221,7 +221,19 @@ class PrefillWorker:
             C = load()
             raw = bytes.fromhex(info["handle"])
             ptr = C.symm_open(raw[:64])
-            self.peer_pools[key] = (ptr, info, int.from_bytes(raw[64:72], "little"))
+            offset = int.from_bytes(raw[64:72], "little")
+            flag_ptr, epoch = 0, 0
+            if info.get("flag_offset"):
+                # this worker's completion word in the decode pool's allocation; the sequence
+                # continues from the word's current value (a restarted sender never reuses an
+                # epoch the receiver already saw)
+                slot = self.args.global_rank % int(C.PUSH_FLAG_SLOTS)
+                flag_ptr = int(ptr) + int(info["flag_offset"]) + 4 * slot
+                from ...parallel.symm import _DevPtr
+                word = torch.as_tensor(_DevPtr(flag_ptr, 4), device=self.runner.device).view(torch.int32)
+                epoch = int(word.cpu().item()) & 0xFFFFFFFF
+                info = dict(info, slot=slot)
+            self.peer_pools[key] = [ptr, info, offset, flag_ptr, epoch]
         return self.peer_pools[key]
 
     def _push(self, payload, dwd: WorkDir, base: str) -> None:
@@ -229,7 +241,8 @@ class PrefillWorker:
         if not dwd.wait_for(f"{base}.recv_ready", self.args.handshake_timeout_s):
             raise TimeoutError("decode worker did not answer recv_ready")
         dst = dwd.read_json(f"{base}.recv_ready")["dst_block_ids"]
-        ptr, info, offset = self._peer_pool(dwd)
+        peer = self._peer_pool(dwd)
+        ptr, info, offset, flag_ptr = peer[0], peer[1], peer[2], peer[3]
         if list(info["shape"][:2]) != list(self.runner.kv_cache.shape[:2]) or \
                 list(info["shape"][3:]) != list(self.runner.kv_cache.shape[3:]) or info["dtype"] != str(self.runner.kv_cache.dtype):
             raise ValueError("decode KV pool layout differs from the prefill pool")
@@ -243,9 +256,17 @@ class PrefillWorker:
             if not info.get("scale_offset"):
                 raise ValueError("fp8 KV needs the decode pool's scales in the exported allocation")
             C.kv_push(r.kv_scale_cache, src, dsti, int(ptr) + int(info["scale_offset"]), int(info["num_blocks"]))
-        if r.is_cuda:
+        done = {"time": time.time()}
+        if flag_ptr:
+            # device completion: the flag rises in stream order after the copies, and the decode
+            # stream waits for it, so no host synchronisation sits between the push and decode
+            # (later prefill kernels that reuse the source blocks run after the push in this stream)
+            peer[4] = (peer[4] + 1) & 0xFFFFFFFF
+            C.kv_push_signal(flag_ptr, peer[4])
+            done.update(slot=info["slot"], epoch=peer[4])
+        elif r.is_cuda:
             torch.cuda.synchronize(r.device)
-        dwd.write_json(rank_name(f"{base}.push_done", self.tp), {"time": time.time()})
+        dwd.write_json(rank_name(f"{base}.push_done", self.tp), done)
 
     # ------------------------------------------------------------- requests
     def finalize_pending_sends(self, block: bool = False) -> None:
@@ -412,6 +433,7 @@ class DecodeWorker:
         self.engine = DecodeEngine(cfg, None, self.runner, self.connector)
         self.pending_recvs = {}   # base -> (state, payload)
         self.pending_push = {}    # base -> (payload, seq blocks, t0)
+        self.push_status = {}     # base -> device status of the push completion wait
         self.active_bases = {}    # request_id -> (base, start time, restore_s)
         self.seen = set()
         if args.backend == "ipc_push":
@@ -426,7 +448,8 @@ class DecodeWorker:
         handle = r.export_kv_pool()
         self.wd.write_json(rank_name("kv_pool.json", self.tp), {
             "handle": handle.hex(), "num_blocks": r.num_blocks, "dtype": str(r.kv_cache.dtype),
-            "shape": list(r.kv_cache.shape), "scale_offset": r.kv_scale_offset})
+            "shape": list(r.kv_cache.shape), "scale_offset": r.kv_scale_offset,
+            "flag_offset": r.push_flag_offset})
 
     def state(self) -> dict:
         return {"role": "decode", "busy": bool(self.engine.scheduler.running), "active": len(self.engine.active),
@@ -435,6 +458,16 @@ class DecodeWorker:
 
     def _finish(self, req) -> None:
         base, t_start, restore_s = self.active_bases.pop(req.request_id)
+        status = self.push_status.pop(base, None)
+        if status is not None:
+            # every rank of the group finishes the same requests in the same order (lockstep
+            # steps), so this agreement is a group collective like the step's own
+            ok = self.ctl.all_ok(int(status.item()) == 1)
+            if not ok:
+                if self.ctl.leader:
+                    _error(self.wd, base, "decode",
+                           RuntimeError("the KV push never signalled completion (device wait timed out)"))
+                return
         if not self.ctl.leader:
             return
         seq = req.seq
@@ -478,6 +511,11 @@ class DecodeWorker:
 
     def _restore_pushed(self, base: str) -> None:
         payload, blocks, t0 = self.pending_push.pop(base)
+        done = self.wd.read_json(self._push_done_name(base, self.tp.rank))
+        if "epoch" in done and self.runner.push_flags is not None:
+            # the stream (and so every decode step of this request) waits for the device flag
+            self.push_status[base] = self.runner.wait_push(int(done["slot"]), int(done["epoch"]),
+                                                           self.args.handshake_timeout_s)
         seq = self.engine._new_sequence(payload)
         seq.block_table = blocks
         self.engine._restore_block_manager_meta(seq)
@@ -572,6 +610,7 @@ class DecodeWorker:
                     _error(self.wd, base, "decode", err or RuntimeError("a peer rank of the decode group failed"))
                 self.engine.abort_by_request_id(rid)
                 self.active_bases.pop(rid, None)
+                self.push_status.pop(base, None)
         for req in list(self.engine.finished_active):
             self._finish(req)
         self.engine.finished_active.clear()
