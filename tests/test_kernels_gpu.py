@@ -74,8 +74,11 @@ def _kv_setup(nb, nkv, bs, dtype, seed=0):
 
 @pytest.mark.parametrize("kv_dtype", [torch.bfloat16, torch.float8_e4m3fn])
 @pytest.mark.parametrize("bs", [16, 256])
-def test_qkv_post(ops, kv_dtype, bs):
-    nq, nkv, T = 8, 2, 40
+@pytest.mark.parametrize("nq,nkv", [(8, 2), (32, 8), (5, 1)])
+def test_qkv_post(ops, kv_dtype, bs, nq, nkv):
+    # (32, 8): Qwen3-8B heads, a warp's 16 heads straddle the K / V boundary; (5, 1): the two
+    # halves of a warp take a query head and a key head in the same pass
+    T = 40
     nb = 16
     kc, vc, ks, vs, g = _kv_setup(nb, nkv, bs, kv_dtype)
     qkv = torch.randn(T, (nq + 2 * nkv) * 128, device=DEV, generator=g).bfloat16()
