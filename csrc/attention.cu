@@ -1156,7 +1156,9 @@ __device__ __forceinline__ constexpr uint32_t o_col(int s) { return s ? 384u : 2
 
 }  // namespace pf
 
-__global__ void __maxnreg__(200)
+// 320 threads: one SM sub-partition holds three of the ten warps, so a thread gets at most 168
+// of the sub-partition's 16 K registers (the launch bound lets ptxas plan for that)
+__global__ void __launch_bounds__(pf::THREADS, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                            const __grid_constant__ CUtensorMap vmap, pf::Args a) {
   // Persistent: one CTA per SM walks the (query tile, KV head, sequence) items round-robin,

@@ -1390,7 +1390,8 @@ cudaError_t run_dec(const DecCfg& d, const void* x, int64_t ldx, const void* w, 
 struct SkParams {
   int m, n, k;
   int np;            // MMA N (tokens per tile, multiple of 16)
-  int mw;            // 128-row weight sub-tiles per CTA (1 or 2)
+  int mrows;         // MMA M: weight rows per sub-tile (128, or 64: twice the CTAs without split-K)
+  int mw;            // weight sub-tiles per CTA (1 or 2; 1 when mrows = 64)
   int splits, kb_per_split, num_kb, stages;
   int act;           // 1: SiLU-and-mul epilogue (gate/up rows interleaved in groups of 16)
   int blocked;       // 1: W stored as [n / 128][k / 64][128][64] (every TMA box one contiguous 16 KB)
@@ -1437,7 +1438,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
                        SkParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int W_BYTES = p.mw * BM * BK * 2;
+  const int MR = p.mrows;
+  const int W_BYTES = p.mw * MR * BK * 2;
   const int X_BYTES = p.np * BK * 2;
   const int STAGE = W_BYTES + X_BYTES;  // multiple of 2 KB: every operand tile stays 1024-aligned
   const int S = p.stages;
@@ -1458,7 +1460,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
   const int tq = blockIdx.x / p.splits;
   const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
   const int nkb = kb1 > kb0 ? kb1 - kb0 : 0;
-  const int wrow0 = tq * p.mw * BM;  // first weight row (output feature) of this tile
+  const int wrow0 = tq * p.mw * MR;  // first weight row (output feature) of this tile
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -1492,8 +1494,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
       mbar_arrive_expect_tx(full(i), (uint32_t)STAGE);
       for (int w = 0; w < p.mw; ++w) {
         int wx, wy;
-        sk_wcoord(p, wrow0 + w * BM, kb, wx, wy);
-        tma_load_2d(smem_u32(smem + i * STAGE + w * BM * BK * 2), &map_w, full(i), wx, wy);
+        sk_wcoord(p, wrow0 + w * MR, kb, wx, wy);
+        tma_load_2d(smem_u32(smem + i * STAGE + w * MR * BK * 2), &map_w, full(i), wx, wy);
       }
     }
     if (tr) tr[1] = globaltimer();
@@ -1511,8 +1513,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
       mbar_arrive_expect_tx(full(s), (uint32_t)STAGE);
       for (int w = 0; w < p.mw; ++w) {
         int wx, wy;
-        sk_wcoord(p, wrow0 + w * BM, kb, wx, wy);
-        tma_load_2d(smem_u32(smem + s * STAGE + w * BM * BK * 2), &map_w, full(s), wx, wy);
+        sk_wcoord(p, wrow0 + w * MR, kb, wx, wy);
+        tma_load_2d(smem_u32(smem + s * STAGE + w * MR * BK * 2), &map_w, full(s), wx, wy);
       }
       tma_load_2d(smem_u32(smem + s * STAGE + W_BYTES), &map_x, full(s), kb * BK, 0);
     }
@@ -1532,7 +1534,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
 #pragma unroll
       for (int k = 0; k < BK / 16; ++k)
         for (int w = 0; w < p.mw; ++w)
-          tc_mma(tmem_base + w * p.np, sdesc(st + w * BM * BK * 2) + 2 * k, xd + 2 * k, p.idesc,
+          tc_mma(tmem_base + w * p.np, sdesc(st + w * MR * BK * 2) + 2 * k, xd + 2 * k, p.idesc,
                  (i > 0 || k > 0) ? 1u : 0u);
       tc_commit(empty(s));
     }
@@ -1547,22 +1549,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
   }
   pdl_wait();  // C (or a peer's receive slot) may still be read by the previous kernel
   float* xp0 = reinterpret_cast<float*>(smem);  // export [sub-tile][token][SK_XLD] over the idle ring
-  const int fpr = ((BM / p.splits + 7) / 8) * 8;  // features per CTA in the reduction (multiple of 8)
-  const int f0 = split * fpr, f1 = min(BM, f0 + fpr);
+  const int fpr = ((MR / p.splits + 7) / 8) * 8;  // features per CTA in the reduction (multiple of 8)
+  const int f0 = split * fpr, f1 = min(MR, f0 + fpr);
   // every sub-tile's export at once when the ring holds them all (one pair of cluster barriers),
   // otherwise one sub-tile at a time
   const int per_pass = (int64_t)p.mw * p.np * SK_XLD * 4 <= (int64_t)S * STAGE ? p.mw : 1;
   for (int w0 = 0; w0 < p.mw; w0 += per_pass) {
     if (warp >= 2 && acc_ok) {
       const int q4 = warp & 3;
-      const int r = q4 * 32 + lane;  // feature row of this thread inside a sub-tile
+      // feature row of this thread inside a sub-tile: M = 128 fills every TMEM lane; M = 64 puts
+      // rows 16 q .. 16 q + 15 in lanes 32 q .. 32 q + 15 of each warp's quarter
+      const int r = MR == BM ? q4 * 32 + lane : q4 * 16 + lane;
+      const bool live = MR == BM || lane < 16;
       for (int w = w0; w < w0 + per_pass; ++w) {
         float* xp = xp0 + (w - w0) * p.np * SK_XLD;
         for (int c0 = 0; c0 < p.np; c0 += 16) {
           uint32_t v[16];
           tmem_ld16(tmem_base + ((uint32_t)(q4 * 32) << 16) + w * p.np + c0, v);
+          if (live) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) xp[(c0 + e) * SK_XLD + r] = __uint_as_float(v[e]);
+            for (int e = 0; e < 16; ++e) xp[(c0 + e) * SK_XLD + r] = __uint_as_float(v[e]);
+          }
         }
       }
     }
@@ -1571,7 +1578,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
     if (tr && threadIdx.x == 0 && w0 == 0) tr[4] = globaltimer();
     for (int w = w0; w < w0 + per_pass; ++w) {
       const uint32_t xbase = smem_u32(xp0 + (w - w0) * p.np * SK_XLD);
-      const int fbase = wrow0 + w * BM;  // output feature of row 0 of this sub-tile
+      const int fbase = wrow0 + w * MR;  // output feature of row 0 of this sub-tile
       if (p.act) {
         // outputs: 16 per 32 rows (rows 32g..32g+15 gates, +16 the ups); items = 8 outputs
         const int g0 = f0 / 32, g1 = (f1 + 31) / 32;
@@ -1655,10 +1662,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
 
 struct SkCfg {
   int np, mw, splits, kb_per_split, stages, smem, tiles;
+  int mrows = BM;  // weight rows per MMA (128 or 64)
 };
 
-int sk_smem(int np, int mw, int stages) {
-  const int stage = mw * BM * BK * 2 + np * BK * 2;
+int sk_smem(int np, int mw, int stages, int mrows = BM) {
+  const int stage = mw * mrows * BK * 2 + np * BK * 2;
   const int ring = stages * stage;
   const int exportb = np * SK_XLD * 4;
   return 1024 + (ring > exportb ? ring : exportb) + 8 * (2 * stages + 4);
@@ -1711,10 +1719,12 @@ std::vector<SkCfg> sk_candidates(int m, int n, int k, int act) {
   const int np = ((m + 15) / 16) * 16;
   const int num_kb = k / BK;
   std::vector<std::pair<double, SkCfg>> scored;
-  for (int mw = 1; mw <= 2; ++mw) {
+  for (int shape = 0; shape < 3; ++shape) {
+    // (rows per MMA, sub-tiles): (64, 1) doubles the CTAs of (128, 1) without splitting K
+    const int mr = shape == 0 ? 64 : BM, mw = shape == 2 ? 2 : 1;
     if (mw * np > 512) continue;
-    const int tiles = (n + mw * BM - 1) / (mw * BM);
-    const int stage = mw * BM * BK * 2 + np * BK * 2;
+    const int tiles = (n + mw * mr - 1) / (mw * mr);
+    const int stage = mw * mr * BK * 2 + np * BK * 2;
     int prev = 0;
     for (int sp = 1; sp <= 8; ++sp) {
       const int kbs = (num_kb + sp - 1) / sp;
@@ -1728,13 +1738,13 @@ std::vector<SkCfg> sk_candidates(int m, int n, int k, int act) {
         if (st > 12) st = 12;
         if (st > kbs) st = kbs < 2 ? 2 : kbs;
         if (st < 2) continue;
-        const int smem = sk_smem(np, mw, st);
+        const int smem = sk_smem(np, mw, st, mr);
         if (smem > budget) continue;
         const int cap = sk_capacity(s_eff, smem);
         const int units = tiles * s_eff;
         if (units > cap) continue;  // one wave only
-        SkCfg c{np, mw, s_eff, kbs, st, smem, tiles};
-        const double bytes = (double)kbs * stage + (s_eff > 1 ? 2.0 * np * BM * 4 * mw : 0.0);
+        SkCfg c{np, mw, s_eff, kbs, st, smem, tiles, mr};
+        const double bytes = (double)kbs * stage + (s_eff > 1 ? 2.0 * np * mr * 4 * mw : 0.0);
         scored.push_back({bytes, c});
       }
     }
@@ -1748,15 +1758,17 @@ cudaError_t run_skinny(const SkCfg& d, const void* x, int64_t ldx, const void* w
                        int m, int n, int k, cudaStream_t stream, int act = 0, const GemmRsEpilogue* rs = nullptr,
                        int blocked = 0, uint64_t* trace = nullptr) {
   if (m > 256 || k % BK || (act && n % 32) || ldc % 8) return cudaErrorInvalidValue;
-  if (blocked && n % BM) return cudaErrorInvalidValue;
+  if (blocked && (n % BM || d.mrows != BM)) return cudaErrorInvalidValue;
+  if (d.mrows != BM && (d.mrows != 64 || d.mw != 1)) return cudaErrorInvalidValue;
   CUtensorMap mx, mw;
-  const bool wok = blocked ? make_map(&mw, w, n * (k / BK), BK, BK, BM) : make_map(&mw, w, n, k, ldw, BM);
+  const bool wok = blocked ? make_map(&mw, w, n * (k / BK), BK, BK, BM) : make_map(&mw, w, n, k, ldw, d.mrows);
   if (!make_map(&mx, x, m, k, ldx, d.np) || !wok) return cudaErrorInvalidValue;
   SkParams p;
   p.m = m;
   p.n = n;
   p.k = k;
   p.np = d.np;
+  p.mrows = d.mrows;
   p.mw = d.mw;
   p.splits = d.splits;
   p.kb_per_split = d.kb_per_split;
@@ -1765,8 +1777,8 @@ cudaError_t run_skinny(const SkCfg& d, const void* x, int64_t ldx, const void* w
   p.act = act;
   p.blocked = blocked;
   p.trace = trace;
-  // D f32, A bf16 (weights), B bf16 (tokens), N = np, M = 128
-  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(d.np >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  // D f32, A bf16 (weights), B bf16 (tokens), N = np, M = mrows
+  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(d.np >> 3) << 17) | ((uint32_t)(d.mrows >> 4) << 24);
   p.c = static_cast<__nv_bfloat16*>(c);
   p.ldc = ldc;
   if (rs) {
@@ -1857,14 +1869,27 @@ static std::vector<GemmPlan> dec_plans_for_tuning(int m, int n, int k, int each,
 }
 
 // Skinny-kernel plans (dec = 2): mt = tokens per tile (MMA N), bn = weight rows per CTA.
+// The `each` cheapest by bytes per CTA come first; the 64-row single-split shapes (more CTAs, no
+// split-K reduction at all) are appended when the cheapest do not already include them.
 static std::vector<GemmPlan> skinny_plans_for_tuning(int m, int n, int k, int each, int act) {
   std::vector<GemmPlan> out;
-  for (const auto& d : sk_candidates(m, n, k, act)) {
-    if ((int)out.size() >= each) break;
+  const auto cands = sk_candidates(m, n, k, act);
+  std::vector<SkCfg> pick;
+  for (const auto& d : cands) {
+    if ((int)pick.size() >= each) break;
+    pick.push_back(d);
+  }
+  for (const auto& d : cands) {
+    if (d.mrows != 64 || d.splits != 1) continue;
+    bool dup = false;
+    for (const auto& q : pick) dup |= q.mrows == d.mrows && q.splits == d.splits && q.stages == d.stages;
+    if (!dup) pick.push_back(d);
+  }
+  for (const auto& d : pick) {
     GemmPlan pl{};
     pl.dec = 2;
     pl.mt = d.np;
-    pl.bn = d.mw * BM;
+    pl.bn = d.mw * d.mrows;
     pl.splits = d.splits;
     pl.kb_per_split = d.kb_per_split;
     pl.num_kb = k / BK;
@@ -1887,7 +1912,9 @@ bool gemm_skinny_plan(int m, int n, int k, int rank, int act, GemmPlan* plan) {
 }
 
 static SkCfg plan_to_skinny(const GemmPlan& pl) {
-  return SkCfg{pl.mt, pl.bn / BM, pl.splits, pl.kb_per_split, pl.stages, pl.smem, pl.tiles};
+  // bn = weight rows per CTA: 64 (one 64-row MMA), 128 or 256 (one or two 128-row MMAs)
+  const int mrows = pl.bn < BM ? 64 : BM;
+  return SkCfg{pl.mt, pl.bn / mrows, pl.splits, pl.kb_per_split, pl.stages, pl.smem, pl.tiles, mrows};
 }
 
 cudaError_t gemm_skinny_run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n,

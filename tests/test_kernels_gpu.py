@@ -270,7 +270,8 @@ def test_gemm_tcgen05(ops, m, n, k):
     (100, 4096, 4096, 0), (200, 2304, 1024, 0), (256, 6144, 4096, 0), (5, 3072, 1024, 1), (129, 768, 4096, 1),
 ])
 def test_gemm_skinny_configs(ops, m, n, k, act):
-    """The skinny kernel (weights on the MMA's M side, cluster split-K) over its top configurations."""
+    """The skinny kernel (weights on the MMA's M side, 128- or 64-row MMAs, cluster split-K) over its
+    top configurations."""
     from nanovllm_self_b200.ops.torch_ref import interleave_gate_up
     g = torch.Generator(device=DEV).manual_seed(m * 13 + n)
     x = (torch.randn(m, k, device=DEV, generator=g) * 0.5).bfloat16()
@@ -280,15 +281,17 @@ def test_gemm_skinny_configs(ops, m, n, k, act):
         gate, up = ref[:, : n // 2], ref[:, n // 2:]
         ref = torch.nn.functional.silu(gate) * up
         w = interleave_gate_up(w[: n // 2], w[n // 2:]).contiguous()
-    ran = 0
-    for rank in range(4):
+    rows = []  # weight rows per CTA of every configuration run (64: the 64-row MMA shape)
+    for rank in range(12):
         out = torch.full((m, n // 2 if act else n), float("nan"), device=DEV, dtype=torch.bfloat16)
         cfg = ops.C.linear_skinny(x, w, out, rank, act)
         if not cfg:
             break
-        ran += 1
+        rows.append(cfg[1])
         _close(out, ref, 0.01 * math.sqrt(k / 1024) * 0.5, 0.02)
-    assert ran > 0
+    assert rows
+    if n // 64 <= 148:  # the 64-row single-split shape fits one wave: it is among the plans
+        assert 64 in rows, rows
     assert ops.C.gemm_error(True) == 0
 
 
