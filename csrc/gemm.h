@@ -19,7 +19,9 @@ struct GemmPlan {
   int mt;            // 128-row sub-tiles of the token operand per output tile (1 or 2)
   int dec;           // 1: decode kernel (all m <= 256 tokens per CTA, runtime bn, cluster split-K);
                      // 2: skinny kernel (weights on the MMA's M side, mt = tokens per tile,
-                     //    bn = weight rows per CTA, cluster split-K)
+                     //    bn = weight rows per CTA, cluster split-K);
+                     // 3: CTA-pair kernel (128 < m <= 256 tokens, M = 256 over two CTAs,
+                     //    bn = weight rows per pair, tiles = pairs)
   int stages, smem;  // decode kernel: weight-ring depth and dynamic shared memory
   int a_stages;      // decode kernel: activation-ring depth
 };
@@ -40,6 +42,10 @@ bool gemm_skinny_plan(int m, int n, int k, int rank, int act, GemmPlan* plan);
 cudaError_t gemm_skinny_run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n,
                             int k, const GemmPlan& plan, int act, int blocked, cudaStream_t stream,
                             uint64_t* trace = nullptr);
+
+// The rank-th CTA-pair kernel configuration (fewest bytes per CTA first) for C[m, n],
+// 128 < m <= 256; false if there is none.  Run it with gemm_bf16.
+bool gemm_pair_plan(int m, int n, int k, int rank, int act, GemmPlan* plan);
 
 // Decode kernel with an explicit (bn, splits, activation-ring depth) configuration.
 cudaError_t gemm_dec_explicit(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m,

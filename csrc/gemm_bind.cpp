@@ -67,7 +67,7 @@ std::vector<int64_t> linear_tuned(const at::Tensor& x, const at::Tensor& w, at::
   // splits >= 100: decode kernel with splits - 100 K slices; >= 200: skinny kernel with
   // splits - 200 K slices (bn = weight rows per CTA)
   return {pl.swap, pl.bn, pl.tiles_p, pl.tiles_q,
-          pl.dec == 2 ? 200 + pl.splits : pl.dec ? 100 + pl.splits : pl.streamk ? -pl.mt : pl.splits, pl.grid};
+          pl.dec == 3 ? 300 : pl.dec == 2 ? 200 + pl.splits : pl.dec ? 100 + pl.splits : pl.streamk ? -pl.mt : pl.splits, pl.grid};
 }
 
 std::vector<int64_t> plan(int64_t m, int64_t n, int64_t k, int64_t force_swap, int64_t force_bn,
@@ -175,6 +175,24 @@ std::vector<int64_t> linear_skinny(const at::Tensor& x, const at::Tensor& w, at:
   return {pl.mt, pl.bn, pl.splits, pl.stages};
 }
 
+// CTA-pair kernel (M = 256 tokens over two CTAs) with the rank-th configuration; returns
+// (weight rows per pair, stages, pairs), empty if none.
+std::vector<int64_t> linear_pair(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, int64_t rank, int64_t act) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16, "bf16 required");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "unit inner stride required");
+  const int m = (int)x.size(0), k = (int)x.size(1), n = (int)w.size(0);
+  TORCH_CHECK(w.size(1) == k && out.size(0) == m && out.size(1) == (act ? n / 2 : n), "shape mismatch");
+  nvb::GemmPlan pl{};
+  if (!nvb::gemm_pair_plan(m, n, k, (int)rank, (int)act, &pl)) return {};
+  at::cuda::CUDAGuard g(x.device());
+  cudaError_t e = nvb::gemm_bf16(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0),
+                                 m, n, k, pl, nullptr, nullptr, at::cuda::getCurrentCUDAStream().stream(), (int)act);
+  TORCH_CHECK(e == cudaSuccess, "gemm_bf16 (pair) failed: ", cudaGetErrorString(e));
+  return {pl.bn, pl.stages, pl.tiles};
+}
+
 int64_t error_code(bool reset) { return nvb::gemm_error_code(reset ? 1 : 0); }
 
 }  // namespace
@@ -195,6 +213,8 @@ void register_gemm(pybind11::module& m) {
   m.def("linear_skinny", &linear_skinny, "skinny tcgen05 GEMM (weights on M) with a ranked configuration",
         pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("rank"), pybind11::arg("act") = 0,
         pybind11::arg("blocked") = 0, pybind11::arg("trace") = c10::nullopt);
+  m.def("linear_pair", &linear_pair, "CTA-pair tcgen05 GEMM (M = 256 tokens over two CTAs), ranked configuration",
+        pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("rank"), pybind11::arg("act") = 0);
   m.def("linear_rs", &linear_rs, "tcgen05 decode GEMM whose rows are stored at their owner rank (reduce-scatter)");
   m.def("gemm_error", &error_code, pybind11::arg("reset") = false);
   m.def("gemm_set_deterministic", [](bool on) { nvb::gemm_set_deterministic(on ? 1 : 0); });

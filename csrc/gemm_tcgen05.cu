@@ -1374,6 +1374,299 @@ cudaError_t run_dec(const DecCfg& d, const void* x, int64_t ldx, const void* w, 
 }
 
 
+// ------------------------------------------------------------------ CTA-pair decode GEMM
+// C[m, n] = X[m, k] W[n, k]^T for 128 < m <= 256 tokens with one M = 256 MMA per k-step over a
+// pair of CTAs (tcgen05.mma.cta_group::2, issued by the even CTA of a 2-CTA cluster).  Each CTA
+// of the pair stages its own 128 token rows and HALF of the pair's BN weight rows, so per pair a
+// weight byte and an activation row each cross into shared memory once: against one CTA that
+// holds all 256 tokens, a CTA moves half the activation bytes, which is what bounds the decode
+// kernel at these sizes (the activations come from L2 once per CTA).  Both CTAs' TMA loads
+// complete on the even CTA's stage barrier (unicast loads; the barrier address is mapped into the
+// even CTA with mapa); the even CTA's commits arrive on both CTAs' barriers (commit multicast).
+// Each CTA's TMEM holds the fp32 accumulator of its 128 tokens x BN outputs; warps 2-5 of both
+// CTAs store it (optionally SiLU-and-mul of interleaved gate/up rows).  Warps: 0 TMA, 1 TMEM +
+// MMA (even CTA), 2-5 epilogue.
+struct PairParams {
+  int m, n, k, bn, num_kb, stages, act;
+  uint32_t idesc;
+  __nv_bfloat16* c;
+  int64_t ldc;
+};
+
+__device__ __forceinline__ uint32_t cluster_map(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+
+// Unicast TMA load into this CTA's shared memory that completes on a barrier of either CTA of
+// the pair (here always the even CTA's).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive on the barrier at this shared-memory offset in every CTA of `mask` once the pair's
+// MMAs issued so far have completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                     PairParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int A_BYTES = BM * BK * 2;  // this CTA's 128 token rows of one k-block
+  const int HB = p.bn / 2;              // weight rows staged by this CTA
+  const int W_BYTES = HB * BK * 2;
+  const int STAGE = A_BYTES + W_BYTES;  // HB % 8 == 0: every tile stays 1024-aligned
+  const int S = p.stages;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * STAGE);
+  // bars: full[S] (used in the even CTA), empty[S], tfull, final
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * S + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 3);
+  const uint32_t bar0 = smem_u32(bars);
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto empty = [&](int s) { return bar0 + 8u * (S + s); };
+  const uint32_t tfull = bar0 + 8u * (2 * S);
+  const uint32_t final_bar = tfull + 8u;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t tmem_cols = 32;
+  while (tmem_cols < (uint32_t)p.bn) tmem_cols <<= 1;
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {  // the same warp in both CTAs: one allocation that spans the pair
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any load or commit reaches them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------------ producer (both CTAs)
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_x)) : "memory");
+    const int wrow = pair * p.bn + (int)rank * HB;
+    const int pre = p.num_kb < S ? p.num_kb : S;
+    for (int i = 0; i < pre; ++i) {  // weights first: independent of the previous kernel
+      if (leader) mbar_arrive_expect_tx(full(i), 2u * (uint32_t)STAGE);
+      tma_load_2d_pair(smem_u32(smem + i * STAGE + A_BYTES), &map_w, cluster_map(full(i), 0), i * BK, wrow);
+    }
+    pdl_wait();  // the activations come from the previous kernel
+    for (int i = 0; i < pre; ++i)
+      tma_load_2d_pair(smem_u32(smem + i * STAGE), &map_x, cluster_map(full(i), 0), i * BK, (int)rank * BM);
+    bool ok = true;
+    int it = pre;
+    for (int i = pre; i < p.num_kb; ++i, ++it) {
+      const int s = i % S;
+      if (!mbar_wait(empty(s), ((i / S) & 1) ^ 1, abort_flag, 30)) {
+        ok = false;
+        break;
+      }
+      if (leader) mbar_arrive_expect_tx(full(s), 2u * (uint32_t)STAGE);
+      const uint32_t fb = cluster_map(full(s), 0);
+      tma_load_2d_pair(smem_u32(smem + s * STAGE + A_BYTES), &map_w, fb, i * BK, wrow);
+      tma_load_2d_pair(smem_u32(smem + s * STAGE), &map_x, fb, i * BK, (int)rank * BM);
+    }
+    if (!ok && leader) {
+      const int n = it < S ? it : S;
+      for (int j = it - n; j < it; ++j) mbar_drain(full(j % S), (j / S) & 1);
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ------------------------------------------------------------------ MMA issuer (even CTA)
+    for (int i = 0; i < p.num_kb; ++i) {
+      const int s = i % S;
+      if (!mbar_wait(full(s), (i / S) & 1, abort_flag, 31)) break;
+      tc_fence_after();
+      const uint32_t st = smem_u32(smem + s * STAGE);
+      const uint64_t ad = sdesc(st), wd = sdesc(st + A_BYTES);
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k) tc_mma_pair(tmem_base, ad + 2 * k, wd + 2 * k, p.idesc, (i > 0 || k > 0) ? 1u : 0u);
+      tc_commit_pair(empty(s), 0x3);
+    }
+    tc_commit_pair(tfull, 0x3);
+    tc_commit_pair(final_bar, 0x1);
+    mbar_drain(final_bar, 0);  // every MMA of the pair has completed before this thread goes on
+  }
+  __syncwarp();
+  if (warp >= 2) {
+    const bool acc_ok = (warp == 2 ? mbar_wait : mbar_wait_sleep)(tfull, 0, abort_flag, 32);
+    tc_fence_after();
+    pdl_wait();  // C may still be read by the previous kernel in the stream
+    const int q4 = warp & 3;
+    const int row = (int)rank * BM + q4 * 32 + lane;  // token of this thread
+#pragma unroll 1
+    for (int c0 = 0; c0 < p.bn; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld32(tmem_base + ((uint32_t)(q4 * 32) << 16) + c0, r);
+      const int qj = pair * p.bn + c0;
+      const int valid = min(32, p.n - qj);
+      if (!acc_ok || row >= p.m || valid <= 0) continue;
+      float f[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+      __nv_bfloat16* crow = p.c + (int64_t)row * p.ldc;
+      if (p.act) {  // bn % 32 == 0 and n % 32 == 0 in this mode
+        act_silu_store(crow + qj / 2, f);
+        continue;
+      }
+      __nv_bfloat16* dst = crow + qj;
+      if (valid == 32) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = f32_to_bf16x8(f + j);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < valid) dst[j] = __float2bfloat16(f[j]);
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  cluster_sync_all();  // the pair's MMAs, loads and commits are all done before TMEM is freed
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
+  }
+}
+
+struct PairCfg {
+  int bn, stages, smem, pairs;
+};
+
+static int pair_smem(int bn, int stages) { return 1024 + stages * (BM * BK * 2 + bn / 2 * BK * 2) + 8 * (2 * stages + 6); }
+
+static int pair_capacity(int smem) {
+  // CTAs of 2-CTA clusters with this shared memory that can be resident at once (cached)
+  static std::map<int, int> cache;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  auto it = cache.find(smem);
+  if (it != cache.end()) return it->second;
+  cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM_MAX);
+  cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 64, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = num_sms() / 2;
+  }
+  cache[smem] = 2 * n;
+  return 2 * n;
+}
+
+// Pair-kernel configurations for 128 < m <= 256: BN (the pair's weight rows, a multiple of 32) and
+// the ring depth, fewest (waves x bytes per CTA) first.
+std::vector<PairCfg> pair_candidates(int m, int n, int k, int act) {
+  std::vector<PairCfg> out;
+  if (m <= BM || m > 2 * BM || k % BK || (act && n % 32)) return out;
+  const int num_kb = k / BK;
+  std::vector<std::pair<double, PairCfg>> scored;
+  for (int bn = 32; bn <= 256; bn += 32) {
+    const int pairs = (n + bn - 1) / bn;
+    const int stage = BM * BK * 2 + bn / 2 * BK * 2;
+    for (int two = 0; two < 2; ++two) {  // one or two CTAs per SM
+      const int budget = two ? DEC_SMEM_MAX / 2 - 2048 : DEC_SMEM_MAX;
+      int st = (budget - 1024 - 8 * 32) / stage;
+      if (st > 10) st = 10;
+      if (st > num_kb) st = num_kb;
+      if (st < 2) continue;
+      const int smem = pair_smem(bn, st);
+      if (smem > budget) continue;
+      const int cap = pair_capacity(smem);
+      const int waves = (2 * pairs + cap - 1) / (cap > 0 ? cap : 1);
+      if (waves > 4) continue;
+      scored.push_back({(double)waves * num_kb * stage, PairCfg{bn, st, smem, pairs}});
+    }
+  }
+  std::sort(scored.begin(), scored.end(), [](const auto& a, const auto& b) { return a.first < b.first; });
+  for (auto& s : scored) out.push_back(s.second);
+  return out;
+}
+
+cudaError_t run_pair(const PairCfg& d, const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc,
+                     int m, int n, int k, cudaStream_t stream, int act = 0) {
+  if (m <= BM || m > 2 * BM || k % BK || d.bn % 32 || d.bn > 256 || (act && n % 32) || ldc % 8 || !c ||
+      ((uintptr_t)c & 15))
+    return cudaErrorInvalidValue;
+  CUtensorMap mx, mw;
+  if (!make_map(&mx, x, m, k, ldx, BM) || !make_map(&mw, w, n, k, ldw, d.bn / 2)) return cudaErrorInvalidValue;
+  PairParams p;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.bn = d.bn;
+  p.num_kb = k / BK;
+  p.stages = d.stages;
+  p.act = act;
+  // D f32, A bf16 (tokens), B bf16 (weights), N = bn, M = 256 over the pair
+  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(d.bn >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+  p.c = static_cast<__nv_bfloat16*>(c);
+  p.ldc = ldc;
+  static std::atomic<uint64_t> done{0};
+  cudaError_t e = smem_opt_in(done, gemm_pair_kernel, DEC_SMEM_MAX);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * d.pairs, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = d.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel, mx, mw, p);
+}
+
 // ------------------------------------------------------------------ skinny decode GEMM
 // Decode-sized GEMM with the WEIGHTS on the MMA's M side (tensor-core "swap" form):
 // D[i, j] = sum_k W[i, k] X[j, k] on tiles of MW x 128 weight rows (one M = 128 MMA each)
@@ -1923,6 +2216,36 @@ cudaError_t gemm_skinny_run(const void* x, int64_t ldx, const void* w, int64_t l
   return run_skinny(plan_to_skinny(plan), x, ldx, w, ldw, c, ldc, m, n, k, stream, act, nullptr, blocked, trace);
 }
 
+// Pair-kernel plans (dec = 3): bn = weight rows per pair, tiles = pairs.
+static std::vector<GemmPlan> pair_plans_for_tuning(int m, int n, int k, int each, int act) {
+  std::vector<GemmPlan> out;
+  for (const auto& d : pair_candidates(m, n, k, act)) {
+    if ((int)out.size() >= each) break;
+    GemmPlan pl{};
+    pl.dec = 3;
+    pl.mt = 2;
+    pl.bn = d.bn;
+    pl.splits = 1;
+    pl.kb_per_split = k / BK;
+    pl.num_kb = k / BK;
+    pl.stages = d.stages;
+    pl.smem = d.smem;
+    pl.tiles = d.pairs;
+    pl.tiles_p = 1;
+    pl.tiles_q = d.pairs;
+    pl.grid = 2 * d.pairs;
+    out.push_back(pl);
+  }
+  return out;
+}
+
+bool gemm_pair_plan(int m, int n, int k, int rank, int act, GemmPlan* plan) {
+  const auto v = pair_plans_for_tuning(m, n, k, rank + 1, act);
+  if (rank < 0 || rank >= (int)v.size()) return false;
+  *plan = v[rank];
+  return true;
+}
+
 static GemmPlan dec_to_plan(const DecCfg& d, int k) {
   GemmPlan pl{};
   pl.dec = 1;
@@ -2029,6 +2352,7 @@ cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, vo
     if (m > pl.mt || k % BK) return cudaErrorInvalidValue;
     return run_skinny(plan_to_skinny(pl), x, ldx, w, ldw, c, ldc, m, n, k, stream, act);
   }
+  if (pl.dec == 3) return run_pair(PairCfg{pl.bn, pl.stages, pl.smem, pl.tiles}, x, ldx, w, ldw, c, ldc, m, n, k, stream, act);
   if (pl.dec) {
     if (m > pl.mt * BM || k % BK) return cudaErrorInvalidValue;
     DecCfg d{pl.mt, pl.bn, pl.splits, pl.kb_per_split, pl.stages, pl.a_stages, pl.smem, pl.tiles, 0.0};
@@ -2174,6 +2498,7 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
   if (m <= 2 * BM && k % BK == 0) {
     for (const auto& d : dec_plans_for_tuning(m, n, k, 6, act)) cands.push_back(d);
     for (const auto& d : skinny_plans_for_tuning(m, n, k, 6, act)) cands.push_back(d);
+    for (const auto& d : pair_plans_for_tuning(m, n, k, 6, act)) cands.push_back(d);
   }
   if (ws && counters) {
     for (int bn : {256, 128}) {

@@ -272,7 +272,7 @@ def gemm_chain(ms=(1, 16, 64, 128, 256), calls: int = 24) -> None:
 
 def gemm_one(m: int, n: int, k: int, impl: str, mode: str, iters: int = 20) -> None:
     """One GEMM shape with one implementation: ``tuned`` (the autotuner's pick), ``cublas``
-    (torch.matmul), ``skinny:R`` / ``dec:R`` (the R-th configuration of that kernel's model)."""
+    (torch.matmul), ``skinny:R`` / ``dec:R`` / ``pair:R`` (the R-th configuration of that kernel's model)."""
     ops = CudaOps()
     x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
     w = (torch.randn(n, k, device="cuda") * 0.02).to(torch.bfloat16)
@@ -296,6 +296,9 @@ def gemm_one(m: int, n: int, k: int, impl: str, mode: str, iters: int = 20) -> N
     elif kind == "dec":
         def fn():
             info["cfg"] = ops.C.linear_dec(x, w, out, int(rank or 0), 0)
+    elif kind == "pair":  # CTA-pair kernel (128 < m <= 256)
+        def fn():
+            info["cfg"] = ops.C.linear_pair(x, w, out, int(rank or 0), 0)
     else:
         raise ValueError(impl)
     fn()
@@ -329,7 +332,7 @@ def main(argv=None):
     p.add_argument("--m", type=int, default=1)
     p.add_argument("--n", type=int, default=6144)
     p.add_argument("--k", type=int, default=4096)
-    p.add_argument("--impl", default="tuned", help="comma-separated: tuned, cublas, skinny:R, skinnyb:R, dec:R")
+    p.add_argument("--impl", default="tuned", help="comma-separated: tuned, cublas, skinny:R, skinnyb:R, dec:R, pair:R")
     p.add_argument("--ms", default=None, help="comma-separated m values (gemm_one), instead of --m")
     p.add_argument("--mode", choices=("time", "profile"), default="time")
     p.add_argument("--iters", type=int, default=20)

@@ -93,8 +93,12 @@ def decode_sweep(args) -> dict:
         llm.generate([r["prompt_ids"] for r in warm], _sp(warm))
         with _Timed(llm) as t:
             m = llm.generate([r["prompt_ids"] for r in rows], _sp(rows), return_metrics=True)["metrics"]
-        out["points"].append({"batch": bs, "tpot_ms": m["tpot_ms_p50"],
-                              "decode_tok_s": bs / (m["tpot_ms_p50"] / 1e3) if m["tpot_ms_p50"] > 0 else 0.0,
+        # the decode rate at this batch: device time of the decode-only steps that ran the whole
+        # batch (TPOT also counts the prefill steps of later requests that interleave with them)
+        n_full, ms_full = m["decode_steps"].get(bs, [0, 0.0])
+        out["points"].append({"batch": bs, "decode_step_ms": ms_full, "decode_steps_timed": n_full,
+                              "decode_tok_s": bs / (ms_full / 1e3) if ms_full > 0 else 0.0,
+                              "tpot_ms_p50": m["tpot_ms_p50"], "ttft_ms_p50": m["ttft_ms_p50"],
                               "prefix_hit_blocks_timed": t.prefix_hits, "clocks": t.clocks})
     return out
 

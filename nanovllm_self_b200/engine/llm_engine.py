@@ -115,6 +115,8 @@ class LLMEngine:
             seqs = self.scheduler.schedule()
         if not seqs:
             return [], [], 0.0
+        # decode-only step (every sequence adds one token after its prefill): timed per batch size
+        self.last_step_decode = all(s.num_new_tokens == 1 and s.is_prefill_done for s in seqs)
         with tr.phase("run"):
             token_ids, need = self.model_runner.run(seqs)
         dev_ms = self.model_runner.last_dev_ms
@@ -147,6 +149,7 @@ class LLMEngine:
         dev_ms_total = 0.0
         steps = 0
         stalls = 0
+        decode_steps = {}  # batch size -> [decode-only steps, their summed device ms]
         t_start = time.perf_counter()
         with torch.inference_mode():
             while not self.scheduler.is_finished():
@@ -161,6 +164,10 @@ class LLMEngine:
                 stalls = 0
                 dev_ms_total += dev_ms
                 steps += 1
+                if self.last_step_decode:
+                    d = decode_steps.setdefault(len(scheduled), [0, 0.0])
+                    d[0] += 1
+                    d[1] += dev_ms
                 if pbar:
                     pbar.update(sum(s.num_completion_tokens for s in seqs) - prev)
         wall = time.perf_counter() - t_start
@@ -191,6 +198,8 @@ class LLMEngine:
             "ttft_ms_p50": _percentile(ttft, 50), "ttft_ms_p99": _percentile(ttft, 99),
             "tpot_ms_p50": _percentile(tpot, 50), "tpot_ms_p99": _percentile(tpot, 99),
             "num_preemptions": self.scheduler.num_preemptions,
+            # decode-only steps by batch size: {batch: [steps, mean device ms per step]}
+            "decode_steps": {b: [n, ms / n] for b, (n, ms) in sorted(decode_steps.items())},
             "block_usage": self.block_manager.get_block_usage_snapshot(),
         }
         if self.enable_profile:

@@ -295,6 +295,35 @@ def test_gemm_skinny_configs(ops, m, n, k, act):
     assert ops.C.gemm_error(True) == 0
 
 
+@pytest.mark.parametrize("m,n,k,act", [
+    (256, 6144, 4096, 0), (129, 4096, 4096, 0), (200, 24576, 4096, 1), (256, 4096, 12288, 0), (177, 1000, 512, 0),
+])
+def test_gemm_pair_configs(ops, m, n, k, act):
+    """The CTA-pair kernel (M = 256 tokens over two CTAs, cta_group::2) over its top configurations,
+    ragged token counts and a ragged last weight tile included."""
+    from nanovllm_self_b200.ops.torch_ref import interleave_gate_up
+    g = torch.Generator(device=DEV).manual_seed(m * 7 + n)
+    x = (torch.randn(m, k, device=DEV, generator=g) * 0.5).bfloat16()
+    w = (torch.randn(n, k, device=DEV, generator=g) * 0.02).bfloat16()
+    ref = x.float() @ w.float().t()
+    if act:
+        gate, up = ref[:, : n // 2], ref[:, n // 2:]
+        ref = torch.nn.functional.silu(gate) * up
+        w = interleave_gate_up(w[: n // 2], w[n // 2:]).contiguous()
+    ops.C.gemm_error(True)
+    ran = []
+    for rank in range(6):
+        out = torch.full((m, n // 2 if act else n), float("nan"), device=DEV, dtype=torch.bfloat16)
+        cfg = ops.C.linear_pair(x, w, out, rank, act)
+        if not cfg:
+            break
+        torch.cuda.synchronize()
+        assert ops.C.gemm_error(True) == 0, cfg
+        ran.append(cfg)
+        _close(out, ref, 0.01 * math.sqrt(k / 1024) * 0.5, 0.02)
+    assert ran
+
+
 @pytest.mark.parametrize("swap,bn,splits", [(0, 256, 1), (0, 128, 3), (1, 32, 1), (1, 64, 4), (1, 256, 2), (0, 64, 1)])
 def test_gemm_forced_configs(ops, swap, bn, splits):
     m, n, k = 200, 1280, 2048
