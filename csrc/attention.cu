@@ -149,11 +149,6 @@ constexpr uint64_t ATT_WAIT_NS = 2000000000ull;
 
 __device__ int g_attn_error = 0;
 
-__device__ __forceinline__ uint64_t att_timer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
 __device__ __forceinline__ bool att_try(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -165,9 +160,9 @@ __device__ __forceinline__ bool att_try(uint32_t bar, uint32_t parity) {
 }
 __device__ __forceinline__ bool att_wait(uint32_t bar, uint32_t parity, int code) {
   if (att_try(bar, parity)) return true;
-  const uint64_t t0 = att_timer();
+  SpinBudget sb;
   while (!att_try(bar, parity)) {
-    if (att_timer() - t0 > ATT_WAIT_NS) {
+    if (sb.expired(ATT_WAIT_NS)) {
       atomicCAS(&g_attn_error, 0, code);
       return false;
     }
@@ -289,8 +284,8 @@ __global__ void __launch_bounds__(160, 2)
       const int n = issued < DSTAGES ? issued : DSTAGES;
       for (int i = issued - n; i < issued; ++i) {
         const uint32_t full = bar0 + 8u * (i % DSTAGES);
-        const uint64_t tw = att_timer();
-        while (!att_try(full, (i / DSTAGES) & 1) && att_timer() - tw < ATT_WAIT_NS) {
+        SpinBudget sb;
+        while (!att_try(full, (i / DSTAGES) & 1) && !sb.expired(ATT_WAIT_NS)) {
         }
       }
       (void)ok;
@@ -617,8 +612,8 @@ __global__ void __launch_bounds__(160, 3)
       const int n = issued < DSTAGES ? issued : DSTAGES;
       for (int i = issued - n; i < issued; ++i) {
         const uint32_t full = bar0 + 8u * (i % DSTAGES);
-        const uint64_t tw = att_timer();
-        while (!att_try(full, (i / DSTAGES) & 1) && att_timer() - tw < ATT_WAIT_NS) {
+        SpinBudget sb;
+        while (!att_try(full, (i / DSTAGES) & 1) && !sb.expired(ATT_WAIT_NS)) {
         }
       }
     }
@@ -1246,10 +1241,10 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
 
   auto wait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
     if (att_try(bar, parity)) return true;
-    const uint64_t tstart = att_timer();
+    SpinBudget sb;
     while (!att_try(bar, parity)) {
       if (*abort_flag) return false;
-      if (att_timer() - tstart > ATT_WAIT_NS) {
+      if (sb.expired(ATT_WAIT_NS)) {
         atomicCAS(&g_attn_error, 0, code);
         *abort_flag = 1;
         return false;
@@ -1260,9 +1255,9 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
   // Exit path: waits for a phase regardless of the abort flag (bounded), so no copy or MMA
   // of this CTA is still writing shared memory or TMEM when the CTA frees them.
   auto settle = [&](uint32_t bar, uint32_t parity) {
-    const uint64_t tstart = att_timer();
+    SpinBudget sb;
     while (!att_try(bar, parity))
-      if (att_timer() - tstart > ATT_WAIT_NS) {
+      if (sb.expired(ATT_WAIT_NS)) {
         atomicCAS(&g_attn_error, 0, 51);
         return;
       }

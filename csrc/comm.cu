@@ -40,11 +40,6 @@ __device__ __forceinline__ uint64_t wait_budget(const CommArgs& a) {
   return a.timeout_ns ? a.timeout_ns : COMM_WAIT_NS;
 }
 
-__device__ __forceinline__ uint64_t comm_timer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
 
 __device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -72,10 +67,10 @@ __device__ __forceinline__ bool reached(uint32_t v, uint32_t e) { return (int32_
 __device__ bool wait_all_flags(uint32_t* const* flags, int rank, int world, size_t flags_off, uint32_t epoch,
                                uint64_t budget_ns, int code) {
   const uint32_t* mine = flags[rank] + flags_off;
-  const uint64_t t0 = comm_timer();
+  SpinBudget sb;
   for (int p = 0; p < world; ++p) {
     while (!reached(ld_relaxed_sys(mine + p), epoch)) {
-      if (comm_timer() - t0 > budget_ns) {
+      if (sb.expired(budget_ns)) {
         atomicCAS(&g_comm_error, 0, code);
         fence_acq_rel_sys();
         return false;
@@ -114,9 +109,9 @@ __device__ bool rank_entry_barrier(const CommArgs& a, size_t flags_off, uint32_t
   }
   // twice CTA 0's budget: when the peers fail to arrive, CTA 0 gives up first, records why
   // (110) and releases this CTA through the go word; 111 means CTA 0 itself never got there
-  const uint64_t t0 = comm_timer();
+  SpinBudget sb;
   while (!reached(ld_acquire_gpu(ctrl + 1), epoch)) {
-    if (comm_timer() - t0 > 2 * wait_budget(a)) {
+    if (sb.expired(2 * wait_budget(a))) {
       atomicCAS(&g_comm_error, 0, 111);
       return false;
     }
@@ -563,7 +558,7 @@ __global__ void push_signal_kernel(uint32_t* flag, uint32_t epoch) {
 
 // status (optional): 1 when the flag arrived, 2 when the wait gave up
 __global__ void push_wait_kernel(const uint32_t* flag, uint32_t epoch, uint64_t timeout_ns, int* status) {
-  const uint64_t t0 = comm_timer();
+  SpinBudget sb;
   for (;;) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
@@ -571,7 +566,7 @@ __global__ void push_wait_kernel(const uint32_t* flag, uint32_t epoch, uint64_t 
       if (status) *status = 1;
       return;
     }
-    if (comm_timer() - t0 > timeout_ns) {
+    if (sb.expired(timeout_ns)) {
       atomicCAS(&g_push_error, 0, 210);  // the sender never signalled: the blocks are not usable
       if (status) *status = 2;
       return;

@@ -30,6 +30,25 @@ __device__ __forceinline__ bool in_range(long long i, long long n, int* word, in
   return true;
 }
 
+// Time bound for a polling loop: call expired() once per failed poll.  %globaltimer is read only
+// on every 64th call (a timer read costs far more than a poll of an mbarrier or a flag, and a
+// read per poll slows the detection of the awaited event); true once more than budget_ns have
+// passed since the first read.
+struct SpinBudget {
+  uint64_t t0 = 0;
+  uint32_t n = 0;
+  __device__ __forceinline__ bool expired(uint64_t budget_ns) {
+    if ((++n & 63u) != 0) return false;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t0 == 0) {
+      t0 = t;
+      return false;
+    }
+    return t - t0 > budget_ns;
+  }
+};
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL_MASK, v, o);

@@ -71,11 +71,11 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 // role of this CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int code) {
   if (mbar_try(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  SpinBudget sb;
   while (true) {
     if (mbar_try(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > WAIT_BUDGET_NS) {
+    if (sb.expired(WAIT_BUDGET_NS)) {
       atomicCAS(&g_gemm_error, 0, code);
       *abort_flag = 1;
       return false;
@@ -88,12 +88,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 // that share their SM sub-partitions.
 __device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, volatile int* abort_flag, int code) {
   if (mbar_try(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  SpinBudget sb;
   while (true) {
-    __nanosleep(512);
+    __nanosleep(128);
     if (mbar_try(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > WAIT_BUDGET_NS) {
+    if (sb.expired(WAIT_BUDGET_NS)) {
       atomicCAS(&g_gemm_error, 0, code);
       *abort_flag = 1;
       return false;
@@ -103,9 +103,9 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, v
 
 // Drain wait used on the error path: short budget, never sets flags.
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer();
+  SpinBudget sb;
   while (!mbar_try(bar, parity)) {
-    if (globaltimer() - t0 > WAIT_BUDGET_NS) return;
+    if (sb.expired(WAIT_BUDGET_NS)) return;
   }
 }
 

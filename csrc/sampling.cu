@@ -221,11 +221,6 @@ __device__ __forceinline__ uint32_t sx_ld_sys(const uint32_t* p) {
 __device__ __forceinline__ void sx_st_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint64_t sx_timer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
 
 __device__ int g_sample_error = 0;
 
@@ -256,11 +251,11 @@ __device__ bool sx_exchange(const SampleX& X, int round, int row, const float* v
     const int64_t fo = ((int64_t)(round - 1) * X.rows_cap + row) * X.world;
     for (int p = 0; p < X.world; ++p) sx_st_sys(X.f[p] + fo + X.rank, epoch);
     const uint32_t* mine = X.f[X.rank] + fo;
-    const uint64_t t0 = sx_timer();
+    SpinBudget sb;
     bool ok = true;
     for (int p = 0; p < X.world && ok; ++p) {
       while ((int32_t)(sx_ld_sys(mine + p) - epoch) < 0) {
-        if (sx_timer() - t0 > X.timeout_ns) {
+        if (sb.expired(X.timeout_ns)) {
           atomicCAS(&g_sample_error, 0, 300 + round);
           ok = false;
           break;
