@@ -38,7 +38,7 @@ bool gemm_dec_plan(int m, int n, int k, int rank, GemmPlan* plan);
 // false if there is none.
 bool gemm_skinny_plan(int m, int n, int k, int rank, int act, GemmPlan* plan);
 // Skinny kernel with W in the blocked layout [n / 128][k / 64][128][64] (blocked = 1) or row-major.
-// trace (optional): 8 uint64 %globaltimer stamps per CTA (see SkParams).
+// trace (optional): 328 uint64 %globaltimer stamps per CTA (see SkParams).
 cudaError_t gemm_skinny_run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n,
                             int k, const GemmPlan& plan, int act, int blocked, cudaStream_t stream,
                             uint64_t* trace = nullptr);

@@ -101,6 +101,13 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, v
   }
 }
 
+// One lane of a converged warp (elect.sync).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile("{\n .reg .pred P;\n elect.sync _|P, 0xffffffff;\n selp.u32 %0, 1, 0, P;\n}\n" : "=r"(pred));
+  return pred != 0;
+}
+
 // Drain wait used on the error path: short budget, never sets flags.
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
   SpinBudget sb;
@@ -786,7 +793,8 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-bool make_map(CUtensorMap* m, const void* base, int rows, int k, int64_t ld_elems, int box_rows) {
+bool make_map(CUtensorMap* m, const void* base, int rows, int k, int64_t ld_elems, int box_rows,
+              CUtensorMapL2promotion promo = CU_TENSOR_MAP_L2_PROMOTION_L2_256B) {
   auto enc = get_encode();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
@@ -794,8 +802,7 @@ bool make_map(CUtensorMap* m, const void* base, int rows, int k, int64_t ld_elem
   cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -1481,14 +1488,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_x)) : "memory");
     const int wrow = pair * p.bn + (int)rank * HB;
+    auto kb_of = [&](int i) { return i; };
     const int pre = p.num_kb < S ? p.num_kb : S;
     for (int i = 0; i < pre; ++i) {  // weights first: independent of the previous kernel
       if (leader) mbar_arrive_expect_tx(full(i), 2u * (uint32_t)STAGE);
-      tma_load_2d_pair(smem_u32(smem + i * STAGE + A_BYTES), &map_w, cluster_map(full(i), 0), i * BK, wrow);
+      tma_load_2d_pair(smem_u32(smem + i * STAGE + A_BYTES), &map_w, cluster_map(full(i), 0), kb_of(i) * BK, wrow);
     }
     pdl_wait();  // the activations come from the previous kernel
     for (int i = 0; i < pre; ++i)
-      tma_load_2d_pair(smem_u32(smem + i * STAGE), &map_x, cluster_map(full(i), 0), i * BK, (int)rank * BM);
+      tma_load_2d_pair(smem_u32(smem + i * STAGE), &map_x, cluster_map(full(i), 0), kb_of(i) * BK, (int)rank * BM);
     bool ok = true;
     int it = pre;
     for (int i = pre; i < p.num_kb; ++i, ++it) {
@@ -1499,28 +1507,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (leader) mbar_arrive_expect_tx(full(s), 2u * (uint32_t)STAGE);
       const uint32_t fb = cluster_map(full(s), 0);
-      tma_load_2d_pair(smem_u32(smem + s * STAGE + A_BYTES), &map_w, fb, i * BK, wrow);
-      tma_load_2d_pair(smem_u32(smem + s * STAGE), &map_x, fb, i * BK, (int)rank * BM);
+      tma_load_2d_pair(smem_u32(smem + s * STAGE + A_BYTES), &map_w, fb, kb_of(i) * BK, wrow);
+      tma_load_2d_pair(smem_u32(smem + s * STAGE), &map_x, fb, kb_of(i) * BK, (int)rank * BM);
     }
     if (!ok && leader) {
       const int n = it < S ? it : S;
       for (int j = it - n; j < it; ++j) mbar_drain(full(j % S), (j / S) & 1);
     }
-  } else if (warp == 1 && lane == 0 && leader) {
+  } else if (warp == 1 && leader) {
     // ------------------------------------------------------------------ MMA issuer (even CTA)
+    // converged warp, one elected lane issues; the TMEM base is broadcast so it is warp-uniform
+    const uint32_t tbase = __shfl_sync(0xffffffffu, tmem_base, 0);
     for (int i = 0; i < p.num_kb; ++i) {
       const int s = i % S;
-      if (!mbar_wait(full(s), (i / S) & 1, abort_flag, 31)) break;
+      int okw = 1;
+      if (lane == 0) okw = mbar_wait(full(s), (i / S) & 1, abort_flag, 31);
+      okw = __shfl_sync(0xffffffffu, okw, 0);
+      if (!okw) break;
       tc_fence_after();
       const uint32_t st = smem_u32(smem + s * STAGE);
       const uint64_t ad = sdesc(st), wd = sdesc(st + A_BYTES);
+      if (elect_one()) {
 #pragma unroll
-      for (int k = 0; k < BK / 16; ++k) tc_mma_pair(tmem_base, ad + 2 * k, wd + 2 * k, p.idesc, (i > 0 || k > 0) ? 1u : 0u);
-      tc_commit_pair(empty(s), 0x3);
+        for (int k = 0; k < BK / 16; ++k) tc_mma_pair(tbase, ad + 2 * k, wd + 2 * k, p.idesc, (i > 0 || k > 0) ? 1u : 0u);
+        tc_commit_pair(empty(s), 0x3);
+      }
+      __syncwarp();
     }
-    tc_commit_pair(tfull, 0x3);
-    tc_commit_pair(final_bar, 0x1);
-    mbar_drain(final_bar, 0);  // every MMA of the pair has completed before this thread goes on
+    if (elect_one()) {
+      tc_commit_pair(tfull, 0x3);
+      tc_commit_pair(final_bar, 0x1);
+      mbar_drain(final_bar, 0);  // every MMA of the pair has completed before this warp goes on
+    }
+    __syncwarp();
   }
   __syncwarp();
   if (warp >= 2) {
@@ -1533,12 +1552,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int c0 = 0; c0 < p.bn; c0 += 32) {
       uint32_t r[32];
       tmem_ld32(tmem_base + ((uint32_t)(q4 * 32) << 16) + c0, r);
-      const int qj = pair * p.bn + c0;
-      const int valid = min(32, p.n - qj);
-      if (!acc_ok || row >= p.m || valid <= 0) continue;
       float f[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+      const int qj = pair * p.bn + c0;
+      const int valid = min(32, p.n - qj);
+      if (!acc_ok || row >= p.m || valid <= 0) continue;
       __nv_bfloat16* crow = p.c + (int64_t)row * p.ldc;
       if (p.act) {  // bn % 32 == 0 and n % 32 == 0 in this mode
         act_silu_store(crow + qj / 2, f);
@@ -1688,13 +1707,19 @@ struct SkParams {
   int splits, kb_per_split, num_kb, stages;
   int act;           // 1: SiLU-and-mul epilogue (gate/up rows interleaved in groups of 16)
   int blocked;       // 1: W stored as [n / 128][k / 64][128][64] (every TMA box one contiguous 16 KB)
-  uint64_t* trace;   // optional: per CTA 8 %globaltimer stamps (start, weights issued, first stage full,
-                     // MMAs done, export done, reduce done, end, unused)
+  uint64_t* trace;   // optional: per CTA SK_TRACE %globaltimer stamps (start, weights issued, first stage
+                     // full, MMAs done, export done, reduce done, end, unused; then per k-block times)
   uint32_t idesc;
   __nv_bfloat16* c;
   int64_t ldc;
   GemmRsEpilogue rs;
 };
+
+// Trace words per CTA: 8 phase stamps, then the issue time of k-blocks S..63 (index 8 + i; the
+// first S are issued before the loop, at stamp 1), the time the MMA thread saw k-blocks 0..63
+// land (index 72 + i), the time it started waiting for them (index 136 + i), the time its MMAs
+// for them were issued (index 200 + i) and the time its commits were issued (index 264 + i).
+constexpr int SK_TRACE = 328;
 
 // TMA coordinates of the weight box (128 rows from `row`, k-block kb).
 __device__ __forceinline__ void sk_wcoord(const SkParams& p, int row, int kb, int& x, int& y) {
@@ -1754,6 +1779,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
   const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
   const int nkb = kb1 > kb0 ? kb1 - kb0 : 0;
   const int wrow0 = tq * p.mw * MR;  // first weight row (output feature) of this tile
+  auto kb_of = [&](int i) { return kb0 + i; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -1774,7 +1800,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_trigger();  // the whole grid is resident (one wave): the next kernel may launch
-  uint64_t* tr = p.trace ? p.trace + (int64_t)blockIdx.x * 8 : nullptr;
+  uint64_t* tr = p.trace ? p.trace + (int64_t)blockIdx.x * SK_TRACE : nullptr;
   if (tr && threadIdx.x == 0) tr[0] = globaltimer();
 
   if (warp == 0 && lane == 0) {
@@ -1783,7 +1809,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_x)) : "memory");
     const int pre = nkb < S ? nkb : S;
     for (int i = 0; i < pre; ++i) {  // weights first: independent of the previous kernel
-      const int kb = kb0 + i;
+      const int kb = kb_of(i);
       mbar_arrive_expect_tx(full(i), (uint32_t)STAGE);
       for (int w = 0; w < p.mw; ++w) {
         int wx, wy;
@@ -1793,7 +1819,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
     }
     if (tr) tr[1] = globaltimer();
     pdl_wait();  // the activations come from the previous kernel
-    for (int i = 0; i < pre; ++i) tma_load_2d(smem_u32(smem + i * STAGE + W_BYTES), &map_x, full(i), (kb0 + i) * BK, 0);
+    for (int i = 0; i < pre; ++i) tma_load_2d(smem_u32(smem + i * STAGE + W_BYTES), &map_x, full(i), kb_of(i) * BK, 0);
     bool ok = true;
     uint32_t it = pre;
     for (int i = pre; i < nkb; ++i, ++it) {
@@ -1802,7 +1828,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
         ok = false;
         break;
       }
-      const int kb = kb0 + i;
+      const int kb = kb_of(i);
+      if (tr && i < 64) tr[8 + i] = globaltimer();
       mbar_arrive_expect_tx(full(s), (uint32_t)STAGE);
       for (int w = 0; w < p.mw; ++w) {
         int wx, wy;
@@ -1815,23 +1842,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
       const uint32_t n = it < (uint32_t)S ? it : (uint32_t)S;
       for (uint32_t j = it - n; j < it; ++j) mbar_drain(full(j % S), (j / S) & 1);
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
+    // The whole warp runs the loop and one elected lane issues (about 8% faster per stage than
+    // a lone lane running it); the TMEM base is broadcast so it is provably warp-uniform.
+    const uint32_t tbase = __shfl_sync(0xffffffffu, tmem_base, 0);
     for (int i = 0; i < nkb; ++i) {
       const int s = i % S;
-      if (!mbar_wait(full(s), (i / S) & 1, abort_flag, 21)) break;
-      if (tr && i == 0) tr[2] = globaltimer();
+      if (tr && lane == 0 && i < 64) tr[136 + i] = globaltimer();
+      int okw = 1;
+      if (lane == 0) okw = mbar_wait(full(s), (i / S) & 1, abort_flag, 21);
+      okw = __shfl_sync(0xffffffffu, okw, 0);
+      if (!okw) break;
+      if (tr && lane == 0 && i == 0) tr[2] = globaltimer();
+      if (tr && lane == 0 && i < 64) tr[72 + i] = globaltimer();
       tc_fence_after();
       const uint32_t st = smem_u32(smem + s * STAGE);
       const uint64_t xd = sdesc(st + W_BYTES);
+      if (elect_one()) {
 #pragma unroll
-      for (int k = 0; k < BK / 16; ++k)
-        for (int w = 0; w < p.mw; ++w)
-          tc_mma(tmem_base + w * p.np, sdesc(st + w * MR * BK * 2) + 2 * k, xd + 2 * k, p.idesc,
-                 (i > 0 || k > 0) ? 1u : 0u);
-      tc_commit(empty(s));
+        for (int k = 0; k < BK / 16; ++k)
+          for (int w = 0; w < p.mw; ++w)
+            tc_mma(tbase + w * p.np, sdesc(st + w * MR * BK * 2) + 2 * k, xd + 2 * k, p.idesc,
+                   (i > 0 || k > 0) ? 1u : 0u);
+        if (tr && i < 64) tr[200 + i] = globaltimer();
+        tc_commit(empty(s));
+        if (tr && i < 64) tr[264 + i] = globaltimer();
+      }
+      __syncwarp();
     }
-    tc_commit(tfull);
+    if (elect_one()) tc_commit(tfull);
   }
   __syncwarp();
   bool acc_ok = true;

@@ -326,9 +326,60 @@ def gemm_one(m: int, n: int, k: int, impl: str, mode: str, iters: int = 20) -> N
                       "plan": ops.last_plan if kind == "tuned" else info.get("cfg")}))
 
 
+def skinny_trace(m: int, n: int, k: int, rank: int) -> None:
+    """In-kernel %globaltimer stamps of one cold launch of the rank-th skinny configuration: per CTA,
+    when each k-block's loads were issued and when the MMA thread saw them land."""
+    ops = CudaOps()
+    x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(n, k, device="cuda") * 0.02).to(torch.bfloat16)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    cfg = ops.C.linear_skinny(x, w, out, rank, 0)  # warm-up
+    tr = torch.zeros(4096 * 328, dtype=torch.int64, device="cuda")
+    flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+    flush.sum()
+    ops.C.linear_skinny(x, w, out, rank, 0, 0, tr)
+    torch.cuda.synchronize()
+    t = tr.view(4096, 328).cpu()
+    live = t[:, 0] > 0
+    t = t[live]
+    t0 = t[:, 0].min()
+    lat, gaps, land, waited, busy, mma, com, tail = [], [], [], [], [], [], [], []
+    for row in t:
+        issue = row[8:72]
+        full = row[72:136]
+        start = row[136:200]
+        after_mma = row[200:264]
+        after_com = row[264:328]
+        for i in range(64):
+            if full[i] > 0 and after_mma[i] > 0 and after_com[i] > 0:
+                mma.append(int(after_mma[i] - full[i]))     # fence + MMA issue (+ one stamp)
+                com.append(int(after_com[i] - after_mma[i]))  # commit issue (+ one stamp)
+            if i < 63 and after_com[i] > 0 and start[i + 1] > 0:
+                tail.append(int(start[i + 1] - after_com[i]))  # loop overhead to the next wait
+        for i in range(64):
+            if issue[i] > 0 and full[i] > 0:
+                lat.append(int(full[i] - issue[i]))
+            if i > 0 and full[i] > 0 and full[i - 1] > 0:
+                land.append(int(full[i] - full[i - 1]))
+                busy.append(int(start[i] - full[i - 1]))  # MMA thread's own work for k-block i - 1
+            if full[i] > 0 and start[i] > 0:
+                waited.append(int(full[i] - start[i]))  # how long it waited for k-block i
+    q = lambda v, p: float(torch.tensor(v, dtype=torch.float64).quantile(p)) / 1e3 if v else None
+    print(json.dumps({"gemm": [m, n, k], "cfg": cfg, "ctas": int(live.sum()),
+                      "first_full_us": q([int(r[2] - t0) for r in t], 0.5),
+                      "mma_done_us_p50": q([int(r[3] - t0) for r in t if r[3] > 0], 0.5),
+                      "end_us_max": q([int(r[6] - t0) for r in t], 1.0),
+                      "issue_to_land_us": {"p10": q(lat, 0.1), "p50": q(lat, 0.5), "p90": q(lat, 0.9)},
+                      "land_to_land_us": {"p10": q(land, 0.1), "p50": q(land, 0.5), "p90": q(land, 0.9)},
+                      "mma_thread_work_us": {"p10": q(busy, 0.1), "p50": q(busy, 0.5), "p90": q(busy, 0.9)},
+                      "mma_thread_wait_us": {"p10": q(waited, 0.1), "p50": q(waited, 0.5), "p90": q(waited, 0.9)},
+                      "mma_issue_us_p50": q(mma, 0.5), "commit_issue_us_p50": q(com, 0.5), "loop_tail_us_p50": q(tail, 0.5)}))
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("case", choices=CASES + ("all", "gemm_sweep", "gemm_one", "gemm_chain"))
+    p.add_argument("case", choices=CASES + ("all", "gemm_sweep", "gemm_one", "gemm_chain", "skinny_trace"))
+    p.add_argument("--rank", type=int, default=0)
     p.add_argument("--m", type=int, default=1)
     p.add_argument("--n", type=int, default=6144)
     p.add_argument("--k", type=int, default=4096)
@@ -342,6 +393,9 @@ def main(argv=None):
         return
     if a.case == "gemm_chain":
         gemm_chain()
+        return
+    if a.case == "skinny_trace":
+        skinny_trace(a.m, a.n, a.k, a.rank)
         return
     if a.case == "gemm_one":
         for impl in a.impl.split(","):
