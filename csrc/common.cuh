@@ -30,6 +30,13 @@ __device__ __forceinline__ bool in_range(long long i, long long n, int* word, in
   return true;
 }
 
+// One lane of a converged warp (elect.sync): the issuing lane of a warp that runs a loop together.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile("{\n .reg .pred P;\n elect.sync _|P, 0xffffffff;\n selp.u32 %0, 1, 0, P;\n}\n" : "=r"(pred));
+  return pred != 0;
+}
+
 // Time bound for a polling loop: call expired() once per failed poll.  %globaltimer is read only
 // on every 64th call (a timer read costs far more than a poll of an mbarrier or a flag, and a
 // read per poll slows the detection of the awaited event); true once more than budget_ns have

@@ -101,13 +101,6 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, v
   }
 }
 
-// One lane of a converged warp (elect.sync).
-__device__ __forceinline__ bool elect_one() {
-  uint32_t pred = 0;
-  asm volatile("{\n .reg .pred P;\n elect.sync _|P, 0xffffffff;\n selp.u32 %0, 1, 0, P;\n}\n" : "=r"(pred));
-  return pred != 0;
-}
-
 // Drain wait used on the error path: short budget, never sets flags.
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
   SpinBudget sb;
