@@ -1330,8 +1330,9 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
         if (j < n) {
           const int gs = g + j, s = gs & 1;
           if (!wait(k_full(s), (gs >> 1) & 1, 42)) { ok = false; break; }
+          // no tcgen05 fence here: both waits are on TMA or tcgen05.commit arrivals, which order the
+          // data this MMA reads and the TMEM it overwrites (the fence is needed after p_ready, below)
           if (gs >= 2 && !wait(s_free(s), ((gs - 2) >> 1) & 1, 43)) { ok = false; break; }
-          fence_after();
           const uint32_t kb = smem_u32(sk + s * TILE);
 #pragma unroll
           for (int k = 0; k < 8; ++k) {

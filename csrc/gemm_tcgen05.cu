@@ -135,6 +135,9 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, i
 
 __device__ __forceinline__ void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
+// tcgen05 fences order tcgen05 operations against thread synchronisation (an mbarrier that other
+// threads arrive on after their own tcgen05 work, or __syncthreads).  The mainloops issue MMAs right
+// after waiting on a TMA-filled stage barrier without one: that wait already orders the staged data.
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -427,7 +430,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          tc_fence_after();
           const uint32_t st = smem_u32(smem + s * STAGE_BYTES);
           const uint64_t qd = sdesc(st + MT * P_BYTES);
 #pragma unroll
@@ -662,7 +664,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int s = it % STAGES;
         const uint32_t round = it / STAGES;
         if (!mbar_wait(full(s), round & 1, abort_flag, 6)) break;
-        tc_fence_after();
         const uint32_t st = smem_u32(smem + s * STAGE_BYTES);
         const uint64_t pd = sdesc(st), qd = sdesc(st + P_BYTES);
 #pragma unroll
@@ -1051,7 +1052,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int sw = i % SW, sa = i % SA;
       if (!mbar_wait(wfull(sw), (i / SW) & 1, abort_flag, 9)) break;
       if (!mbar_wait(afull(sa), (i / SA) & 1, abort_flag, 9)) break;
-      tc_fence_after();
       const uint64_t wd = sdesc(smem_u32(w_ring + sw * W_BYTES));
       const uint32_t ab = smem_u32(a_ring + sa * A_BYTES);
 #pragma unroll
@@ -1517,7 +1517,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0) okw = mbar_wait(full(s), (i / S) & 1, abort_flag, 31);
       okw = __shfl_sync(0xffffffffu, okw, 0);
       if (!okw) break;
-      tc_fence_after();
       const uint32_t st = smem_u32(smem + s * STAGE);
       const uint64_t ad = sdesc(st), wd = sdesc(st + A_BYTES);
       if (elect_one()) {
@@ -1849,7 +1848,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)  // two CTAs per SM when their
       if (!okw) break;
       if (tr && lane == 0 && i == 0) tr[2] = globaltimer();
       if (tr && lane == 0 && i < 64) tr[72 + i] = globaltimer();
-      tc_fence_after();
       const uint32_t st = smem_u32(smem + s * STAGE);
       const uint64_t xd = sdesc(st + W_BYTES);
       if (elect_one()) {
