@@ -215,7 +215,7 @@ int64_t sample_f_words(int64_t world, int64_t rows_cap) { return nvb::sample_f_w
 int64_t sample_error(bool reset) { return nvb::sample_error_code(reset ? 1 : 0); }
 
 // First index-check error recorded by the checked kernels (401: gathered norm row out of range,
-// 402: KV slot beyond the pool), 0 if none.
+// 402: KV slot beyond the pool, 403: a q/k/v stage copy did not arrive in time), 0 if none.
 int64_t bounds_error(bool reset) {
   const int a = nvb::norm_check_code(reset ? 1 : 0);
   const int b = nvb::qkv_check_code(reset ? 1 : 0);

@@ -56,6 +56,30 @@ struct SpinBudget {
   }
 };
 
+// Gumbel-max sampling noise, shared by the sampler kernels and the lm_head GEMM's sampling
+// epilogue so that both draw the same noise for (seed, step, row, global column).
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ float gumbel(uint64_t seed, uint64_t step, int row, int64_t col) {
+  uint64_t h = mix64(seed + 0x9E3779B97F4A7C15ull * (step + 1));
+  h = mix64(h ^ ((uint64_t)row << 40) ^ (uint64_t)col);
+  // 23 random bits: (k + 0.5) / 2^23 is exact in fp32 and lies in [2^-24, 1 - 2^-24], so u < 1 and
+  // the noise is finite (24 bits would round the top value up to u = 1 and give g = +inf,
+  // letting a random column win about once per 2^24 columns)
+  const float u = ((float)(h >> 41) + 0.5f) * (1.0f / 8388608.0f);
+  return -logf(-logf(u));
+}
+
+// Noised score of a logit at temperature 1 / inv_t: l * inv_t + g, rounded once (explicit fma, so
+// every kernel that computes it gets the same bits).
+__device__ __forceinline__ float noised(float l, float inv_t, uint64_t seed, uint64_t step, int row, int64_t col) {
+  return __fmaf_rn(l, inv_t, gumbel(seed, step, row, col));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL_MASK, v, o);

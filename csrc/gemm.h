@@ -51,14 +51,36 @@ bool gemm_pair_plan(int m, int n, int k, int rank, int act, GemmPlan* plan);
 cudaError_t gemm_dec_explicit(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m,
                               int n, int k, int bn, int splits, int a_stages, cudaStream_t stream);
 
+// Sampling epilogue of the lm_head GEMM: the product is not stored; each output value is rounded
+// to bf16, noised (Gumbel-max, for rows whose temperature is > 0) and folded into a per-token key
+// by an atomic max, so that the key of token row i names the sampled column.  keys[m] must be zero
+// before the launch (sample_keys decodes the keys and zeroes them again).
+struct GemmSampleEpilogue {
+  unsigned long long* keys = nullptr;  // [m]
+  const float* temps = nullptr;        // [m] temperature per row (<= 0: greedy)
+  const int64_t* seed_step = nullptr;  // (seed, step) of the noise
+  int64_t col_offset = 0;              // global column of output feature 0 (vocab shard start)
+};
+
 // ws: fp32 split-K scratch (plan.ws_elems); counters: 4 int32 per output tile, all zero
 // before the first launch (the kernel leaves them zero).
 // act = 1: fused SiLU-and-mul epilogue.  W's rows are gate/up interleaved in groups of 16
 // (rows 32j..32j+15 gate features 16j..16j+15, rows 32j+16..32j+31 the matching up
 // features) and C receives silu(gate) * up: [m, n / 2] with row stride ldc.  Needs n % 32
 // == 0, the normal orientation and a tile width that is a multiple of 32.
+// se (optional): the sampling epilogue instead of storing C (persistent-kernel plans only:
+// sample_plan_ok).
 cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n, int k,
-                      const GemmPlan& plan, float* ws, int* counters, cudaStream_t stream, int act = 0);
+                      const GemmPlan& plan, float* ws, int* counters, cudaStream_t stream, int act = 0,
+                      const GemmSampleEpilogue* se = nullptr);
+bool sample_plan_ok(const GemmPlan& plan);
+
+// lm_head GEMM with the sampling epilogue.  The plan is chosen on first use of a shape by timing the
+// persistent-kernel candidates with the epilogue itself (tune = true, outside stream capture), then
+// cached; inside a capture, or without tuning, the heuristic plan is used.
+cudaError_t gemm_bf16_sample(const void* x, int64_t ldx, const void* w, int64_t ldw, int m, int n, int k,
+                             const GemmSampleEpilogue& se, float* ws, int64_t ws_elems, int* counters,
+                             int64_t num_counters, bool tune, cudaStream_t stream, GemmPlan* chosen);
 
 // Same product, configuration chosen by timing candidates on first use of a shape (outside
 // stream capture) and cached; inside a capture the cached or heuristic plan is used.

@@ -5,6 +5,7 @@
 
 #include "comm.h"
 #include "gemm.h"
+#include "kernels.h"
 
 namespace {
 
@@ -68,6 +69,61 @@ std::vector<int64_t> linear_tuned(const at::Tensor& x, const at::Tensor& w, at::
   // splits - 200 K slices (bn = weight rows per CTA)
   return {pl.swap, pl.bn, pl.tiles_p, pl.tiles_q,
           pl.dec == 3 ? 300 : pl.dec == 2 ? 200 + pl.splits : pl.dec ? 100 + pl.splits : pl.streamk ? -pl.mt : pl.splits, pl.grid};
+}
+
+// lm_head GEMM with the sampler in its epilogue: tok[i] = the token sampled from row i of x @ w^T
+// (greedy where temps[i] <= 0, else Gumbel-max at temps[i]), the logits never stored.  keys:
+// int64 [>= m] scratch, zero between calls.  force_* (any set): an explicit persistent-kernel plan
+// (as `linear`); otherwise the tuned one (tune: time candidates on first use of the shape).
+std::vector<int64_t> linear_sample(const at::Tensor& x, const at::Tensor& w, at::Tensor& keys, const at::Tensor& temps,
+                                   const at::Tensor& seed_step, int64_t col_offset, at::Tensor& out_tok,
+                                   const c10::optional<at::Tensor>& out_val, const c10::optional<at::Tensor>& ws,
+                                   const c10::optional<at::Tensor>& counters, bool tune, int64_t force_swap,
+                                   int64_t force_bn, int64_t force_splits) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && keys.is_cuda(), "CUDA tensors required");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "bf16 required");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1, "2-D, unit inner stride");
+  const int m = (int)x.size(0), k = (int)x.size(1), n = (int)w.size(0);
+  TORCH_CHECK(w.size(1) == k, "shape mismatch");
+  TORCH_CHECK(keys.scalar_type() == at::kLong && keys.is_contiguous() && keys.numel() >= m, "keys int64 [>= m]");
+  TORCH_CHECK(temps.scalar_type() == at::kFloat && temps.numel() >= m, "temps fp32 [>= m]");
+  TORCH_CHECK(seed_step.scalar_type() == at::kLong && seed_step.numel() >= 2, "seed_step int64[2]");
+  TORCH_CHECK(out_tok.scalar_type() == at::kInt && out_tok.numel() >= m, "out_tok int32 [>= m]");
+  at::cuda::CUDAGuard g(x.device());
+  float* wsp = nullptr;
+  int* ctr = nullptr;
+  int64_t ws_n = 0, ctr_n = 0;
+  if (ws.has_value() && counters.has_value()) {
+    TORCH_CHECK(ws->scalar_type() == at::kFloat && counters->scalar_type() == at::kInt, "fp32 ws, int32 counters");
+    wsp = ws->data_ptr<float>();
+    ws_n = ws->numel();
+    ctr = counters->data_ptr<int>();
+    ctr_n = counters->numel();
+  }
+  nvb::GemmSampleEpilogue se;
+  se.keys = reinterpret_cast<unsigned long long*>(keys.data_ptr<int64_t>());
+  se.temps = temps.data_ptr<float>();
+  se.seed_step = seed_step.data_ptr<int64_t>();
+  se.col_offset = col_offset;
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  nvb::GemmPlan pl{};
+  cudaError_t e;
+  if (force_swap >= 0 || force_bn > 0 || force_splits != 0) {
+    pl = nvb::gemm_plan(m, n, k, (int)force_swap, (int)force_bn, (int)force_splits);
+    TORCH_CHECK(nvb::sample_plan_ok(pl), "the sampling epilogue needs a persistent-kernel plan");
+    TORCH_CHECK(!pl.streamk || (wsp && pl.ws_elems <= ws_n && 4 * (int64_t)pl.tiles <= ctr_n),
+                "stream-K scratch too small");
+    e = nvb::gemm_bf16(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), nullptr, 0, m, n, k, pl, wsp, ctr, stream,
+                       0, &se);
+  } else {
+    e = nvb::gemm_bf16_sample(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), m, n, k, se, wsp, ws_n, ctr, ctr_n,
+                              tune, stream, &pl);
+  }
+  TORCH_CHECK(e == cudaSuccess, "gemm_bf16 (sampling epilogue) failed: ", cudaGetErrorString(e));
+  e = nvb::launch_sample_keys(se.keys, m, out_tok.data_ptr<int>(),
+                              out_val.has_value() ? out_val->data_ptr<float>() : nullptr, stream);
+  TORCH_CHECK(e == cudaSuccess, "sample_keys failed: ", cudaGetErrorString(e));
+  return {pl.swap, pl.bn, pl.tiles_p, pl.tiles_q, pl.streamk ? -pl.mt : pl.splits, pl.grid};
 }
 
 std::vector<int64_t> plan(int64_t m, int64_t n, int64_t k, int64_t force_swap, int64_t force_bn,
@@ -216,6 +272,12 @@ void register_gemm(pybind11::module& m) {
   m.def("linear_pair", &linear_pair, "CTA-pair tcgen05 GEMM (M = 256 tokens over two CTAs), ranked configuration",
         pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("rank"), pybind11::arg("act") = 0);
   m.def("linear_rs", &linear_rs, "tcgen05 decode GEMM whose rows are stored at their owner rank (reduce-scatter)");
+  m.def("linear_sample", &linear_sample, "lm_head tcgen05 GEMM with the sampler in its epilogue", pybind11::arg("x"),
+        pybind11::arg("w"), pybind11::arg("keys"), pybind11::arg("temps"), pybind11::arg("seed_step"),
+        pybind11::arg("col_offset"), pybind11::arg("out_tok"), pybind11::arg("out_val") = pybind11::none(),
+        pybind11::arg("ws") = pybind11::none(), pybind11::arg("counters") = pybind11::none(),
+        pybind11::arg("tune") = true, pybind11::arg("force_swap") = -1, pybind11::arg("force_bn") = 0,
+        pybind11::arg("force_splits") = 0);
   m.def("gemm_error", &error_code, pybind11::arg("reset") = false);
   m.def("gemm_set_deterministic", [](bool on) { nvb::gemm_set_deterministic(on ? 1 : 0); });
   m.def("gemm_deterministic", []() { return nvb::gemm_deterministic() != 0; });

@@ -198,7 +198,83 @@ struct Params {
   int streamk;               // 1: stream-K split of tiles x k-blocks over the grid
   int64_t sk_iters;          // stream-K: tiles * num_kb
   int act;                   // 1: SiLU-and-mul epilogue (see act_silu_store)
+  // Sampling epilogue (lm_head; keys != nullptr): C is not stored.  Each output value is rounded
+  // to bf16 (the logit the sampler would read), noised for rows at temperature > 0 (Gumbel-max,
+  // the sampler kernels' noise), and folded into keys[token] with an atomic max of
+  // (orderable score << 32 | ~global column): the maximum is the sampled token, the lowest column
+  // winning ties.  keys is all zero before the launch; sample_keys decodes and re-zeroes it.
+  unsigned long long* keys;
+  const float* temps;        // [m] temperature per token row (<= 0: greedy)
+  const int64_t* seed_step;  // (seed, step) of the sampler noise
+  int64_t col_offset;        // global column of output feature 0 (vocab shard start)
 };
+
+// Order-preserving map of a float onto uint32; NaN and -inf -> 0, which never wins (the sampler
+// kernels skip them too: a row with no finite score gets token 0).
+__device__ __forceinline__ uint32_t orderable(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (v != v || v == -INFINITY) ? 0u : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+}
+
+// Sampling epilogue of 32 accumulator columns [qc, qc + 32) of accumulator row pi (see Params).
+// swap: rows are vocabulary features (a warp's lanes hold 32 consecutive ones) and columns are
+// tokens; per column the warp takes the maximum of the order-preserving score words with one
+// redux.sync and the first lane holding it with a ballot (the 32 columns are independent, so the
+// reductions overlap), and lane j issues the atomic for token qc + j.  Otherwise row pi is a token
+// and the thread reduces its 32 features itself.  Called by all 32 lanes of a warp together.
+__device__ __forceinline__ void sample_chunk(const Params& p, int pi, int qc, const float* f) {
+  const uint64_t seed = (uint64_t)p.seed_step[0], step = (uint64_t)p.seed_step[1];
+  if (!p.swap) {
+    if (pi >= p.p_rows) return;
+    const float t = p.temps[pi];
+    const bool greedy = !(t > 0.f);
+    const float inv_t = greedy ? 1.f : 1.f / t;
+    uint32_t best = 0u;
+    int bc = -1;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int c = qc + j;
+      if (c >= p.q_rows) break;
+      float v = bf16_round(f[j]);
+      if (!greedy) v = noised(v, inv_t, seed, step, pi, p.col_offset + c);
+      const uint32_t u = orderable(v);
+      if (u > best) {
+        best = u;
+        bc = c;
+      }
+    }
+    if (bc >= 0)
+      atomicMax(p.keys + pi, ((unsigned long long)best << 32) | (0xFFFFFFFFu - (uint32_t)(p.col_offset + bc)));
+    return;
+  }
+  const int lane = threadIdx.x & 31;
+  const bool row_ok = pi < p.p_rows;
+  const int my_tok = qc + lane;
+  const float my_t = my_tok < p.q_rows ? p.temps[my_tok] : 0.f;
+  const int ncol = min(32, p.q_rows - qc);  // uniform over the warp
+  uint32_t my_best = 0u;
+  int my_src = -1;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j >= ncol) break;
+    const float t = __shfl_sync(FULL_MASK, my_t, j);
+    uint32_t u = 0u;
+    if (row_ok) {
+      float v = bf16_round(f[j]);
+      if (t > 0.f) v = noised(v, 1.f / t, seed, step, qc + j, p.col_offset + pi);
+      u = orderable(v);
+    }
+    const uint32_t umax = __reduce_max_sync(FULL_MASK, u);
+    const unsigned b = __ballot_sync(FULL_MASK, u == umax);
+    if (lane == j) {
+      my_best = umax;
+      my_src = __ffs(b) - 1;
+    }
+  }
+  if (lane < ncol && my_best != 0u)
+    atomicMax(p.keys + my_tok,
+              ((unsigned long long)my_best << 32) | (0xFFFFFFFFu - (uint32_t)(p.col_offset + (pi - lane) + my_src)));
+}
 
 // Fused SiLU-and-mul epilogue.  The weight rows of a gate/up projection are interleaved
 // in groups of 16 (rows 32j..32j+15 = gate features 16j.., rows 32j+16..32j+31 = the
@@ -228,8 +304,13 @@ __device__ __forceinline__ void unit_coords(const Params& p, int unit, int& tp, 
   tq = r / gsize;
 }
 
-// Store 32 accumulator columns [qc, qc + 32) of accumulator row pi as bf16.
+// Store 32 accumulator columns [qc, qc + 32) of accumulator row pi as bf16 (or, with the sampling
+// epilogue, fold them into the per-token keys).
 __device__ __forceinline__ void store_chunk(const Params& p, int pi, int qc, const float* f) {
+  if (p.keys) {
+    sample_chunk(p, pi, qc, f);
+    return;
+  }
   if (pi >= p.p_rows) return;
   if (p.act) {  // normal orientation only; q_rows % 32 == 0
     if (qc < p.q_rows) act_silu_store(p.c + (int64_t)pi * p.ldc + qc / 2, f);
@@ -2372,13 +2453,20 @@ GemmPlan gemm_plan(int m, int n, int k, int force_swap, int force_bn, int force_
   return pl;
 }
 
+bool sample_plan_ok(const GemmPlan& pl) { return !pl.dec && (pl.streamk || pl.splits <= 1); }
+
 cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int m, int n, int k,
-                      const GemmPlan& pl, float* ws, int* counters, cudaStream_t stream, int act) {
+                      const GemmPlan& pl, float* ws, int* counters, cudaStream_t stream, int act,
+                      const GemmSampleEpilogue* se) {
   if (m == 0 || n == 0) return cudaSuccess;
   if (act && (pl.swap || n % 32 || pl.bn % 32)) return cudaErrorInvalidValue;
   if (k % 8 || ldx % 8 || ldw % 8) return cudaErrorInvalidValue;
   if (((uintptr_t)x & 15) || ((uintptr_t)w & 15)) return cudaErrorMisalignedAddress;
-  if (!pl.swap && (ldc % 8 || ((uintptr_t)c & 15))) return cudaErrorInvalidValue;
+  if (se) {  // the sampling epilogue lives in the persistent kernel (one K range per tile, or stream-K)
+    if (act || !sample_plan_ok(pl) || !se->keys || !se->temps || !se->seed_step) return cudaErrorInvalidValue;
+  } else if (!pl.swap && (ldc % 8 || ((uintptr_t)c & 15))) {
+    return cudaErrorInvalidValue;
+  }
   if (pl.dec == 2) {
     if (m > pl.mt || k % BK) return cudaErrorInvalidValue;
     return run_skinny(plan_to_skinny(pl), x, ldx, w, ldw, c, ldc, m, n, k, stream, act);
@@ -2415,6 +2503,10 @@ cudaError_t gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, vo
   prm.counters = counters;
   prm.streamk = pl.streamk;
   prm.act = act;
+  prm.keys = se ? se->keys : nullptr;
+  prm.temps = se ? se->temps : nullptr;
+  prm.seed_step = se ? se->seed_step : nullptr;
+  prm.col_offset = se ? se->col_offset : 0;
   prm.sk_iters = (int64_t)pl.tiles * pl.num_kb;
   cudaError_t e;
   if (pl.streamk) {
@@ -2584,6 +2676,88 @@ cudaError_t gemm_bf16_tuned(const void* x, int64_t ldx, const void* w, int64_t l
   }
   if (chosen) *chosen = best;
   return gemm_bf16(x, ldx, w, ldw, c, ldc, m, n, k, best, ws, counters, stream, act);
+}
+
+cudaError_t gemm_bf16_sample(const void* x, int64_t ldx, const void* w, int64_t ldw, int m, int n, int k,
+                             const GemmSampleEpilogue& se, float* ws, int64_t ws_elems, int* counters,
+                             int64_t num_counters, bool tune, cudaStream_t stream, GemmPlan* chosen) {
+  if (m == 0 || n == 0) return cudaSuccess;
+  static std::map<std::tuple<int, int, int>, GemmPlan> cache;  // guarded by tune_mutex()
+  const auto key = std::make_tuple(m_bucket(m), n, k);
+  auto fits = [&](const GemmPlan& pl) {
+    return sample_plan_ok(pl) && (!pl.streamk || (ws && counters && pl.ws_elems <= ws_elems &&
+                                                  4 * (int64_t)pl.tiles <= num_counters));
+  };
+  // the plain GEMM's heuristic plan when the persistent kernel runs it (deterministic mode then
+  // rounds every logit as the logits path does), else the heuristic orientation with one K range
+  GemmPlan best = gemm_plan(m, n, k, -1, 0, 0);
+  if (!sample_plan_ok(best)) best = gemm_plan(m, n, k, -1, 0, 1);
+  {
+    std::lock_guard<std::mutex> g(tune_mutex());
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      if (chosen) *chosen = it->second;
+      return gemm_bf16(x, ldx, w, ldw, nullptr, 0, m, n, k, it->second, ws, counters, stream, 0, &se);
+    }
+  }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(stream, &cap);
+  if (tune && cap == cudaStreamCaptureStatusNone && !gemm_deterministic()) {
+    // time the persistent-kernel candidates with the sampling epilogue itself (its cost depends on
+    // the orientation), each after a 256 MiB read, then clear the keys they left behind
+    std::vector<GemmPlan> cands{best};
+    for (int bn : {256, 128}) cands.push_back(gemm_plan(m, n, k, 0, bn, 1));
+    if (m <= 256) cands.push_back(gemm_plan(m, n, k, 1, m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256, 1));
+    for (int bn : {256, 128}) {
+      cands.push_back(gemm_plan(m, n, k, 0, bn, -1));
+      if (m > BM) cands.push_back(gemm_plan(m, n, k, 0, bn, -2));
+    }
+    const size_t flush_bytes = (size_t)256 << 20;
+    void* flush = nullptr;
+    if (cudaMalloc(&flush, flush_bytes) != cudaSuccess) {
+      cudaGetLastError();
+      flush = nullptr;
+    }
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    float best_ms = 1e30f;
+    for (const auto& pl : cands) {
+      if (!fits(pl)) continue;
+      if (gemm_bf16(x, ldx, w, ldw, nullptr, 0, m, n, k, pl, ws, counters, stream, 0, &se) != cudaSuccess) {
+        cudaGetLastError();
+        continue;
+      }
+      float total = 0.f;
+      bool good = true;
+      for (int r = 0; r < 3 && good; ++r) {
+        if (flush)
+          l2_evict_kernel<<<num_sms() * 4, 256, 0, stream>>>(static_cast<const uint4*>(flush), flush_bytes / 16 - 16,
+                                                            static_cast<int*>(flush) + (flush_bytes / 4 - 1));
+        cudaEventRecord(e0, stream);
+        good = gemm_bf16(x, ldx, w, ldw, nullptr, 0, m, n, k, pl, ws, counters, stream, 0, &se) == cudaSuccess;
+        cudaEventRecord(e1, stream);
+        cudaEventSynchronize(e1);
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        total += ms;
+      }
+      if (good && total < best_ms) {
+        best_ms = total;
+        best = pl;
+      }
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (flush) cudaFree(flush);
+    cudaMemsetAsync(se.keys, 0, sizeof(unsigned long long) * (size_t)m, stream);
+    std::lock_guard<std::mutex> g(tune_mutex());
+    cache[key] = best;
+  } else if (!fits(best)) {
+    best = gemm_plan(m, n, k, 0, 128, 1);
+  }
+  if (chosen) *chosen = best;
+  return gemm_bf16(x, ldx, w, ldw, nullptr, 0, m, n, k, best, ws, counters, stream, 0, &se);
 }
 
 cudaError_t gemm_bf16_rs(const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t ldc, int m, int n, int k,

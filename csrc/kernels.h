@@ -76,5 +76,8 @@ cudaError_t launch_sample_rows(const void* logits, int logits_is_bf16, int64_t l
                                const float* temps, const float* top_p, const int64_t* seed_step, int* out_tok,
                                float* out_val, const SampleX& X, cudaStream_t stream);
 int sample_error_code(int reset);
+// Tokens (and, optionally, winning scores) from the per-row keys of the lm_head GEMM's sampling
+// epilogue; zeroes the keys for the next launch.
+cudaError_t launch_sample_keys(unsigned long long* keys, int rows, int* out_tok, float* out_val, cudaStream_t stream);
 
 }  // namespace nvb

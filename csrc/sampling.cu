@@ -15,21 +15,7 @@
 
 namespace nvb {
 
-__device__ __forceinline__ uint64_t mix64(uint64_t z) {
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  return z ^ (z >> 31);
-}
-
-__device__ __forceinline__ float gumbel(uint64_t seed, uint64_t step, int row, int64_t col) {
-  uint64_t h = mix64(seed + 0x9E3779B97F4A7C15ull * (step + 1));
-  h = mix64(h ^ ((uint64_t)row << 40) ^ (uint64_t)col);
-  // 23 random bits: (k + 0.5) / 2^23 is exact in fp32 and lies in [2^-24, 1 - 2^-24], so u < 1 and
-  // the noise is finite (24 bits would round the top value up to u = 1 and give g = +inf,
-  // letting a random column win about once per 2^24 columns)
-  const float u = ((float)(h >> 41) + 0.5f) * (1.0f / 8388608.0f);
-  return -logf(-logf(u));
-}
+__device__ int g_sample_error = 0;  // 300+: a vocab-parallel exchange timed out
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v);
@@ -48,7 +34,7 @@ __device__ __forceinline__ void consider(float v, int c, float& best, int& bidx)
 // Partial (max, argmax) of the noised scores over one column chunk of one row.  bf16
 // rows are read 8 columns per 16-byte load when the row start is 16-byte aligned.
 template <typename T>
-__global__ void __launch_bounds__(256) sample_partial_kernel(const T* __restrict__ logits, int64_t ld, int V,
+__global__ void __launch_bounds__(256, 4) sample_partial_kernel(const T* __restrict__ logits, int64_t ld, int V,
                                                              int64_t col_offset, const float* __restrict__ temps,
                                                              const int64_t* __restrict__ seed_step,
                                                              float* __restrict__ part_val, int* __restrict__ part_idx,
@@ -65,34 +51,56 @@ __global__ void __launch_bounds__(256) sample_partial_kernel(const T* __restrict
   int bidx = 0x7fffffff;
   const T* lr = logits + (int64_t)row * ld;
   constexpr bool VEC = sizeof(T) == 2;
-  if (VEC && (((uintptr_t)(lr + c0)) & 15) == 0 && greedy) {
+  if (VEC && (((uintptr_t)(lr + c0)) & 15) == 0) {
     const int nv = (c1 - c0) >> 3;
     const uint4* src = reinterpret_cast<const uint4*>(lr + c0);
-    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-      float f[8];
-      bf16x8_to_f32(__ldg(src + i), f);
+    const int nb = blockDim.x;
+    int i = threadIdx.x;
+    if (greedy) {
+      // Four independent 16-byte loads in flight per thread (one at a time left each SM with about
+      // 20 KB in flight, under half of what HBM needs).  The 8 values of a load are reduced with
+      // bf16x2 max first; only a load whose maximum beats the running one is searched for the
+      // column (a thread visits its columns in increasing order, so the first maximum wins ties).
+      for (; i < nv; i += 4 * nb) {
+        uint4 r[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) consider(f[j], c0 + i * 8 + j, best, bidx);
-    }
-    for (int c = c0 + nv * 8 + threadIdx.x; c < c1; c += blockDim.x) consider(to_f<T>(lr[c]), c, best, bidx);
-  } else if (VEC && (((uintptr_t)(lr + c0)) & 15) == 0) {
-    const int nv = (c1 - c0) >> 3;
-    const uint4* src = reinterpret_cast<const uint4*>(lr + c0);
-    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-      float f[8];
-      bf16x8_to_f32(__ldg(src + i), f);
+        for (int k = 0; k < 4; ++k)
+          if (i + k * nb < nv) r[k] = __ldg(src + i + k * nb);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c = c0 + i * 8 + j;
-        consider(f[j] * inv_t + gumbel(seed, step, row, col_offset + c), c, best, bidx);
+        for (int k = 0; k < 4; ++k) {
+          if (i + k * nb >= nv) break;
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r[k]);
+          const __nv_bfloat162 m2 = __hmax2(__hmax2(h[0], h[1]), __hmax2(h[2], h[3]));
+          const float m = fmaxf(__low2float(m2), __high2float(m2));
+          if (m > best) {
+            float f[8];
+            bf16x8_to_f32(r[k], f);
+            int j = 0;
+            while (j < 7 && f[j] != m) ++j;
+            best = m;
+            bidx = c0 + (i + k * nb) * 8 + j;
+          }
+        }
+      }
+    } else {
+      for (; i < nv; i += nb) {
+        float f[8];
+        bf16x8_to_f32(__ldg(src + i), f);
+        const int cb = c0 + i * 8;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          consider(noised(f[j], inv_t, seed, step, row, col_offset + cb + j), cb + j, best, bidx);
       }
     }
-    for (int c = c0 + nv * 8 + threadIdx.x; c < c1; c += blockDim.x)
-      consider(to_f<T>(lr[c]) * inv_t + gumbel(seed, step, row, col_offset + c), c, best, bidx);
+    for (int c = c0 + nv * 8 + threadIdx.x; c < c1; c += nb) {
+      float v = to_f<T>(lr[c]);
+      if (!greedy) v = noised(v, inv_t, seed, step, row, col_offset + c);
+      consider(v, c, best, bidx);
+    }
   } else {
     for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
       float v = to_f<T>(lr[c]);
-      if (!greedy) v = v * inv_t + gumbel(seed, step, row, col_offset + c);
+      if (!greedy) v = noised(v, inv_t, seed, step, row, col_offset + c);
       consider(v, c, best, bidx);
     }
   }
@@ -157,10 +165,41 @@ __global__ void sample_final_kernel(const float* __restrict__ part_val, const in
   }
 }
 
+// Tokens from the keys of the lm_head GEMM's sampling epilogue (orderable score << 32 | ~column);
+// every key is zeroed again for the next launch.  A row whose key stayed zero (no finite score)
+// gets token 0, as the chunked sampler gives it.
+__global__ void sample_keys_kernel(unsigned long long* __restrict__ keys, int rows, int* __restrict__ out_tok,
+                                   float* __restrict__ out_val) {
+  pdl_wait();     // the keys come from the previous kernel in the stream
+  pdl_trigger();  // the next kernel may start its prologue
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows) return;
+  const unsigned long long k = keys[i];
+  keys[i] = 0ull;
+  if (k == 0ull) {
+    out_tok[i] = 0;
+    if (out_val) out_val[i] = -INFINITY;
+    return;
+  }
+  out_tok[i] = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+  if (out_val) {
+    const uint32_t u = (uint32_t)(k >> 32);
+    out_val[i] = __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
+  }
+}
+
+cudaError_t launch_sample_keys(unsigned long long* keys, int rows, int* out_tok, float* out_val, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  launch_pdl(sample_keys_kernel, dim3((rows + 255) / 256), dim3(256), 0, stream, keys, rows, out_tok, out_val);
+  NVB_LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
 int sample_num_chunks(int rows, int V) {
-  // ~4 CTAs per SM in total, chunks of at least 4096 columns (a multiple of 8, so every
-  // chunk of a 16-byte-aligned row starts aligned)
-  int want = (4 * 148 + rows - 1) / (rows > 0 ? rows : 1);
+  // at most 4 CTAs per SM in total (the partial kernel's residency), so every CTA runs in the first
+  // wave; chunks of at least 4096 columns (a multiple of 8, so every chunk of a 16-byte-aligned row
+  // starts aligned)
+  int want = (4 * 148) / (rows > 0 ? rows : 1);
   int max_chunks = (V + 4095) / 4096;
   int n = want < max_chunks ? want : max_chunks;
   return n < 1 ? 1 : n;
@@ -222,7 +261,6 @@ __device__ __forceinline__ void sx_st_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-__device__ int g_sample_error = 0;
 
 // Float offsets of the exchange regions and word offsets of the flags (see SampleX).
 __device__ __forceinline__ int64_t sx_region(const SampleX& X, int round) {
@@ -475,7 +513,7 @@ __global__ void __launch_bounds__(1024) sample_rows_kernel(const T* __restrict__
   for (int c = threadIdx.x; c < V; c += blockDim.x) {
     const float l = to_f<T>(lr[c]);
     if (use_p && M - l * inv_t >= cut_d) continue;
-    const float v = greedy ? l : l * inv_t + gumbel(seed, step, row, col_offset + c);
+    const float v = greedy ? l : noised(l, inv_t, seed, step, row, col_offset + c);
     consider(v, c, best, bidx);
   }
 #pragma unroll

@@ -28,7 +28,8 @@ from ..ops.cuda_ops import CudaOps
 NQ, NKV, D, HID, INTER, VOCAB = 32, 8, 128, 4096, 12288, 151936
 CASES = ("attn_decode", "attn_decode_fp8", "attn_prefill", "attn_prefill_mma", "attn_prefill_fp8",
          "attn_prefill_flash_attn", "gemm_prefill", "gemm_decode", "gemm_decode256", "gemm_gate_up_silu256", "qkv_post",
-         "qkv_post_fp8", "add_rmsnorm", "silu_mul", "sample")
+         "qkv_post_fp8", "add_rmsnorm", "silu_mul", "sample", "lm_head_sample256", "lm_head_logits_sample256",
+         "lm_head_sample256_t", "lm_head_logits_sample256_t", "lm_head_logits256")
 # Qwen3-8B decode GEMM shapes (n, k) for gemm_sweep: qkv, o_proj, gate_up, down_proj, lm_head
 DECODE_SHAPES = {"qkv": ((NQ + 2 * NKV) * D, HID), "o_proj": (HID, NQ * D), "gate_up": (2 * INTER, HID),
                  "down_proj": (HID, INTER), "lm_head": (VOCAB, HID)}
@@ -128,6 +129,22 @@ def build_case(name: str, ops: CudaOps, dev="cuda"):
         t = torch.zeros(256, device=dev)
         st = torch.tensor([0, 1], dtype=torch.int64, device=dev)
         return (lambda: ops.sample(logits, t, step=st)), logits.numel() * 2, None
+    if name.startswith("lm_head"):
+        # Qwen3-8B lm_head at a 256-token decode step, greedy (or, "_t", every row at temperature
+        # 0.8): the sampler in the GEMM epilogue ("lm_head_sample256"), the GEMM writing bf16 logits
+        # followed by the sampler kernel ("lm_head_logits_sample256"), or the GEMM alone
+        m = 256
+        x = torch.randn(m, HID, device=dev).to(torch.bfloat16)
+        w = (torch.randn(VOCAB, HID, device=dev) * 0.02).to(torch.bfloat16)
+        t = torch.full((m,), 0.8 if name.endswith("_t") else 0.0, device=dev)
+        st = torch.tensor([0, 1], dtype=torch.int64, device=dev)
+        wbytes = 2 * (m * HID + VOCAB * HID)
+        if name.startswith("lm_head_sample256"):
+            return (lambda: ops.lm_head_sample(x, w, t, st)), wbytes, 2 * m * VOCAB * HID
+        out = torch.empty(m, VOCAB, device=dev, dtype=torch.bfloat16)
+        if name == "lm_head_logits256":
+            return (lambda: ops.linear(x, w, out)), wbytes + 2 * m * VOCAB, 2 * m * VOCAB * HID
+        return (lambda: ops.sample(ops.linear(x, w, out), t, step=st)), wbytes, 2 * m * VOCAB * HID
     raise ValueError(f"unknown case {name!r}; one of {', '.join(CASES)}")
 
 

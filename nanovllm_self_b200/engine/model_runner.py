@@ -331,10 +331,22 @@ class ModelRunner:
 
     # ------------------------------------------------------------- execution
     def _forward_and_sample(self, ids, pos, ctx, temps, topp):
+        if self._fused_sampler_ok(ctx):
+            # one rank, no top-p rows: the sampler runs in the lm_head GEMM's epilogue
+            h, residual, normed = self.model.forward_hidden(ids, pos, ctx, self.kv_layers, self.kv_scale_layers)
+            if ctx.logits_indices.numel() == 0:
+                return torch.empty(0, dtype=torch.int32, device=ids.device)
+            x = self.model.final_rows(h, residual, ctx.logits_indices, normed)
+            return self.ops.lm_head_sample(x, self.model.lm_head, temps, self._step_tensor(), self.model.vocab_start)
         logits = self.model.forward(ids, pos, ctx, self.kv_layers, self.kv_scale_layers)
         if logits.shape[0] == 0:
             return torch.empty(0, dtype=torch.int32, device=ids.device)
         return self.sample(logits, temps, topp)
+
+    def _fused_sampler_ok(self, ctx) -> bool:
+        return (self.is_cuda and self.config.fused_sampler and self.tp.size == 1 and not self._use_top_p
+                and hasattr(self.ops, "lm_head_sample")
+                and ctx.logits_indices.numel() <= getattr(self.ops, "sample_keys_cap", 0))
 
     def sample(self, logits, temps, topp):
         if self.tp.size > 1 and self.comm is not None:

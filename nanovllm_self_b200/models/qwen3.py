@@ -158,9 +158,13 @@ class Qwen3ForCausalLM:
 
     def compute_logits(self, h, residual, logits_indices: torch.Tensor, normed: bool = False) -> torch.Tensor:
         """Final norm on the sampled rows only, then the (vocab-parallel) lm_head."""
-        ops = self.ops
         if logits_indices.numel() == 0:
             return torch.empty(0, self.vocab_end - self.vocab_start, device=h.device, dtype=torch.float32)
+        return self.ops.linear(self.final_rows(h, residual, logits_indices, normed), self.lm_head)
+
+    def final_rows(self, h, residual, logits_indices: torch.Tensor, normed: bool = False) -> torch.Tensor:
+        """The final-normed hidden rows of the sampled tokens (the lm_head's input)."""
+        ops = self.ops
         if normed:
             x = h.index_select(0, logits_indices)
         elif self.comm is not None and self.tp_size > 1:
@@ -169,7 +173,7 @@ class Qwen3ForCausalLM:
             x, _ = self.comm.allreduce_add_rmsnorm(hs, rs, self.norm, self.eps, final=True)
         else:
             x, _ = ops.add_rmsnorm_rows(h, residual, self.norm, self.eps, logits_indices)
-        return ops.linear(x, self.lm_head)
+        return x
 
     def forward(self, input_ids, positions, ctx, kv_caches, kv_scales=None):
         h, residual, normed = self.forward_hidden(input_ids, positions, ctx, kv_caches, kv_scales)

@@ -15,6 +15,7 @@ _GEMM_WS_ELEMS = 24 << 20        # fp32 stream-K partial tiles (96 MiB: 2 per CT
 _GEMM_COUNTERS = 1 << 16         # split-K arrival counters (4 per output tile)
 _ATTN_PART_ROWS = 1 << 16        # (seq, q head, split) rows of split-KV scratch
 _SAMPLE_PART = 1 << 16
+_SAMPLE_KEYS = 4096              # rows of one fused lm_head + sampler call
 
 
 class _Scratch:
@@ -25,6 +26,7 @@ class _Scratch:
         self.part_lse = torch.empty(_ATTN_PART_ROWS, dtype=torch.float32, device=device)
         self.sample_val = torch.empty(_SAMPLE_PART, dtype=torch.float32, device=device)
         self.sample_idx = torch.empty(_SAMPLE_PART, dtype=torch.int32, device=device)
+        self.sample_keys = torch.zeros(_SAMPLE_KEYS, dtype=torch.int64, device=device)  # zero between calls
 
 
 class CudaOps:
@@ -145,6 +147,22 @@ class CudaOps:
         return out
 
     # -------------------------------------------------------------- sampling
+    sample_keys_cap = _SAMPLE_KEYS
+
+    def lm_head_sample(self, x, w, temperatures, step, col_offset=0):
+        """Tokens sampled from x @ w^T (greedy where the temperature is <= 0, else Gumbel-max at
+        it) by the lm_head GEMM's sampling epilogue: the logits are never written to memory.
+        Same draws as ``linear`` followed by ``sample`` (same bf16 logits, same noise)."""
+        rows = x.shape[0]
+        tok = torch.empty(rows, dtype=torch.int32, device=x.device)
+        if rows == 0:
+            return tok
+        sc = self.scratch(x.device)
+        self.last_plan = self.C.linear_sample(x, w, sc.sample_keys, temperatures, step, int(col_offset), tok, None,
+                                              sc.gemm, sc.gemm_counters, True)
+        self.launches += 2
+        return tok
+
     def sample(self, logits, temperatures, top_p=None, seeds=None, step=None, batch_greedy_compat=False,
                generator=None, use_top_p=False, col_offset=0):
         rows, V = logits.shape

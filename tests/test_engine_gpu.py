@@ -92,3 +92,23 @@ def test_qwen3_0_6b_random_runs():
     got = _engine_logits(llm, p)
     ref = dense_logits(llm.model_runner.model, p)
     assert torch.nn.functional.cosine_similarity(got, ref, dim=0).item() > 0.995
+
+
+def test_fused_sampler_equals_logits_path():
+    """Greedy decoding with the sampler in the lm_head GEMM's epilogue matches the logits + sampler
+    path token for token, unless the two runs first part at a near-tie of the dense oracle's logits
+    (the two lm_head plans may round a logit to the neighbouring bf16 value)."""
+    prompts = _prompts(5)
+    sp = SamplingParams(temperature=0.0, max_tokens=24, ignore_eos=True)
+    outs = []
+    for fused in (True, False):
+        llm = _llm(fused_sampler=fused, deterministic=True)
+        outs.append(llm.generate(prompts, sp))
+        model = llm.model_runner.model
+    for a, b in zip(*outs):
+        if a == b:
+            continue
+        i = next(j for j in range(len(a)) if a[j] != b[j])
+        ref = dense_logits(model, a[:i])
+        gap = (ref[a[i]] - ref[b[i]]).abs().item()
+        assert gap < 0.05, (i, gap)

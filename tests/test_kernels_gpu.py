@@ -112,6 +112,44 @@ def test_qkv_post(ops, kv_dtype, bs, nq, nkv):
         _close(vc, vc2, 0.03)
 
 
+@pytest.mark.parametrize("kv_dtype", [torch.bfloat16, torch.float8_e4m3fn])
+@pytest.mark.parametrize("nq,nkv", [(32, 8), (8, 2), (4, 1)])
+def test_qkv_post_many_chunks(ops, kv_dtype, nq, nkv):
+    # enough tokens that every CTA of the persistent kernel refills its stage ring several times,
+    # and a count that is not a multiple of the tokens per stage (the last stage is partial)
+    T, bs = 9001, 16
+    nb = (T + bs - 1) // bs + 3
+    kc, vc, ks, vs, g = _kv_setup(nb, nkv, bs, kv_dtype, seed=2)
+    qkv = torch.randn(T, (nq + 2 * nkv) * 128, device=DEV, generator=g).bfloat16()
+    qn = (1 + 0.1 * torch.randn(128, device=DEV, generator=g)).bfloat16()
+    kn = (1 + 0.1 * torch.randn(128, device=DEV, generator=g)).bfloat16()
+    pos = torch.arange(T, device=DEV, dtype=torch.int32)
+    cs = R.rope_cos_sin(128, 16384, 1e6, device=DEV)
+    table = torch.randperm(nb, generator=torch.Generator().manual_seed(3)).to(DEV)
+    p = pos.long()
+    slots = (table[p // bs] * bs + p % bs).to(torch.int32)
+    q = ops.qkv_post(qkv, qn, kn, 1e-6, pos, cs, kc, vc, slots, ks, vs, nq, nkv, 128)
+    kc2, vc2 = torch.zeros_like(kc, dtype=torch.float32), torch.zeros_like(vc, dtype=torch.float32)
+    ks2 = vs2 = None
+    if kv_dtype == torch.float8_e4m3fn:
+        kc2, vc2 = torch.zeros_like(kc), torch.zeros_like(vc)
+        ks2, vs2 = torch.ones_like(ks), torch.ones_like(vs)
+    qf = qkv.float()
+    qr = R.apply_rope(R.rmsnorm(qf[:, :nq * 128].reshape(T, nq, 128), qn.float(), 1e-6), pos, cs)
+    kr = R.apply_rope(R.rmsnorm(qf[:, nq * 128:(nq + nkv) * 128].reshape(T, nkv, 128), kn.float(), 1e-6), pos, cs)
+    vr = qf[:, (nq + nkv) * 128:].reshape(T, nkv, 128)
+    R.store_kv(kr, vr, kc2, vc2, slots, ks2, vs2)
+    _close(q.view(T, nq, 128), qr, 0.03)
+    if kv_dtype == torch.float8_e4m3fn:
+        _close(kc.float() * ks[:, :, None, None], kc2.float() * ks2[:, :, None, None], 0.05, 0.08)
+        _close(vc.float() * vs[:, :, None, None], vc2.float() * vs2[:, :, None, None], 0.05, 0.08)
+        _close(ks, ks2, 1e-3)
+    else:
+        _close(kc, kc2, 0.03)
+        _close(vc, vc2, 0.03)
+    assert ops.C.bounds_error(True) == 0
+
+
 def _paged_case(q_lens, k_lens, nq, nkv, bs, kv_dtype, seed=1):
     nb = sum((k + bs - 1) // bs for k in k_lens) + 4
     g = torch.Generator(device=DEV).manual_seed(seed)
@@ -207,6 +245,74 @@ def test_sample_greedy_and_temperature(ops):
         counts += torch.bincount(t.long().cpu(), minlength=4).float()
     freq = counts / counts.sum()
     assert torch.allclose(freq, torch.tensor([0.1, 0.2, 0.3, 0.4]), atol=0.02), freq
+
+
+@pytest.mark.parametrize("rows,V,ld", [(256, 151936, 151936), (3, 151936, 151936), (5, 151941, 151944),
+                                       (4, 18992, 18992), (2, 1001, 1003)])
+def test_sample_bf16_rows(ops, rows, V, ld):
+    # bf16 logits: the bulk-copy path (16-byte aligned rows, with a column tail when V % 8 != 0), and
+    # rows whose stride breaks the alignment (plain loads); bf16 rows hold many exact ties, and the
+    # first maximum must win as in torch.argmax
+    g = torch.Generator(device=DEV).manual_seed(rows + V)
+    full = torch.randn(rows, ld, device=DEV, generator=g).bfloat16()
+    logits = full[:, :V]
+    logits[0, V - 1] = 9.0  # the winner in the tail (or the last vector) of row 0
+    if rows > 1:
+        logits[1, 3] = 9.0
+        logits[1, V // 2] = 9.0  # a tie: the first column wins
+    temps = torch.zeros(rows, device=DEV)
+    step = torch.tensor([5, 1], dtype=torch.int64, device=DEV)
+    tok = ops.sample(logits, temps, step=step)
+    assert torch.equal(tok.long(), logits.float().argmax(-1))
+    # temperature: a dominant column is always drawn; a 4-way distribution follows softmax(l / T)
+    hot = logits.clone()
+    hot[:, V // 3] = 60.0
+    tok = ops.sample(hot, torch.ones(rows, device=DEV), step=step)
+    assert bool((tok == V // 3).all())
+    small = torch.log(torch.tensor([[0.1, 0.2, 0.3, 0.4]], device=DEV)).repeat(4096, 1).bfloat16()
+    counts = torch.zeros(4)
+    for s in range(4):
+        t = ops.sample(small, torch.ones(4096, device=DEV), step=torch.tensor([13, s], dtype=torch.int64, device=DEV))
+        counts += torch.bincount(t.long().cpu(), minlength=4).float()
+    freq = counts / counts.sum()
+    ref = torch.softmax(small[0].float(), -1).cpu()
+    assert torch.allclose(freq, ref, atol=0.02), (freq, ref)
+    assert ops.C.sample_error(True) == 0
+
+
+@pytest.mark.parametrize("m", [1, 7, 64, 256, 300])
+@pytest.mark.parametrize("n,col_offset", [(151936, 0), (18992, 37984), (1000, 0)])
+def test_lm_head_sample_matches_logits_path(ops, m, n, col_offset):
+    """The lm_head GEMM with the sampler in its epilogue draws exactly the tokens of the same GEMM
+    writing bf16 logits followed by the sampler kernel (greedy and temperature rows, same noise),
+    in both orientations, tile widths and stream-K, and leaves its key scratch zeroed."""
+    k = 1024
+    g = torch.Generator(device=DEV).manual_seed(m * 7 + n)
+    x = torch.randn(m, k, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(n, k, device=DEV, generator=g) * 0.05).bfloat16()
+    temps = torch.tensor([0.0, 0.7, 0.0, 1.3], device=DEV).repeat((m + 3) // 4)[:m].contiguous()
+    step = torch.tensor([3, 5], dtype=torch.int64, device=DEV)
+    sc = ops.scratch(DEV)
+    plans = [(0, 128, 1), (0, 256, 1), (0, 128, -1)]
+    if m <= 256:
+        plans.append((1, 0, 1))
+    for swap, bn, splits in plans:
+        tok = torch.empty(m, dtype=torch.int32, device=DEV)
+        ops.C.linear_sample(x, w, sc.sample_keys, temps, step, col_offset, tok, None, sc.gemm, sc.gemm_counters,
+                            False, swap, bn, splits)
+        logits = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+        ops.C.linear(x, w, logits, sc.gemm, sc.gemm_counters, swap, bn, splits, 0)
+        ref = ops.sample(logits, temps, step=step, col_offset=col_offset)
+        assert torch.equal(tok, ref), (swap, bn, splits, (tok != ref).nonzero()[:4].tolist())
+        assert bool((sc.sample_keys[:m] == 0).all())
+    # the tuned plan: greedy rows take the fp32 argmax up to bf16 rounding of close logits
+    tok = ops.lm_head_sample(x, w, temps, step, col_offset)
+    ref32 = x.float() @ w.float().t()
+    greedy = temps <= 0
+    got = ref32.gather(1, (tok.long() - col_offset)[:, None])[:, 0]
+    assert bool((got[greedy] >= ref32.max(1).values[greedy] - 0.02).all())
+    assert bool((sc.sample_keys[:m] == 0).all())
+    assert ops.C.gemm_error(True) == 0
 
 
 def test_temperature_sampling_never_leaves_the_live_columns(ops):
