@@ -165,11 +165,13 @@ class Qwen3ForCausalLM:
     def final_rows(self, h, residual, logits_indices: torch.Tensor, normed: bool = False) -> torch.Tensor:
         """The final-normed hidden rows of the sampled tokens (the lm_head's input)."""
         ops = self.ops
+        # every row sampled (decode steps: one token per sequence, indices 0..T-1): no gather
+        every_row = logits_indices.numel() == h.shape[0]
         if normed:
-            x = h.index_select(0, logits_indices)
+            x = h if every_row else h.index_select(0, logits_indices)
         elif self.comm is not None and self.tp_size > 1:
-            hs = h.index_select(0, logits_indices)
-            rs = residual.index_select(0, logits_indices)
+            hs = h if every_row else h.index_select(0, logits_indices)
+            rs = residual if every_row else residual.index_select(0, logits_indices)
             x, _ = self.comm.allreduce_add_rmsnorm(hs, rs, self.norm, self.eps, final=True)
         else:
             x, _ = ops.add_rmsnorm_rows(h, residual, self.norm, self.eps, logits_indices)

@@ -107,12 +107,16 @@ class PDPool:
         for wd in self.pwd + self.dwd:
             wd.touch("shutdown")
         deadline = time.time() + timeout_s
+        codes = []
         for p in self.procs:
             try:
                 p.wait(timeout=max(0.1, deadline - time.time()) if not force else 5)
             except subprocess.TimeoutExpired:
                 p.kill()
                 p.wait(timeout=10)
+            codes.append(p.returncode)
+        # exit status of every worker process (torchrun's for a TP group): 0 = a clean shutdown
+        self.exit_codes = codes
         self.procs = []
 
     # --------------------------------------------------------------- routing

@@ -392,11 +392,12 @@ class PrefillWorker:
         from ...ops._ext import available, load
         if self.peer_pools and available():
             C = load()
-            for ptr, _, _ in self.peer_pools.values():
+            for entry in self.peer_pools.values():  # [ptr, info, offset, flag_ptr, epoch]
                 try:
-                    C.symm_close(int(ptr))
+                    C.symm_close(int(entry[0]))
                 except RuntimeError:
                     pass
+            self.peer_pools.clear()
         self.runner.release_graphs()
         _close_worlds(self)
 

@@ -62,6 +62,7 @@ def test_clean_run_passes_the_audit(tmp_path):
         assert s["num_errors"] == 0, pool.results
     finally:
         pool.shutdown()
+    assert all(c == 0 for c in pool.exit_codes), pool.exit_codes  # every worker shut down cleanly
     rep = audit(tmp_path)
     assert not rep["processes"] and not rep["error_files"] and not rep["handshake_leftovers"], rep
     assert not rep["pending_state"] and not rep["sockets"], rep

@@ -69,6 +69,7 @@ def test_pd_pool_two_gpus(tmp_path, backend):
     finally:
         pool.shutdown()
     assert s["num_errors"] == 0, pool.results
+    assert pool.exit_codes == [0, 0], pool.exit_codes  # both workers shut down cleanly
     got = {pool.submitted[b]["row"]["id"]: r["output_ids"] for b, r in pool.results.items()}
     _exact(got, want)
 
@@ -92,5 +93,6 @@ def test_pd_pool_ipc_push_fp8_kv(tmp_path):
     finally:
         pool.shutdown()
     assert s["num_errors"] == 0, pool.results
+    assert pool.exit_codes == [0, 0], pool.exit_codes  # both workers shut down cleanly
     got = {pool.submitted[b]["row"]["id"]: r["output_ids"] for b, r in pool.results.items()}
     _exact(got, want)
