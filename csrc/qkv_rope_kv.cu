@@ -76,28 +76,62 @@ __device__ __forceinline__ float half_max(float v, unsigned hmask) {
   return v;
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE round-to-nearest operations per instruction,
+// the same results as the scalar forms).
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mul.rn.f32x2 rd, ra, rb;\n"
+      " mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mov.b64 rc, {%6, %7};\n"
+      " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 // RMSNorm with weights w (this lane's 8; nullptr: none), then NeoX rotation with the tables c / sn
 // (cos / sin of frequencies 4 hl .. 4 hl + 3; nullptr: none) of the 8 elements x held by this lane
 // (x[i] and x[4 + i] are elements 4 hl + i and 64 + 4 hl + i).  Explicit roundings (no contraction),
-// so the scale of an fp8 block computed here and recomputed elsewhere in the launch agree bit for bit.
+// so the scale of an fp8 block computed here and recomputed elsewhere in the launch agree bit for bit;
+// pairs of elements go through the packed f32x2 forms (half the instructions, the same bits).
 __device__ __forceinline__ void norm_rope(float eps, const float* w, const float* c, const float* sn,
                                           unsigned hmask, float* x) {
-  if (w) {
-    float ss = 0.f;
+  // v[0..1]: elements 4 hl .. 4 hl + 3, v[2..3]: 64 + 4 hl .. (pairs of x)
+  float2 v[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss = __fmaf_rn(x[i], x[i], ss);
+  for (int i = 0; i < 4; ++i) v[i] = make_float2(x[2 * i], x[2 * i + 1]);
+  if (w) {
+    float2 acc = mul2(v[0], v[0]);
+    acc = fma2(v[1], v[1], acc);
+    acc = fma2(v[2], v[2], acc);
+    acc = fma2(v[3], v[3], acc);
+    float ss = __fadd_rn(acc.x, acc.y);
     ss = half_sum(ss, hmask);
     const float inv = rsqrtf(ss / (float)HD + eps);
+    const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = __fmul_rn(__fmul_rn(x[i], inv), w[i]);
+    for (int i = 0; i < 4; ++i) v[i] = mul2(mul2(v[i], inv2), make_float2(w[2 * i], w[2 * i + 1]));
   }
   if (c) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float a = x[i], b = x[4 + i];
-      x[i] = __fmaf_rn(a, c[i], -__fmul_rn(b, sn[i]));
-      x[4 + i] = __fmaf_rn(b, c[i], __fmul_rn(a, sn[i]));
+    for (int i = 0; i < 2; ++i) {
+      const float2 cc = make_float2(c[2 * i], c[2 * i + 1]), ss2 = make_float2(sn[2 * i], sn[2 * i + 1]);
+      const float2 a = v[i], b = v[2 + i];
+      const float2 bs = mul2(b, ss2);
+      v[i] = fma2(a, cc, make_float2(-bs.x, -bs.y));  // a c - b s
+      v[2 + i] = fma2(b, cc, mul2(a, ss2));           // b c + a s
     }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = v[i].x;
+    x[2 * i + 1] = v[i].y;
   }
 }
 

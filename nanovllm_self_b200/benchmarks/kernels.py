@@ -28,7 +28,7 @@ from ..ops.cuda_ops import CudaOps
 NQ, NKV, D, HID, INTER, VOCAB = 32, 8, 128, 4096, 12288, 151936
 CASES = ("attn_decode", "attn_decode_fp8", "attn_prefill", "attn_prefill_mma", "attn_prefill_fp8",
          "attn_prefill_flash_attn", "gemm_prefill", "gemm_decode", "gemm_decode256", "gemm_gate_up_silu256", "qkv_post",
-         "qkv_post_fp8", "add_rmsnorm", "silu_mul", "sample", "lm_head_sample256", "lm_head_logits_sample256",
+         "qkv_post_fp8", "add_rmsnorm", "silu_mul", "sample", "qkv_post256", "lm_head_sample256", "lm_head_logits_sample256",
          "lm_head_sample256_t", "lm_head_logits_sample256_t", "lm_head_logits256")
 # Qwen3-8B decode GEMM shapes (n, k) for gemm_sweep: qkv, o_proj, gate_up, down_proj, lm_head
 DECODE_SHAPES = {"qkv": ((NQ + 2 * NKV) * D, HID), "o_proj": (HID, NQ * D), "gate_up": (2 * INTER, HID),
@@ -102,7 +102,7 @@ def build_case(name: str, ops: CudaOps, dev="cuda"):
     if name.startswith("qkv_post"):
         from ..ops.torch_ref import rope_cos_sin
         fp8 = name.endswith("fp8")
-        T = 16384
+        T = 256 if name == "qkv_post256" else 16384  # a 256-sequence decode step, or a prefill chunk
         qkv = torch.randn(T, (NQ + 2 * NKV) * D, device=dev).to(torch.bfloat16)
         nb = T // 256 + 1
         kdt = torch.float8_e4m3fn if fp8 else torch.bfloat16
