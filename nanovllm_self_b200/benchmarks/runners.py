@@ -6,7 +6,14 @@
 * ``decode_sweep`` - decode tok/s at batch sizes 1/8/32/128/256 with a fixed context (config 3);
 * ``kv_dtype``     - the same workload with bf16 and fp8 KV caches (``benchmark_kv_cache_dtype.py``);
 * ``prefix``       - the multi-turn agent prefix workload (config 4): prefix-hit rate and tok/s;
-* ``pd``           - P/D pool with Poisson arrivals (config 5): p50/p99 TTFT and TPOT.
+* ``pd``           - P/D pool with Poisson arrivals (config 5): p50/p99 TTFT and TPOT;
+* ``graph_matrix`` - decode with CUDA graphs against eager decode per batch size, with the graph bucket
+  each batch lands in (``benchmark_cuda_graph_matrix.py``, ``_compare.py``, ``_exact_buckets.py``);
+* ``mixed``        - mixed-length / shared-prefix regression: greedy outputs against the dense oracle for
+  every prefill-attention kernel x CUDA-graph combination, prefix-block reuse checked
+  (``benchmark_p0_mixed_workload.py``);
+* ``decode_vs_hf`` - this engine against the HuggingFace ``generate`` loop on the same random checkpoint
+  (``benchmark_decode.py``).
 Every driver prints one JSON line (rank 0 under ``torch.distributed.run`` for ``--tp`` > 1), with the
 SM clocks and throttle reasons sampled during its timed part.  Warm-up runs use different prompt
 token ids than the timed runs (same lengths), so no timed prefill is served from the prefix cache;
@@ -169,9 +176,156 @@ def pd(args) -> dict:
     return s
 
 
+def graph_matrix(args) -> dict:
+    """Decode with CUDA graphs against eager decode, per batch size (one engine of each kind)."""
+    from ..engine.model_runner import graph_buckets
+    batches = [int(b) for b in args.batches.split(",")]
+    graph_max = max(args.max_num_seqs, max(batches))
+    buckets = graph_buckets(graph_max)
+    timed = {}
+    for eager in (False, True):
+        llm = _llm(args, enforce_eager=eager, cuda_graph_max_bs=graph_max, max_num_seqs=graph_max)
+        vocab = llm.model_runner.arch.vocab_size
+        graphs = bool(getattr(llm.model_runner, "graphs", None))
+        for bs in batches:
+            rows = datasets.uniform_serving(bs, vocab, (args.prompt_len, args.prompt_len), (args.gen, args.gen), seed=bs)
+            warm = _fresh(rows, vocab, WARMUP_SEED + bs)
+            llm.generate([r["prompt_ids"] for r in warm], _sp(warm))
+            with _Timed(llm) as t:
+                m = llm.generate([r["prompt_ids"] for r in rows], _sp(rows), return_metrics=True)["metrics"]
+            n_full, ms_full = m["decode_steps"].get(bs, [0, 0.0])
+            timed[(eager, bs)] = {"graphs_captured": graphs, "decode_step_ms": ms_full, "decode_steps_timed": n_full,
+                                  "decode_tok_s": bs / (ms_full / 1e3) if ms_full > 0 else 0.0,
+                                  "tpot_ms_p50": m["tpot_ms_p50"], "e2e_tok_s": m["e2e_throughput_tok_s"],
+                                  "prefix_hit_blocks_timed": t.prefix_hits, "clocks": t.clocks}
+        llm.shutdown()
+        del llm
+        if torch.cuda.is_available():
+            torch.cuda.empty_cache()
+    points = []
+    for bs in batches:
+        g, e = timed[(False, bs)], timed[(True, bs)]
+        bucket = next((b for b in buckets if b >= bs), None)
+        points.append({"batch": bs, "bucket": bucket, "bucket_kind": "exact" if bucket == bs else "rounded_up",
+                       "graph": g, "eager": e,
+                       "graph_speedup": e["decode_step_ms"] / g["decode_step_ms"] if g["decode_step_ms"] > 0 else 0.0})
+    return {"bench": "graph_matrix", "model": args.model, "tp": args.tp, "prompt_len": args.prompt_len,
+            "gen": args.gen, "points": points}
+
+
+def _first_divergence(model, prompt, got, want):
+    """(index, oracle logit gap between its token and the engine's) of the first differing token."""
+    from ..models.reference import dense_logits
+    for i, (a, b) in enumerate(zip(got, want)):
+        if a != b:
+            ref = dense_logits(model, list(prompt) + list(got[:i]))
+            return i, float((ref[b] - ref[a]).item())
+    return None, 0.0
+
+
+def mixed(args) -> dict:
+    """Greedy outputs of mixed-length batches against the dense oracle, for every prefill-attention
+    kernel x CUDA-graph combination, and prefix-block reuse of a request sharing a long prefix."""
+    from ..models.reference import greedy_generate
+    cuda = str(args.device).startswith("cuda")
+    gen = args.gen
+    combos = [(k, g) for k in (("tcgen05", "mma") if cuda else ("torch",)) for g in ((True, False) if cuda else (False,))]
+    results, oracle = [], {}
+    for kernel, graph in combos:
+        llm = _llm(args, enforce_eager=not graph)
+        runner = llm.model_runner
+        if kernel != "torch":
+            runner.ops.prefill_tc = kernel == "tcgen05"
+        vocab, bs = runner.arch.vocab_size, runner.block_size
+        g = torch.Generator().manual_seed(7)
+        rand = lambda n: torch.randint(0, vocab, (n,), generator=g).tolist()  # noqa: E731
+        short = rand(24)
+        prefix = rand(2 * bs + 37)
+        cases = {"single_short": [short], "mixed_pair": [rand(9), rand(61)], "batch8_short": [short] * 8}
+        sp = SamplingParams(temperature=0.0, max_tokens=gen, ignore_eos=True)
+        for name, prompts in cases.items():
+            t0 = time.perf_counter()
+            outs = [o[len(p):] for o, p in zip(llm.generate(prompts, sp), prompts)]
+            wall = time.perf_counter() - t0
+            rows = []
+            for p, o in zip(prompts, outs):
+                key = tuple(p)
+                if key not in oracle:
+                    oracle[key] = greedy_generate(runner.model, p, gen) if args.tp == 1 else None
+                want = oracle[key]
+                idx, gap = _first_divergence(runner.model, p, o, want) if want is not None else (None, 0.0)
+                rows.append({"match": want == o if want is not None else None, "first_divergence": idx,
+                             "oracle_gap_at_divergence": gap})
+            results.append({"kernel": kernel, "cuda_graph": graph, "case": name, "batch": len(prompts), "gen": gen,
+                            "tok_s": len(prompts) * gen / wall, "rows": rows})
+        # shared long prefix: the second request must reuse every full block of the prefix
+        a, b = prefix + rand(17), prefix + rand(23)
+        llm.generate([a], sp)
+        hits0 = llm.block_manager.num_prefix_hit_blocks
+        out_b = llm.generate([b], sp)[0][len(b):]
+        hits = llm.block_manager.num_prefix_hit_blocks - hits0
+        if tuple(b) not in oracle:
+            oracle[tuple(b)] = greedy_generate(runner.model, b, gen) if args.tp == 1 else None
+        want = oracle[tuple(b)]
+        idx, gap = _first_divergence(runner.model, b, out_b, want) if want is not None else (None, 0.0)
+        results.append({"kernel": kernel, "cuda_graph": graph, "case": "shared_prefix", "batch": 1, "gen": gen,
+                        "prefix_hit_blocks": hits, "expected_hit_blocks": len(prefix) // bs,
+                        "rows": [{"match": want == out_b if want is not None else None, "first_divergence": idx,
+                                  "oracle_gap_at_divergence": gap}]})
+        llm.shutdown()
+        del llm
+        if cuda:
+            torch.cuda.empty_cache()
+    return {"bench": "mixed", "model": args.model, "tp": args.tp, "block_size": args.block_size, "results": results}
+
+
+def decode_vs_hf(args) -> dict:
+    """This engine against the HuggingFace generate loop, greedy, on one seeded random checkpoint."""
+    import tempfile
+    from .. import HFLLM
+    from ..models.configs import PRESETS
+    from ..models.loader import has_checkpoint, save_hf_checkpoint
+    arch = PRESETS[args.model]
+    path = args.checkpoint or os.path.join(tempfile.gettempdir(), f"nvb_hf_{args.model}_seed0")
+    if not has_checkpoint(path):
+        save_hf_checkpoint(arch, path, seed=0)
+    rows = datasets.uniform_serving(args.batch, arch.vocab_size, (args.prompt_len, args.prompt_len),
+                                    (args.gen, args.gen))
+    prompts = [r["prompt_ids"] for r in rows]
+    sp = SamplingParams(temperature=0.0, max_tokens=args.gen, ignore_eos=True)
+    llm = LLM(path, device=args.device, max_model_len=args.max_model_len, max_num_seqs=args.max_num_seqs,
+              block_size=args.block_size)
+    llm.generate([r["prompt_ids"] for r in _fresh(rows, arch.vocab_size, WARMUP_SEED)], sp)
+    t0 = time.perf_counter()
+    res = llm.generate(prompts, sp, return_metrics=True)
+    ours_s = time.perf_counter() - t0
+    ours = [o[len(p):] for o, p in zip(res["outputs"], prompts)]
+    llm.shutdown()
+    del llm
+    hf = HFLLM(path, device=args.device, eos_token_id=-1)
+    ids = torch.tensor(prompts, dtype=torch.long)
+    hf.generate(ids[:, :8], max_token=2, temperature=0.0)  # warm-up
+    if str(args.device).startswith("cuda"):
+        torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    out = hf.generate(ids, max_token=args.gen, temperature=0.0)
+    if str(args.device).startswith("cuda"):
+        torch.cuda.synchronize()
+    hf_s = time.perf_counter() - t0
+    theirs = out[:, ids.shape[1]:].tolist()
+    first = sum(a[:1] == b[:1] for a, b in zip(ours, theirs)) / len(ours)
+    agree = [next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), len(a)) for a, b in zip(ours, theirs)]
+    n = args.batch * args.gen
+    return {"bench": "decode_vs_hf", "model": args.model, "batch": args.batch, "prompt_len": args.prompt_len,
+            "gen": args.gen, "ours_tok_s": n / ours_s, "ours_device_tok_s": res["metrics"]["throughput_tok_s"],
+            "hf_tok_s": n / hf_s, "speedup": hf_s / ours_s, "first_token_agreement": first,
+            "mean_agreeing_prefix_tokens": sum(agree) / len(agree)}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("name", choices=["runtime", "decode_sweep", "kv_dtype", "prefix", "pd"])
+    ap.add_argument("name", choices=["runtime", "decode_sweep", "kv_dtype", "prefix", "pd", "graph_matrix", "mixed",
+                                     "decode_vs_hf"])
     ap.add_argument("--model", default="qwen3-8b")
     ap.add_argument("--device", default="cuda")
     ap.add_argument("--tp", type=int, default=1)
@@ -191,6 +345,7 @@ def main(argv=None):
     ap.add_argument("--num-decode", type=int, default=1)
     ap.add_argument("--pd-backend", default="ipc_push")
     ap.add_argument("--work-root", default="/tmp/nvb_pd")
+    ap.add_argument("--checkpoint", default=None, help="decode_vs_hf: HF checkpoint directory (written if empty)")
     args = ap.parse_args(argv)
     if args.name == "pd":
         # the pool launches its own worker processes (TP groups via torchrun): run it from one process

@@ -34,12 +34,18 @@ LLM_self = LLM
 class HFLLM:
     """Naive HuggingFace ``generate`` loop (reference ``llm_engine``, ``llm_engine.py:27-96``)."""
 
-    def __init__(self, model_path: str, device: str = "cuda", dtype=torch.bfloat16):
-        from transformers import AutoModelForCausalLM, AutoTokenizer
-        self.tokenizer = AutoTokenizer.from_pretrained(model_path)
-        self.model = AutoModelForCausalLM.from_pretrained(model_path, torch_dtype=dtype).to(device)
+    def __init__(self, model_path: str, device: str = "cuda", dtype=torch.bfloat16, eos_token_id: int | None = None):
+        """``eos_token_id``: stop token (default: the directory's tokenizer's; -1 never stops, for
+        checkpoints without a tokenizer)."""
+        from transformers import AutoModelForCausalLM
+        self.model = AutoModelForCausalLM.from_pretrained(model_path, dtype=dtype).to(device)
         self.device = device
-        self.eos_token_id = self.tokenizer.eos_token_id
+        self.tokenizer = None
+        if eos_token_id is None:
+            from transformers import AutoTokenizer
+            self.tokenizer = AutoTokenizer.from_pretrained(model_path)
+            eos_token_id = self.tokenizer.eos_token_id
+        self.eos_token_id = eos_token_id
 
     @torch.inference_mode()
     def generate(self, input_ids: torch.Tensor, max_token: int = 20, temperature: float = 0.8):
