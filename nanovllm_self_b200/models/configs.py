@@ -76,6 +76,11 @@ PRESETS = {
     "tiny": Qwen3Arch(vocab_size=1024, hidden_size=128, intermediate_size=384, num_hidden_layers=2,
                       num_attention_heads=4, num_key_value_heads=2, head_dim=32, max_position_embeddings=4096,
                       tie_word_embeddings=True, bos_token_id=1, eos_token_id=2, name="tiny"),
+    # Qwen3-8B's head ratio (32 query / 8 KV heads, here 16 / 8) at tiny size: shards down to TP8, where
+    # every rank keeps one KV head, as Qwen3-8B does at TP8.
+    "tiny-tp8": Qwen3Arch(vocab_size=1024, hidden_size=128, intermediate_size=512, num_hidden_layers=2,
+                          num_attention_heads=16, num_key_value_heads=8, head_dim=32, max_position_embeddings=4096,
+                          tie_word_embeddings=False, bos_token_id=1, eos_token_id=2, name="tiny-tp8"),
     # Same topology as tiny but with head_dim 128 so the GPU kernels (head_dim 128 only) run it.
     "tiny-gpu": Qwen3Arch(vocab_size=2048, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
                           num_attention_heads=4, num_key_value_heads=2, head_dim=128, max_position_embeddings=8192,

@@ -31,10 +31,10 @@ def _kw():
     return dict(device="cpu", dtype="fp32", block_size=16, max_model_len=256, num_blocks=64, comm_backend="nccl")
 
 
-def _worker(rank, world, port, out_path, temperature):
+def _worker(rank, world, port, out_path, temperature, model="tiny"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
-    llm = LLM("tiny", tensor_parallel_size=world, **_kw())
+    llm = LLM(model, tensor_parallel_size=world, **_kw())
     out = llm.generate(_prompts(), SamplingParams(temperature=temperature, max_tokens=12, ignore_eos=True))
     with open(f"{out_path}.{rank}", "w") as f:
         json.dump(out, f)
@@ -55,3 +55,16 @@ def test_tp2_equals_tp1_on_cpu(tmp_path, temperature):
     assert outs[0] == outs[1], "ranks disagree"
     if temperature == 0.0:
         assert outs[0] == ref
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_tp4_tp8_equal_tp1_on_cpu(tmp_path, world):
+    """Qwen3-8B's 2:1 query / KV head ratio sharded 4 and 8 ways (at TP8 one KV head per rank, the
+    layout of Qwen3-8B at TP8): greedy tokens equal the one-rank engine's."""
+    sp = SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True)
+    ref = LLM("tiny-tp8", **_kw()).generate(_prompts(), sp)
+    out_path = str(tmp_path / "tp")
+    mp.spawn(_worker, args=(world, _free_port(), out_path, 0.0, "tiny-tp8"), nprocs=world, join=True)
+    outs = [json.load(open(f"{out_path}.{r}")) for r in range(world)]
+    assert all(o == outs[0] for o in outs), "ranks disagree"
+    assert outs[0] == ref
