@@ -232,10 +232,8 @@ def mixed(args) -> dict:
     combos = [(k, g) for k in (("tcgen05", "mma") if cuda else ("torch",)) for g in ((True, False) if cuda else (False,))]
     results, oracle = [], {}
     for kernel, graph in combos:
-        llm = _llm(args, enforce_eager=not graph)
+        llm = _llm(args, enforce_eager=not graph, **({} if kernel == "torch" else {"prefill_attention": kernel}))
         runner = llm.model_runner
-        if kernel != "torch":
-            runner.ops.prefill_tc = kernel == "tcgen05"
         vocab, bs = runner.arch.vocab_size, runner.block_size
         g = torch.Generator().manual_seed(7)
         rand = lambda n: torch.randint(0, vocab, (n,), generator=g).tolist()  # noqa: E731

@@ -122,6 +122,10 @@ class EngineConfig:
     # Allocate the KV pool with cudaMalloc + CUDA IPC so another process can push blocks
     # into it (the decode side of the NVLink P/D push).
     kv_pool_ipc: bool = False
+    # Prefill attention kernel over bf16 KV: "tcgen05" (TMEM accumulators, the default) or "mma"
+    # (the mma.sync kernel, which fp8 KV always uses).  The reference's per-layer backend switch
+    # (nanovllm/layers/attention.py:58, forward_backend) made a config field.
+    prefill_attention: str = "tcgen05"
     extra: dict = field(default_factory=dict)
 
     def __post_init__(self):
@@ -132,6 +136,8 @@ class EngineConfig:
             raise ValueError(f"unsupported kv_cache_quant_mode: {self.kv_cache_quant_mode}")
         if self.comm_backend not in COMM_BACKENDS:
             raise ValueError(f"unsupported comm_backend: {self.comm_backend}")
+        if self.prefill_attention not in ("tcgen05", "mma"):
+            raise ValueError(f"unsupported prefill_attention: {self.prefill_attention}")
         kv = resolve_torch_dtype(self.kv_cache_dtype)
         if self.kv_cache_quant_mode == "int8_mock":
             kv = torch.int8

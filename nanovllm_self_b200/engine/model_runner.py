@@ -64,6 +64,8 @@ class ModelRunner:
             else:
                 random_init(self.model, seed=config.seed, std=config.init_std)
         self.ops = get_ops(self.device, config.use_custom_kernels)
+        if hasattr(self.ops, "prefill_tc"):
+            self.ops.prefill_tc = config.prefill_attention == "tcgen05"
         if config.deterministic and hasattr(self.ops, "C"):
             self.ops.C.gemm_set_deterministic(True)
         self.comm = comm
