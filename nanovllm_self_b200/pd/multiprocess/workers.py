@@ -78,6 +78,13 @@ def add_common_args(ap: argparse.ArgumentParser) -> None:
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel size of this worker (torchrun launch)")
     ap.add_argument("--gpu-offset", type=int, default=0, help="rank r of the group uses GPU gpu_offset + r")
     ap.add_argument("--comm-backend", default="fused")
+    # backpressure (reference persistent_prefill_worker.py:834-842, persistent_decode_worker.py:704-727)
+    ap.add_argument("--max-pending-sends", type=int, default=0,
+                    help="prefill: NCCL sends in flight before the worker completes them (0: no cap)")
+    ap.add_argument("--max-active-decode-requests", type=int, default=0,
+                    help="decode: requests admitted at once, restoring, pushed to or decoding (0: no cap)")
+    ap.add_argument("--max-pending-recvs", type=int, default=0,
+                    help="decode: NCCL receives in flight before new handoffs wait in the work directory (0: no cap)")
 
 
 def build_runner(args, kv_pool_ipc: bool = False) -> ModelRunner:
@@ -352,7 +359,9 @@ class PrefillWorker:
 
     def _next_command(self, idle_since: float, max_idle_s) -> dict:
         """Rank 0: what the group does next."""
-        self.finalize_pending_sends()
+        # at the send cap, complete the sends in flight before taking another request
+        cap = getattr(self.args, "max_pending_sends", 0)
+        self.finalize_pending_sends(block=cap > 0 and len(self.pending_sends) >= cap)
         for path in self.wd.glob("*.request.json"):
             if path.name in self.processed:
                 continue
@@ -536,10 +545,20 @@ class DecodeWorker:
             names += [p.name[:-len(".prefill_done")] for p in self.wd.glob("*.prefill_done")
                       if self.wd.exists(p.name[:-len(".prefill_done")] + ".payload.pkl")
                       or self.wd.exists(p.name[:-len(".prefill_done")] + ".payload.rank0.pkl")]
-        for base in names:
-            if base not in self.seen:
-                self.seen.add(base)
-                ops.append(("admit", base))
+        # admission caps: handoffs beyond them stay in the work directory until a slot frees up
+        cap = getattr(self.args, "max_active_decode_requests", 0)
+        recv_cap = getattr(self.args, "max_pending_recvs", 0)
+        in_flight = len(self.engine.active) + len(self.pending_push) + len(self.pending_recvs)
+        recvs = len(self.pending_recvs)
+        for base in sorted(names):
+            if base in self.seen:
+                continue
+            if (cap > 0 and in_flight >= cap) or (recv_cap > 0 and self.args.backend == "sync_gpu" and recvs >= recv_cap):
+                break
+            recvs += self.args.backend == "sync_gpu"
+            self.seen.add(base)
+            ops.append(("admit", base))
+            in_flight += 1
         for base, (payload, blocks, t0) in self.pending_push.items():
             done = [self.wd.exists(self._push_done_name(base, r)) for r in range(self.tp.size)]
             if all(done):

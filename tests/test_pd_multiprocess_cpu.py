@@ -125,3 +125,26 @@ def test_pool_tp2_groups_match_monolithic(tmp_path):
     got = {pool.submitted[b]["row"]["id"]: r["output_ids"] for b, r in pool.results.items()}
     assert got == want
     assert json.loads((tmp_path / "decode_0" / "worker_ready.json").read_text())["tp"] == 2
+
+
+@pytest.mark.parametrize("backend,caps", [("shared_memory", ["--max-active-decode-requests", "1"])])
+def test_backpressure_caps_throttle_without_losing_requests(tmp_path, backend, caps):
+    """With one admitted decode request at a time, a burst of requests still completes with the
+    monolithic engine's tokens: the handoffs beyond the cap wait in the work directory instead of
+    failing.  (The NCCL send / receive caps apply to the sync_gpu backend, which runs on GPUs.)"""
+    rows = _rows()
+    ref = LLM("tiny", device="cpu", dtype="fp32", block_size=16, num_blocks=64, max_model_len=256)
+    want = {r["id"]: ref.generate([r["prompt_ids"]], SamplingParams(temperature=0, max_tokens=r["max_tokens"],
+                                                                    ignore_eos=True))[0][len(r["prompt_ids"]):]
+            for r in rows}
+    pool = PDPool(tmp_path, 1, 1, backend, "tiny", prefill_devices=["cpu"], decode_devices=["cpu"],
+                  worker_args=ARGS + caps, handshake_timeout_s=60, nccl_port=29841)
+    pool.start()
+    try:
+        summary = pool.run(rows, concurrency=4, timeout_s=300)
+    finally:
+        pool.shutdown()
+    assert summary["num_errors"] == 0, pool.results
+    assert pool.exit_codes == [0, 0], pool.exit_codes
+    got = {pool.submitted[b]["row"]["id"]: r["output_ids"] for b, r in pool.results.items()}
+    assert got == want
