@@ -220,7 +220,7 @@ def main(argv=None):
             json.dump(results, f, indent=1)
         with open(args.out + ".jsonl", "w") as f:
             for r in per_request:
-                f.write(json.dumps({k: v for k, v in r.items() if k != "output_ids"}) + "\n")
+                f.write(json.dumps(r) + "\n")  # with output_ids: the correctness check compares them
 
 
 if __name__ == "__main__":

@@ -170,6 +170,23 @@ class PDPool:
                     done.append(base)
         return done
 
+    def request_rows(self) -> list:
+        """One row per finished request in the fields every P/D and single-engine driver
+        writes (``request_id``, token counts, ``ttft_s``/``tpot_s``/``e2e_s``, ``output_ids``,
+        or ``error``)."""
+        rows = []
+        for base, res in self.results.items():
+            row = self.submitted[base]["row"]
+            out = {"request_id": row.get("id", base), "session_id": row.get("session_id"),
+                   "input_tokens": len(row["prompt_ids"]), "max_tokens": row["max_tokens"]}
+            if "error" in res:
+                out["error"] = res["error"]
+            else:
+                out.update(output_tokens=len(res["output_ids"]), ttft_s=res["ttft_s"], tpot_s=res["tpot_s"],
+                           e2e_s=res["e2e_s"], output_ids=res["output_ids"])
+            rows.append(out)
+        return rows
+
     def dead_workers(self) -> list:
         """(role, index, exit code) of every worker process that has exited."""
         dead = []
@@ -255,7 +272,7 @@ def main(argv=None):
     ap.add_argument("--concurrency", type=int, default=4)
     ap.add_argument("--input-mean", type=float, default=2048)
     ap.add_argument("--output-mean", type=float, default=256)
-    ap.add_argument("--out", default=None)
+    ap.add_argument("--out", default=None, help="JSON summary path; per-request rows go to <out>.jsonl")
     ap.add_argument("--tp", type=int, default=1, help="each worker is a TP group of this many GPUs")
     args, rest = ap.parse_known_args(argv)
     rng = np.random.default_rng(0)
@@ -276,6 +293,9 @@ def main(argv=None):
     if args.out:
         with open(args.out, "w") as f:
             json.dump(summary, f, indent=1)
+        with open(args.out + ".jsonl", "w") as f:
+            for r in pool.request_rows():
+                f.write(json.dumps(r) + "\n")
 
 
 if __name__ == "__main__":
