@@ -345,6 +345,14 @@ class ModelRunner:
             return torch.empty(0, dtype=torch.int32, device=ids.device)
         return self.sample(logits, temps, topp)
 
+    @torch.inference_mode()
+    def logits(self, seqs: list[Sequence]) -> torch.Tensor:
+        """One eager step's logits, ``[rows that need logits, vocab shard]``, without sampling:
+        the KV cache is written as in :meth:`run`, the sequences' state is left unchanged."""
+        pk = self._pack(seqs)
+        ids, pos, ctx, _, _ = self._to_device(pk)
+        return self.model.forward(ids, pos, ctx, self.kv_layers, self.kv_scale_layers)
+
     def _fused_sampler_ok(self, ctx) -> bool:
         return (self.is_cuda and self.config.fused_sampler and self.tp.size == 1 and not self._use_top_p
                 and hasattr(self.ops, "lm_head_sample")
