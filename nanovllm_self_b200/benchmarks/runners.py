@@ -12,6 +12,9 @@
 * ``mixed``        - mixed-length / shared-prefix regression: greedy outputs against the dense oracle for
   every prefill-attention kernel x CUDA-graph combination, prefix-block reuse checked
   (``benchmark_p0_mixed_workload.py``);
+* ``prefill_matrix`` - TTFT, prefill and decode tok/s per prompt length x batch for every prefill-attention
+  kernel x CUDA-graph combination, with each combination's gain over the mma.sync kernel without graphs
+  (``benchmark_prefill_backends.py``, ``benchmark_prefill_graph_matrix.py``);
 * ``decode_vs_hf`` - this engine against the HuggingFace ``generate`` loop on the same random checkpoint
   (``benchmark_decode.py``).
 Every driver prints one JSON line (rank 0 under ``torch.distributed.run`` for ``--tp`` > 1), with the
@@ -213,6 +216,59 @@ def graph_matrix(args) -> dict:
             "gen": args.gen, "points": points}
 
 
+def _combos(cuda: bool) -> list:
+    """(prefill-attention kernel, CUDA graphs) pairs this device runs; the torch ops on CPU."""
+    return [(k, g) for k in (("tcgen05", "mma") if cuda else ("torch",)) for g in ((True, False) if cuda else (False,))]
+
+
+def _gain_pct(base, new, larger_is_better):
+    if not base:
+        return 0.0
+    return (new - base) / base * 100.0 if larger_is_better else (base - new) / base * 100.0
+
+
+def prefill_matrix(args) -> dict:
+    """Per (prompt length, batch): TTFT, prefill tok/s, ITL and decode tok/s under every prefill kernel x
+    graph combination (one engine per combination, fresh prompts for warm-up and timed runs), and each
+    combination's gain over the baseline combination (mma.sync prefill, eager; the torch ops on CPU)."""
+    cuda = str(args.device).startswith("cuda")
+    combos = _combos(cuda)
+    base_key = "mma_graph_off" if cuda else "torch_graph_off"
+    lens = [int(x) for x in args.prompt_lens.split(",")]
+    batches = [int(x) for x in args.prefill_batches.split(",")]
+    per = {}
+    for kernel, graph in combos:
+        key = f"{kernel}_graph_{'on' if graph else 'off'}"
+        llm = _llm(args, enforce_eager=not graph, **({} if kernel == "torch" else {"prefill_attention": kernel}))
+        vocab = llm.model_runner.arch.vocab_size
+        for n in lens:
+            for b in batches:
+                rows = datasets.uniform_serving(b, vocab, (n, n), (args.gen, args.gen), seed=31 * n + b)
+                warm = _fresh(rows, vocab, WARMUP_SEED + 31 * n + b)
+                llm.generate([r["prompt_ids"] for r in warm], _sp(warm))
+                with _Timed(llm) as t:
+                    m = llm.generate([r["prompt_ids"] for r in rows], _sp(rows), return_metrics=True)["metrics"]
+                ttft = m["ttft_ms_p50"]
+                per.setdefault((n, b), {})[key] = {
+                    "ttft_ms": ttft, "prefill_tok_s": b * n / (ttft / 1e3) if ttft > 0 else 0.0,
+                    "itl_ms": m["tpot_ms_p50"],
+                    "decode_tok_s": b / (m["tpot_ms_p50"] / 1e3) if m["tpot_ms_p50"] > 0 else 0.0,
+                    "e2e_tok_s": m["e2e_throughput_tok_s"], "prefix_hit_blocks_timed": t.prefix_hits,
+                    "clocks": t.clocks}
+        llm.shutdown()
+        del llm
+        if cuda:
+            torch.cuda.empty_cache()
+    cases = []
+    for (n, b), by in per.items():
+        base = by[base_key]
+        gains = {k: {"ttft_gain_pct": _gain_pct(base["ttft_ms"], v["ttft_ms"], False),
+                     "decode_gain_pct": _gain_pct(base["decode_tok_s"], v["decode_tok_s"], True)}
+                 for k, v in by.items() if k != base_key}
+        cases.append({"prompt_len": n, "batch": b, "gen": args.gen, "combos": by, "gain_vs_" + base_key: gains})
+    return {"bench": "prefill_matrix", "model": args.model, "tp": args.tp, "baseline": base_key, "cases": cases}
+
+
 def _first_divergence(model, prompt, got, want):
     """(index, oracle logit gap between its token and the engine's) of the first differing token."""
     from ..models.reference import dense_logits
@@ -229,7 +285,7 @@ def mixed(args) -> dict:
     from ..models.reference import greedy_generate
     cuda = str(args.device).startswith("cuda")
     gen = args.gen
-    combos = [(k, g) for k in (("tcgen05", "mma") if cuda else ("torch",)) for g in ((True, False) if cuda else (False,))]
+    combos = _combos(cuda)
     results, oracle = [], {}
     for kernel, graph in combos:
         llm = _llm(args, enforce_eager=not graph, **({} if kernel == "torch" else {"prefill_attention": kernel}))
@@ -323,7 +379,7 @@ def decode_vs_hf(args) -> dict:
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("name", choices=["runtime", "decode_sweep", "kv_dtype", "prefix", "pd", "graph_matrix", "mixed",
-                                     "decode_vs_hf"])
+                                     "prefill_matrix", "decode_vs_hf"])
     ap.add_argument("--model", default="qwen3-8b")
     ap.add_argument("--device", default="cuda")
     ap.add_argument("--tp", type=int, default=1)
@@ -336,6 +392,8 @@ def main(argv=None):
     ap.add_argument("--gen", type=int, default=64)
     ap.add_argument("--context", type=int, default=2048)
     ap.add_argument("--batches", default="1,8,32,128,256")
+    ap.add_argument("--prompt-lens", default="128,512,2048", help="prefill_matrix: prompt lengths")
+    ap.add_argument("--prefill-batches", default="1,8", help="prefill_matrix: batch sizes")
     ap.add_argument("--sessions", type=int, default=64)
     ap.add_argument("--num-requests", type=int, default=512)
     ap.add_argument("--rate", type=float, default=8.0)

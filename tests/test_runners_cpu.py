@@ -36,3 +36,14 @@ def test_decode_vs_hf_on_one_checkpoint(capsys, tmp_path):
     assert r["ours_tok_s"] > 0 and r["hf_tok_s"] > 0
     assert 0.0 <= r["first_token_agreement"] <= 1.0
     assert 0 <= r["mean_agreeing_prefix_tokens"] <= 4
+
+
+def test_prefill_matrix_reports_every_case(capsys):
+    r = _run(capsys, ["prefill_matrix", *BASE, "--prompt-lens", "8,40", "--prefill-batches", "1,3", "--gen", "3"])
+    assert r["baseline"] == "torch_graph_off"
+    assert sorted((c["prompt_len"], c["batch"]) for c in r["cases"]) == [(8, 1), (8, 3), (40, 1), (40, 3)]
+    for c in r["cases"]:
+        m = c["combos"]["torch_graph_off"]
+        assert m["ttft_ms"] > 0 and m["prefill_tok_s"] > 0 and m["decode_tok_s"] > 0
+        assert m["prefix_hit_blocks_timed"] == 0
+        assert c["gain_vs_torch_graph_off"] == {}
