@@ -11,6 +11,11 @@ Reference counterparts, restated for this framework's per-request rows:
   ``input_tokens``, ``output_tokens``, ``ttft_s``, ``tpot_s``, ``e2e_s``, ``output_ids``).
 * ``compare_synthetic_benchmark.py`` -- :func:`compare_summaries`: the P/D summary over the
   single-engine one (TTFT / TPOT percentiles, p90 end-to-end latency, throughput).
+* ``compare_agent_pd_pool_strategies.py`` / ``compare_agent_pd_strategies.py`` --
+  :func:`policy_report`: the routing policies' summaries (one :class:`~.pairs.PDPairs` or
+  :class:`~.pool.PDPool` run per policy) side by side, each over ``round_robin``
+  (throughput, TTFT, TPOT, p90 end-to-end), with affinity hits and the requests-per-pair
+  imbalance, and :func:`markdown_table` for the report.
 * ``check_pipeline_correctness.py:44-66`` -- :func:`check_correctness`: two runs' rows
   matched by request id; passed when both ran the same requests and every request's
   generated token ids are equal (times are never compared).  Used to check one KV backend,
@@ -21,6 +26,7 @@ Command line (rows are JSON lines, one per request; summaries are JSON)::
     python -m nanovllm_self_b200.pd.multiprocess.evaluation single --model qwen3-8b --out single.json
     python -m nanovllm_self_b200.pd.multiprocess.evaluation compare --single single.json --pd pd.json
     python -m nanovllm_self_b200.pd.multiprocess.evaluation correctness --left a.jsonl --right b.jsonl
+    python -m nanovllm_self_b200.pd.multiprocess.evaluation policies --summaries pairs.json --markdown p.md
 """
 from __future__ import annotations
 
@@ -119,6 +125,45 @@ def compare_summaries(single: dict, pd: dict) -> dict:
     return res
 
 
+def policy_report(summaries: list, baseline: str = "round_robin") -> dict:
+    """Each policy's summary next to the baseline policy's: latency and throughput, their ratios over
+    the baseline (``*_over_<baseline>``), affinity hit rate and the requests-per-pair imbalance
+    (largest pair over the mean; 1.0 is an even spread)."""
+    base = next((x for x in summaries if x.get("policy") == baseline), summaries[0])
+    bname = base.get("policy", baseline)
+    rows = []
+    for x in summaries:
+        per = x.get("requests_per_pair") or []
+        row = {"policy": x.get("policy"), "num_requests": x.get("num_requests"), "num_errors": x.get("num_errors")}
+        for k in ("output_tok_s", "ttft_ms_p50", "ttft_ms_p99", "tpot_ms_p50", "tpot_ms_p99", "e2e_s_p90",
+                  "affinity_hit_rate"):
+            row[k] = x.get(k)
+        row["requests_per_pair"] = per
+        row["pair_imbalance"] = max(per) / (sum(per) / len(per)) if per and sum(per) else None
+        for k in ("output_tok_s", "ttft_ms_p50", "tpot_ms_p50", "e2e_s_p90"):
+            a, b = base.get(k), x.get(k)
+            row[f"{k}_over_{bname}"] = b / a if a and b is not None else None
+        rows.append(row)
+    return {"baseline": bname, "policies": rows}
+
+
+def markdown_table(report: dict) -> str:
+    b = report["baseline"]
+    head = ["policy", "tok/s", f"tok/s / {b}", "TTFT p50 ms", "TTFT p99 ms", "TPOT p50 ms", "e2e p90 s",
+            "affinity hits", "pair imbalance", "errors"]
+
+    def f(v, fmt="{:.2f}"):
+        return "-" if v is None else fmt.format(v)
+    lines = ["| " + " | ".join(head) + " |", "|" + "---|" * len(head)]
+    for r in report["policies"]:
+        lines.append("| " + " | ".join([str(r["policy"]), f(r["output_tok_s"], "{:.1f}"),
+                                        f(r[f"output_tok_s_over_{b}"]), f(r["ttft_ms_p50"], "{:.1f}"),
+                                        f(r["ttft_ms_p99"], "{:.1f}"), f(r["tpot_ms_p50"]), f(r["e2e_s_p90"]),
+                                        f(r["affinity_hit_rate"]), f(r["pair_imbalance"]),
+                                        str(r["num_errors"])]) + " |")
+    return "\n".join(lines) + "\n"
+
+
 def _by_id(rows: list) -> dict:
     return {r["request_id"]: r for r in rows if not r.get("warmup")}
 
@@ -180,6 +225,11 @@ def main(argv=None):
     c.add_argument("--single", required=True)
     c.add_argument("--pd", required=True, help="summary JSON (a list takes its first entry)")
     c.add_argument("--out", default=None)
+    q = sub.add_parser("policies", help="routing policies side by side, each over round_robin")
+    q.add_argument("--summaries", nargs="+", required=True, help="summary JSON files (a list or one summary each)")
+    q.add_argument("--baseline", default="round_robin")
+    q.add_argument("--out", default=None)
+    q.add_argument("--markdown", default=None)
     k = sub.add_parser("correctness", help="per-request token equality of two runs' rows")
     k.add_argument("--left", required=True)
     k.add_argument("--right", required=True)
@@ -201,6 +251,14 @@ def main(argv=None):
         single = json.loads(Path(a.single).read_text())
         pd = json.loads(Path(a.pd).read_text())
         res = compare_summaries(single[0] if isinstance(single, list) else single, pd[0] if isinstance(pd, list) else pd)
+    elif a.cmd == "policies":
+        sums = []
+        for path in a.summaries:
+            x = json.loads(Path(path).read_text())
+            sums += x if isinstance(x, list) else [x]
+        res = policy_report(sums, a.baseline)
+        if a.markdown:
+            Path(a.markdown).write_text(markdown_table(res))
     else:
         res = check_correctness(read_rows(a.left), read_rows(a.right))
     print(json.dumps(res))

@@ -250,7 +250,8 @@ class PDPool:
         wall = time.time() - t0
         ok = [r for r in self.results.values() if "error" not in r]
         gen = sum(len(r["output_ids"]) for r in ok)
-        return {"num_requests": len(rows), "num_errors": len(self.results) - len(ok), "wall_s": wall,
+        return {"policy": self.p_router.policy, "num_requests": len(rows), "num_errors": len(self.results) - len(ok),
+                "wall_s": wall,
                 "output_tok_s": gen / wall if wall > 0 else 0.0,
                 "ttft_ms_p50": _pct([r["ttft_s"] * 1e3 for r in ok], 50),
                 "ttft_ms_p99": _pct([r["ttft_s"] * 1e3 for r in ok], 99),

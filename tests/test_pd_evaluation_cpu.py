@@ -107,3 +107,26 @@ def test_compare_summaries_ratios(tmp_path, capsys):
     (tmp_path / "p.json").write_text(json.dumps([pd]))
     ev.main(["compare", "--single", str(tmp_path / "s.json"), "--pd", str(tmp_path / "p.json")])
     assert json.loads(capsys.readouterr().out)["output_tok_s_pd_over_single"] == 1.5
+
+
+def test_policy_report_against_round_robin(tmp_path, capsys):
+    sums = [{"policy": "round_robin", "num_requests": 8, "num_errors": 0, "output_tok_s": 100.0, "ttft_ms_p50": 40.0,
+             "ttft_ms_p99": 90.0, "tpot_ms_p50": 5.0, "tpot_ms_p99": 6.0, "e2e_s_p90": 2.0,
+             "affinity_hit_rate": 0.25, "requests_per_pair": [4, 4]},
+            {"policy": "affinity_load_aware", "num_requests": 8, "num_errors": 0, "output_tok_s": 125.0,
+             "ttft_ms_p50": 30.0, "ttft_ms_p99": 70.0, "tpot_ms_p50": 5.0, "tpot_ms_p99": 6.5, "e2e_s_p90": 1.5,
+             "affinity_hit_rate": 0.75, "requests_per_pair": [6, 2]}]
+    rep = ev.policy_report(sums)
+    rr, aff = rep["policies"]
+    assert rep["baseline"] == "round_robin" and rr["output_tok_s_over_round_robin"] == 1.0
+    assert aff["output_tok_s_over_round_robin"] == 1.25 and aff["ttft_ms_p50_over_round_robin"] == 0.75
+    assert rr["pair_imbalance"] == 1.0 and aff["pair_imbalance"] == 1.5
+    md = ev.markdown_table(rep)
+    assert md.count("\n") == 4 and "| affinity_load_aware | 125.0 | 1.25 |" in md
+    (tmp_path / "a.json").write_text(json.dumps(sums[:1]))
+    (tmp_path / "b.json").write_text(json.dumps(sums[1]))
+    ev.main(["policies", "--summaries", str(tmp_path / "a.json"), str(tmp_path / "b.json"),
+             "--markdown", str(tmp_path / "p.md")])
+    assert [r["policy"] for r in json.loads(capsys.readouterr().out)["policies"]] == ["round_robin",
+                                                                                    "affinity_load_aware"]
+    assert (tmp_path / "p.md").read_text() == md
