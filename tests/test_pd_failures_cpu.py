@@ -200,3 +200,29 @@ def test_audit_reports_each_kind_of_leftover(tmp_path):
         proc.kill()
         proc.wait()
     assert not audit(tmp_path, shm_dir=tmp_path / "no_shm")["processes"]
+
+
+@pytest.mark.skipif(not hasattr(signal, "SIGSTOP"), reason="needs POSIX job-control signals")
+def test_stalled_decode_worker_times_out_then_recovers(tmp_path):
+    """A decode worker that stops answering (SIGSTOP) makes its request time out alone; once it
+    runs again (SIGCONT) it serves new requests and shuts down cleanly."""
+    pool = _pool(tmp_path)
+    pool.start()
+    dproc = pool.procs[1]
+    try:
+        os.kill(dproc.pid, signal.SIGSTOP)
+        try:
+            s = pool.run(_rows(1, seed=11), concurrency=1, timeout_s=120, request_timeout_s=5)
+        finally:
+            os.kill(dproc.pid, signal.SIGCONT)
+        assert s["num_errors"] == 1
+        assert "no completion within" in next(iter(pool.results.values()))["error"]
+        assert dproc.poll() is None  # stalled, not dead
+        n_before = len(pool.results)
+        s = pool.run(_rows(2, seed=12), concurrency=2, timeout_s=120, request_timeout_s=60)
+        new = list(pool.results.values())[n_before:]
+        assert len(new) == 2 and all("error" not in r for r in new), new
+    finally:
+        pool.shutdown()
+    assert all(c == 0 for c in pool.exit_codes), pool.exit_codes
+    assert not audit(tmp_path)["processes"]
