@@ -126,6 +126,9 @@ class EngineConfig:
     # (the mma.sync kernel, which fp8 KV always uses).  The reference's per-layer backend switch
     # (nanovllm/layers/attention.py:58, forward_backend) made a config field.
     prefill_attention: str = "tcgen05"
+    # Timeout of the tensor-parallel process group: a collective whose peer never joins (a rank
+    # that died or stalls between steps) ends with an error after this long instead of waiting.
+    dist_timeout_s: float = 600.0
     extra: dict = field(default_factory=dict)
 
     def __post_init__(self):

@@ -48,7 +48,7 @@ class LLMEngine:
         self.config = config
         self.enable_profile = enable_profile
         self.tracer = StepTracer(enabled=enable_profile)
-        self.tp = init_tensor_parallel(config.tensor_parallel_size, config.device)
+        self.tp = init_tensor_parallel(config.tensor_parallel_size, config.device, timeout_s=config.dist_timeout_s)
         self.comm = None
         if self.tp.size > 1:
             from ..parallel.comm import TPComm
