@@ -64,6 +64,7 @@ class PDPool:
         self.dwd = [WorkDir(self.root / f"decode_{i}") for i in range(num_decode)]
         self.submitted = {}
         self.results = {}
+        self.warmup_bases = set()
         self._seq = 0
 
     # ------------------------------------------------------------- lifecycle
@@ -179,6 +180,8 @@ class PDPool:
             row = self.submitted[base]["row"]
             out = {"request_id": row.get("id", base), "session_id": row.get("session_id"),
                    "input_tokens": len(row["prompt_ids"]), "max_tokens": row["max_tokens"]}
+            if base in self.warmup_bases:
+                out["warmup"] = True
             if "error" in res:
                 out["error"] = res["error"]
             else:
@@ -229,16 +232,19 @@ class PDPool:
         next_arrival = 0.0
         i = 0
         inflight = set()
+        mine = []  # this run's requests: the summary covers them only
         while i < len(rows) or inflight:
             now = time.time() - t0
             if i < len(rows):
                 if rate:
                     if now >= next_arrival:
-                        inflight.add(self.submit(rows[i], i, now))
+                        mine.append(self.submit(rows[i], i, now))
+                        inflight.add(mine[-1])
                         i += 1
                         next_arrival += rng.expovariate(rate)
                 elif len(inflight) < (concurrency or 1):
-                    inflight.add(self.submit(rows[i], i, now))
+                    mine.append(self.submit(rows[i], i, now))
+                    inflight.add(mine[-1])
                     i += 1
             for b in self._collect():
                 inflight.discard(b)
@@ -248,16 +254,23 @@ class PDPool:
                 raise TimeoutError("P/D pool run timed out")
             time.sleep(0.001)
         wall = time.time() - t0
-        ok = [r for r in self.results.values() if "error" not in r]
+        ok = [self.results[b] for b in mine if "error" not in self.results[b]]
         gen = sum(len(r["output_ids"]) for r in ok)
-        return {"policy": self.p_router.policy, "num_requests": len(rows), "num_errors": len(self.results) - len(ok),
+        return {"policy": self.p_router.policy, "num_requests": len(rows), "num_errors": len(mine) - len(ok),
                 "wall_s": wall,
                 "output_tok_s": gen / wall if wall > 0 else 0.0,
                 "ttft_ms_p50": _pct([r["ttft_s"] * 1e3 for r in ok], 50),
                 "ttft_ms_p99": _pct([r["ttft_s"] * 1e3 for r in ok], 99),
                 "tpot_ms_p50": _pct([r["tpot_s"] * 1e3 for r in ok], 50),
                 "tpot_ms_p99": _pct([r["tpot_s"] * 1e3 for r in ok], 99),
+                "e2e_s_p90": _pct([r["e2e_s"] for r in ok], 90),
                 "prefill_router": self.p_router.summary(), "decode_router": self.d_router.summary()}
+
+    def warmup(self, rows: list, concurrency: int = 1, timeout_s: float = 3600.0) -> None:
+        """Serve `rows` unmeasured; their rows carry ``warmup: true`` (the correctness check skips them)."""
+        before = set(self.submitted)
+        self.run(rows, concurrency=concurrency, timeout_s=timeout_s)
+        self.warmup_bases |= set(self.submitted) - before
 
 
 def main(argv=None):
@@ -275,19 +288,32 @@ def main(argv=None):
     ap.add_argument("--output-mean", type=float, default=256)
     ap.add_argument("--out", default=None, help="JSON summary path; per-request rows go to <out>.jsonl")
     ap.add_argument("--tp", type=int, default=1, help="each worker is a TP group of this many GPUs")
+    ap.add_argument("--prefill-gpus", default=None, help="TP = 1: GPU index of each prefill worker, e.g. 0,2")
+    ap.add_argument("--decode-gpus", default=None, help="TP = 1: GPU index of each decode worker, e.g. 1,3")
+    ap.add_argument("--load-mode", choices=["closed_loop", "batch"], default="closed_loop",
+                    help="closed_loop: --concurrency in flight (or Poisson at --rate); batch: every request at once")
+    ap.add_argument("--warmup", type=int, default=0, help="unmeasured requests served first")
     args, rest = ap.parse_known_args(argv)
-    rng = np.random.default_rng(0)
-    rows = []
-    for i in range(args.num_requests):
-        n_in = int(np.clip(rng.lognormal(np.log(args.input_mean), 0.5), 16, 8192))
-        n_out = int(np.clip(rng.lognormal(np.log(args.output_mean), 0.5), 4, 1024))
-        rows.append({"id": f"req-{i}", "prompt_ids": rng.integers(0, 151936, n_in).tolist(), "max_tokens": n_out,
-                     "input_tokens": n_in})
+    from .pairs import synthetic_rows
+    rows = synthetic_rows(args.num_requests + args.warmup, args.input_mean, args.output_mean,
+                          sessions=max(1, args.num_requests // 4), max_output=1024)
+    kw = {}
+    if args.prefill_gpus:
+        kw["prefill_devices"] = [f"cuda:{g}" for g in args.prefill_gpus.split(",")]
+        args.num_prefill = len(kw["prefill_devices"])
+    if args.decode_gpus:
+        kw["decode_devices"] = [f"cuda:{g}" for g in args.decode_gpus.split(",")]
+        args.num_decode = len(kw["decode_devices"])
     pool = PDPool(args.work_root, args.num_prefill, args.num_decode, args.backend, args.model, policy=args.policy,
-                  worker_args=rest, tp=args.tp)
+                  worker_args=rest, tp=args.tp, **kw)
     pool.start()
     try:
-        summary = pool.run(rows, concurrency=args.concurrency, rate=args.rate)
+        if args.warmup:
+            pool.warmup(rows[:args.warmup])
+        measured = rows[args.warmup:]
+        conc = len(measured) if args.load_mode == "batch" else args.concurrency
+        summary = pool.run(measured, concurrency=conc, rate=None if args.load_mode == "batch" else args.rate)
+        summary.update(load_mode=args.load_mode, warmup=args.warmup)
     finally:
         pool.shutdown()
     print(json.dumps(summary))

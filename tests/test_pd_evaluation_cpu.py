@@ -56,13 +56,18 @@ def test_pool_passes_correctness_against_single(tmp_path, capsys):
                   worker_args=ARGS, handshake_timeout_s=60, nccl_port=29861)
     pool.start()
     try:
+        warm = [dict(r, id="w-" + r["id"]) for r in rows[:2]]
+        pool.warmup(warm)
         pd_summary = pool.run(rows, concurrency=3, timeout_s=300)
     finally:
         pool.shutdown()
     pd_rows = pool.request_rows()
-    assert pd_summary["num_errors"] == 0 and len(pd_rows) == len(rows)
+    # the summary covers the measured run only; the warm-up rows are flagged and skipped by the check
+    assert pd_summary["num_errors"] == 0 and pd_summary["num_requests"] == len(rows)
+    assert len(pd_rows) == len(rows) + 2 and sum(r.get("warmup", False) for r in pd_rows) == 2
     res = ev.check_correctness(single, pd_rows)
     assert res["passed"] and res["num_common"] == len(rows), res
+    pd_rows = [r for r in pd_rows if not r.get("warmup")]
 
     # the same check through the command line, on the rows as files
     a, b = tmp_path / "single.jsonl", tmp_path / "pd.jsonl"
