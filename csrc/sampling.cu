@@ -237,14 +237,14 @@ cudaError_t launch_sample(const void* logits, int logits_is_bf16, int64_t ld, in
 //
 // Top-p (nucleus) without sorting: with z = logit / T, M = max z over the whole vocabulary
 // and d = M - z, the nucleus is {d < d*} for the smallest d* whose softmax mass reaches p.
-//   round 1: M (max over ranks);
-//   round 2: Z = sum exp(-d) and a histogram of exp(-d) over SAMPLE_NB bins of d in [0, 32)
+//   pass 1: M (max over ranks);
+//   pass 2: Z = sum exp(-d) and a histogram of exp(-d) over SAMPLE_NB bins of d in [0, 32)
 //            (bins of 1/32; columns beyond d = 32 carry < 1e-13 of the mass each);
-//   round 3: the bin where the cumulative mass crosses p Z is split again into SAMPLE_NB
+//   pass 3: the bin where the cumulative mass crosses p Z is split again into SAMPLE_NB
 //            sub-bins (resolution 1/32768 in d, a probability ratio of 1.00003: ties);
-//   round 4: Gumbel-max over the nucleus (argmax of z + g over d < d*), which samples the
+//   pass 4: Gumbel-max over the nucleus (argmax of z + g over d < d*), which samples the
 //            renormalised nucleus distribution, then the (score, token) pairs of the ranks.
-// Greedy and plain temperature rows skip rounds 1-3.
+// Greedy and plain temperature rows skip passes 1-3.
 namespace {
 
 __device__ __forceinline__ uint32_t sx_ld_acquire(const uint32_t* p) {
@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(1024) sample_rows_kernel(const T* __restrict__
       M = red[0];
       __syncthreads();
     }
-    // round 2: mass histogram over d = M - z in [0, 32)
+    // pass 2: mass histogram over d = M - z in [0, 32)
     for (int i = threadIdx.x; i <= SAMPLE_NB; i += blockDim.x) hist[i] = 0.f;
     __syncthreads();
     float zl = 0.f;
@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(1024) sample_rows_kernel(const T* __restrict__
     if (b1 >= SAMPLE_NB) {
       cut_d = 32.f;  // the mass reaches p only with the far tail: keep the whole window
     } else {
-      // round 3: split bin b1
+      // pass 3: split bin b1
       __syncthreads();
       for (int i = threadIdx.x; i < SAMPLE_NB; i += blockDim.x) hist[i] = 0.f;
       __syncthreads();

@@ -3,7 +3,7 @@
 Reference counterparts, restated for this framework's per-request rows:
 
 * ``pd_self/multiprocess/evaluation/benchmark_synthetic_single_gpu.py`` -- the synthetic
-  requests served by one monolithic engine, the baseline a P/D run is judged against.
+  requests served by one monolithic engine, the baseline a P/D run is compared with.
   Here :func:`run_single` drives :class:`~nanovllm_self_b200.engine.llm_engine.LLMEngine`
   through ``add_request`` / ``step`` with the same arrival process as the P/D drivers
   (closed loop at a concurrency, or Poisson at a rate), so both sides see the same load, and
