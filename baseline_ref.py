@@ -192,11 +192,15 @@ def run_reference_arm(args, workload, step_seed, ClockSampler, dist_info, reduce
     rank, world, local = dist_info()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    torch.cuda.set_device(local)
     if args.kv == "fp8":
         if rank == 0:
             unavailable("the reference has no fp8 KV cache (only int8_mock)")
         return
+    if not torch.cuda.is_available():
+        if rank == 0:
+            unavailable("no CUDA device on this machine (the reference runs on GPUs only)")
+        return
+    torch.cuda.set_device(local)
     try:
         path = ensure_checkpoint(args.model, 0, rank, f"cuda:{local}")
     except Exception as e:  # pragma: no cover - box dependent
