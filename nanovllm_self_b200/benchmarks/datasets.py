@@ -11,6 +11,14 @@
   config 4: 64 sessions, one 4096-token prefix, 4 turns of lognormal(512, 0.6) appends,
   128 output tokens per turn).
 All generators are seeded and return plain dict rows (``prompt_ids``, ``max_tokens`` ...).
+
+From the shell, each generator writes its rows as JSON lines plus a summary (row count, token
+totals and percentiles, rows per profile / session)::
+
+    python -m nanovllm_self_b200.benchmarks.datasets synthetic --per-profile 50 --out synth.jsonl
+    python -m nanovllm_self_b200.benchmarks.datasets sharegpt --input sg.json --model-path <ckpt> --out sg.jsonl
+    python -m nanovllm_self_b200.benchmarks.datasets agent --sessions 64 --out agent.jsonl
+    python -m nanovllm_self_b200.benchmarks.datasets uniform|pd --num-requests 256 --out rows.jsonl
 """
 from __future__ import annotations
 
@@ -108,3 +116,64 @@ def pd_lognormal(n: int, vocab: int = 151936, in_mean=2048, in_sigma=0.5, in_max
         rows.append({"id": f"pd{i}", "prompt_ids": rng.integers(0, vocab, li).tolist(), "max_tokens": lo,
                      "input_tokens": li})
     return rows
+
+
+def summarize(rows: list) -> dict:
+    """Row count, input / output token totals and percentiles, rows per profile and per session."""
+    ins = np.asarray([len(r["prompt_ids"]) for r in rows] or [0])
+    outs = np.asarray([r["max_tokens"] for r in rows] or [0])
+    pct = lambda a: {f"p{q}": float(np.percentile(a, q)) for q in (50, 90, 99)}  # noqa: E731
+    out = {"rows": len(rows), "input_tokens": int(ins.sum()), "output_tokens": int(outs.sum()),
+           "input_pct": pct(ins), "output_pct": pct(outs)}
+    for key in ("profile", "session_id"):
+        if rows and key in rows[0]:
+            counts: dict = {}
+            for r in rows:
+                counts[r[key]] = counts.get(r[key], 0) + 1
+            out[f"rows_per_{key}"] = counts
+    return out
+
+
+def main(argv=None) -> dict:
+    import argparse
+    ap = argparse.ArgumentParser(description="write a benchmark workload as JSON lines plus a summary")
+    ap.add_argument("kind", choices=["synthetic", "sharegpt", "agent", "uniform", "pd"])
+    ap.add_argument("--out", required=True, help="rows (JSON lines); the summary goes to <out>.summary.json")
+    ap.add_argument("--vocab", type=int, default=151936)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--per-profile", type=int, default=50, help="synthetic: rows per length profile")
+    ap.add_argument("--input", help="sharegpt: the ShareGPT JSON file")
+    ap.add_argument("--model-path", help="sharegpt: checkpoint directory whose tokenizer encodes the turns")
+    ap.add_argument("--max-rows", type=int, default=1000)
+    ap.add_argument("--max-tokens", type=int, default=256, help="sharegpt / agent: output tokens per row")
+    ap.add_argument("--sessions", type=int, default=64)
+    ap.add_argument("--turns", type=int, default=4)
+    ap.add_argument("--prefix-len", type=int, default=4096)
+    ap.add_argument("--num-requests", type=int, default=256)
+    a = ap.parse_args(argv)
+    if a.kind == "synthetic":
+        rows = length_matrix(a.per_profile, a.vocab, a.seed)
+    elif a.kind == "sharegpt":
+        if not (a.input and a.model_path):
+            raise SystemExit("sharegpt needs --input and --model-path (a tokenizer)")
+        from transformers import AutoTokenizer
+        tok = AutoTokenizer.from_pretrained(a.model_path)
+        rows = sharegpt_first_turns(a.input, lambda t: tok(t)["input_ids"], a.max_rows, a.max_tokens)
+    elif a.kind == "agent":
+        rows = agent_sessions(a.sessions, a.vocab, a.prefix_len, a.turns, output_tokens=a.max_tokens, seed=a.seed)
+    elif a.kind == "uniform":
+        rows = uniform_serving(a.num_requests, a.vocab, seed=a.seed)
+    else:
+        rows = pd_lognormal(a.num_requests, a.vocab, seed=a.seed)
+    with open(a.out, "w") as f:
+        for r in rows:
+            f.write(json.dumps(r) + "\n")
+    summary = dict(summarize(rows), kind=a.kind, seed=a.seed, path=a.out)
+    with open(a.out + ".summary.json", "w") as f:
+        json.dump(summary, f, indent=1)
+    print(json.dumps({k: v for k, v in summary.items() if not k.startswith("rows_per_session")}))
+    return summary
+
+
+if __name__ == "__main__":
+    main()

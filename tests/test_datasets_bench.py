@@ -37,3 +37,18 @@ def test_optimization_loop_picks_a_candidate():
                                                                "prefill_chunk_size": 8})])
     res = loop.run()
     assert res["best"]["candidate"] in ("default", "chunked") and len(res["results"]) == 2
+
+
+def test_dataset_cli_writes_rows_and_summary(tmp_path, capsys):
+    import json
+    out = str(tmp_path / "synth.jsonl")
+    s = datasets.main(["synthetic", "--per-profile", "3", "--vocab", "1000", "--out", out])
+    rows = [json.loads(x) for x in open(out)]
+    assert len(rows) == s["rows"] == 3 * len(datasets.PROFILES)
+    assert s["rows_per_profile"] == {p: 3 for p in datasets.PROFILES}
+    assert s["input_tokens"] == sum(len(r["prompt_ids"]) for r in rows)
+    assert json.load(open(out + ".summary.json"))["kind"] == "synthetic"
+    a = datasets.main(["agent", "--sessions", "2", "--turns", "3", "--prefix-len", "32", "--vocab", "500",
+                       "--out", str(tmp_path / "agent.jsonl")])
+    assert a["rows"] == 6 and a["rows_per_session_id"] == {"sess-0": 3, "sess-1": 3}
+    capsys.readouterr()
