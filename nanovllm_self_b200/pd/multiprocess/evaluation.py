@@ -220,6 +220,7 @@ def main(argv=None):
     s.add_argument("--output-mean", type=float, default=256)
     s.add_argument("--max-model-len", type=int, default=9216)
     s.add_argument("--block-size", type=int, default=256)
+    s.add_argument("--dataset", default=None, help="JSON-lines rows (benchmarks.datasets); default synthetic")
     s.add_argument("--out", default=None, help="summary JSON; rows go to <out>.jsonl")
     c = sub.add_parser("compare", help="P/D summary over the single-engine summary")
     c.add_argument("--single", required=True)
@@ -237,11 +238,14 @@ def main(argv=None):
     a = ap.parse_args(argv)
     if a.cmd == "single":
         from ...llm import LLM
-        from .pairs import synthetic_rows
+        from .pairs import load_rows, synthetic_rows
         from ...models.configs import resolve_arch
         llm = LLM(a.model, device=a.device, dtype=a.dtype, max_model_len=a.max_model_len, block_size=a.block_size)
         vocab = resolve_arch(a.model).vocab_size
-        rows = synthetic_rows(a.num_requests + a.warmup, a.input_mean, a.output_mean, vocab=vocab)
+        if a.dataset:
+            rows = load_rows(a.dataset, a.num_requests + a.warmup)
+        else:
+            rows = synthetic_rows(a.num_requests + a.warmup, a.input_mean, a.output_mean, vocab=vocab)
         res, out = run_single(llm, rows, a.concurrency, a.rate, a.warmup)
         res.update(model=a.model, device=a.device, dtype=a.dtype)
         if a.out:

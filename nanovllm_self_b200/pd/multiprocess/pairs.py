@@ -186,6 +186,23 @@ def synthetic_rows(n: int, input_mean: float = 2048, output_mean: float = 256, s
     return rows
 
 
+def load_rows(path, limit: int | None = None) -> list:
+    """Rows from a JSON-lines workload file (``benchmarks.datasets``), the first `limit` of them;
+    every row gets an ``id`` and ``input_tokens`` if it has none."""
+    rows = []
+    with open(path) as f:
+        for line in f:
+            if not line.strip():
+                continue
+            r = json.loads(line)
+            r.setdefault("id", f"req-{len(rows)}")
+            r.setdefault("input_tokens", len(r["prompt_ids"]))
+            rows.append(r)
+            if limit is not None and len(rows) >= limit:
+                break
+    return rows
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description="fixed P/D pairs / synthetic P/D pipeline benchmark")
     ap.add_argument("--work-root", required=True)
@@ -201,8 +218,12 @@ def main(argv=None):
     ap.add_argument("--output-mean", type=float, default=256)
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--out", default=None, help="JSON summary path; per-request rows go to <out>.jsonl")
+    ap.add_argument("--dataset", default=None, help="JSON-lines rows (benchmarks.datasets); default synthetic")
     args, rest = ap.parse_known_args(argv)
-    rows = synthetic_rows(args.num_requests + args.warmup, args.input_mean, args.output_mean)
+    if args.dataset:
+        rows = load_rows(args.dataset, args.num_requests + args.warmup)
+    else:
+        rows = synthetic_rows(args.num_requests + args.warmup, args.input_mean, args.output_mean)
     pairs = PDPairs(args.work_root, args.pairs, args.backend, args.model, worker_args=rest, tp=args.tp)
     pairs.start()
     results, per_request = [], []

@@ -293,10 +293,14 @@ def main(argv=None):
     ap.add_argument("--load-mode", choices=["closed_loop", "batch"], default="closed_loop",
                     help="closed_loop: --concurrency in flight (or Poisson at --rate); batch: every request at once")
     ap.add_argument("--warmup", type=int, default=0, help="unmeasured requests served first")
+    ap.add_argument("--dataset", default=None, help="JSON-lines rows (benchmarks.datasets); default synthetic")
     args, rest = ap.parse_known_args(argv)
-    from .pairs import synthetic_rows
-    rows = synthetic_rows(args.num_requests + args.warmup, args.input_mean, args.output_mean,
-                          sessions=max(1, args.num_requests // 4), max_output=1024)
+    from .pairs import load_rows, synthetic_rows
+    if args.dataset:
+        rows = load_rows(args.dataset, args.num_requests + args.warmup)
+    else:
+        rows = synthetic_rows(args.num_requests + args.warmup, args.input_mean, args.output_mean,
+                              sessions=max(1, args.num_requests // 4), max_output=1024)
     kw = {}
     if args.prefill_gpus:
         kw["prefill_devices"] = [f"cuda:{g}" for g in args.prefill_gpus.split(",")]

@@ -135,3 +135,20 @@ def test_policy_report_against_round_robin(tmp_path, capsys):
     assert [r["policy"] for r in json.loads(capsys.readouterr().out)["policies"]] == ["round_robin",
                                                                                     "affinity_load_aware"]
     assert (tmp_path / "p.md").read_text() == md
+
+
+def test_single_runs_a_prepared_dataset(tmp_path, capsys):
+    from nanovllm_self_b200.benchmarks import datasets
+    from nanovllm_self_b200.pd.multiprocess.pairs import load_rows
+    path = str(tmp_path / "u.jsonl")
+    datasets.main(["uniform", "--num-requests", "5", "--vocab", "1024", "--out", path])
+    rows = load_rows(path, 3)
+    assert len(rows) == 3 and all(r["input_tokens"] == len(r["prompt_ids"]) for r in rows)
+    capsys.readouterr()
+    out = str(tmp_path / "single.json")
+    ev.main(["single", "--model", "tiny", "--device", "cpu", "--dtype", "fp32", "--max-model-len", "2048",
+             "--block-size", "16", "--dataset", path, "--num-requests", "2", "--warmup", "1", "--concurrency", "2",
+             "--out", out])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["num_requests"] == 2 and res["num_errors"] == 0
+    assert [r["request_id"] for r in ev.read_rows(out + ".jsonl")] != []
