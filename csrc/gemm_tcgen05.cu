@@ -945,10 +945,11 @@ int num_sms() {
 
 template <int BN>
 int max_active_clusters(int splits) {
-  // CTAs of `splits`-wide clusters that can be resident at once (cached per size).
-  static int cache[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  // CTAs of `splits`-wide clusters that can be resident at once (cached per size; atomic entries,
+  // so threads that query at the same time only ever store the same value).
+  static std::atomic<int> cache[9];
   if (splits < 2 || splits > 8) return 0;
-  if (cache[splits]) return cache[splits];
+  if (int c = cache[splits].load(std::memory_order_relaxed)) return c;
   constexpr int STAGES = stages_for<BN>();
   constexpr int SMEM = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
   auto kern = gemm_cluster_kernel<BN, STAGES>;
@@ -972,8 +973,8 @@ int max_active_clusters(int splits) {
     cudaGetLastError();
     n = num_sms() / splits;
   }
-  cache[splits] = n * splits;
-  return cache[splits];
+  cache[splits].store(n * splits, std::memory_order_relaxed);
+  return n * splits;
 }
 
 int cluster_capacity(int bn, int splits) {
