@@ -933,12 +933,14 @@ cudaError_t run(const CUtensorMap& mp, const CUtensorMap& mq, const Params& prm,
 }
 
 int num_sms() {
-  static int n = 0;
+  static std::atomic<int> cached{0};
+  int n = cached.load(std::memory_order_relaxed);
   if (!n) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (n <= 0) n = 148;
+    cached.store(n, std::memory_order_relaxed);
   }
   return n;
 }

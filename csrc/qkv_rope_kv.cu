@@ -12,6 +12,7 @@
 // a block sets that block-head's scale to absmax(first token) * 4 / 448; other tokens
 // use it.  A token whose block's first token is written in the same launch recomputes
 // that first token's values to derive the identical scale (no inter-CTA ordering).
+#include <atomic>
 #include "common.cuh"
 #include "kernels.h"
 
@@ -419,22 +420,22 @@ cudaError_t launch_qkv_post(const void* qkv, int64_t qkv_stride, void* q_out, co
   if (e != cudaSuccess) return e;
   // resident CTAs per SM (registers and shared memory), once per device and stage size: the grid
   // is one wave, every CTA loops over its chunks
-  static int occ_smem[64], occ_ctas[64], occ_sms[64];
+  // one word per device, (smem << 32) | (SMs << 16) | CTAs per SM, so a reader never sees a
+  // mix of two entries
+  static std::atomic<uint64_t> occ[64];
   int dev = 0;
   cudaGetDevice(&dev);
   int sms = 0, per_sm = 0;
-  if (dev >= 0 && dev < 64 && occ_smem[dev] == smem) {
-    sms = occ_sms[dev];
-    per_sm = occ_ctas[dev];
+  const uint64_t w = dev >= 0 && dev < 64 ? occ[dev].load(std::memory_order_relaxed) : 0;
+  if (w && (int)(w >> 32) == smem) {
+    sms = (int)((w >> 16) & 0xffff);
+    per_sm = (int)(w & 0xffff);
   } else {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qkv_post_kernel, QKV_THREADS, (size_t)smem);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) {
-      occ_sms[dev] = sms;
-      occ_ctas[dev] = per_sm;
-      occ_smem[dev] = smem;
-    }
+    if (dev >= 0 && dev < 64 && sms > 0 && sms < 65536 && per_sm > 0 && per_sm < 65536)
+      occ[dev].store(((uint64_t)smem << 32) | ((uint64_t)sms << 16) | (uint64_t)per_sm, std::memory_order_relaxed);
   }
   if (sms <= 0) sms = 148;
   if (per_sm <= 0) per_sm = 1;
