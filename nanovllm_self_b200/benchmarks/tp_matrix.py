@@ -13,7 +13,11 @@ sharding actually divides the model: ``weight_shard_ratio`` = TP x the largest r
 bytes / TP = 1's weight bytes (1.0 when everything is sharded; the replicated norms put it a
 little above), and the same for the KV pool per block.
 
-Run every size with one command per size, then the summary::
+Every size and the summary in one command (TP > 1 sizes through ``torch.distributed.run``)::
+
+    python -m nanovllm_self_b200.benchmarks.tp_matrix matrix --result-dir /tmp/tpm --tps 1,2,4 --model qwen3-8b
+
+or one command per size, then the summary::
 
     python -m nanovllm_self_b200.benchmarks.tp_matrix run --result-dir /tmp/tpm --model qwen3-8b
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m nanovllm_self_b200.benchmarks.tp_matrix \\
@@ -114,32 +118,79 @@ def summarize(result_dir, tps=(1, 2, 4)) -> dict:
     return summary
 
 
+RUN_OPTS = ("model", "device", "dtype", "max_tokens", "max_model_len", "block_size", "num_blocks", "kv")
+
+
+def run_matrix(result_dir, tps, run_argv: list, timeout_s: float = 3600.0, port: int = 29871) -> dict:
+    """Each TP size as its own job (TP = 1 in one process, larger sizes under
+    ``torch.distributed.run`` on 127.0.0.1), then :func:`summarize`."""
+    import subprocess
+    import sys
+    for tp in tps:
+        mod = ["-m", "nanovllm_self_b200.benchmarks.tp_matrix", "run", "--result-dir", str(result_dir), *run_argv]
+        if tp > 1:
+            cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={tp}",
+                   "--master-addr", "127.0.0.1", f"--master-port={port + tp}", *mod]
+        else:
+            cmd = [sys.executable, *mod]
+        subprocess.run(cmd, check=True, timeout=timeout_s)
+    return summarize(result_dir, tuple(tps))
+
+
+def _run_args(p):
+    p.add_argument("--model", default="qwen3-8b")
+    p.add_argument("--device", default="cuda")
+    p.add_argument("--dtype", default="bf16")
+    p.add_argument("--max-tokens", type=int, default=16)
+    p.add_argument("--max-model-len", type=int, default=4096)
+    p.add_argument("--block-size", type=int, default=256)
+    p.add_argument("--num-blocks", type=int, default=-1, help="-1 sizes the KV pool from free memory")
+    p.add_argument("--kv", default="none", help="kv_cache_quant_mode")
+
+
+def _print_summary(res) -> None:
+    print(json.dumps({tp: {k: c[k] for k in ("matches_tp1", "weight_shard_ratio", "kv_block_shard_ratio",
+                                              "max_memory_allocated_mb_per_rank")}
+                      for tp, c in res["cases"].items()}))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description="TP consistency / per-rank memory matrix")
     sub = ap.add_subparsers(dest="cmd", required=True)
     r = sub.add_parser("run", help="one TP size (launch with torchrun for TP > 1)")
     r.add_argument("--result-dir", required=True)
-    r.add_argument("--model", default="qwen3-8b")
-    r.add_argument("--device", default="cuda")
-    r.add_argument("--dtype", default="bf16")
-    r.add_argument("--max-tokens", type=int, default=16)
-    r.add_argument("--max-model-len", type=int, default=4096)
-    r.add_argument("--block-size", type=int, default=256)
-    r.add_argument("--kv", default="none", help="kv_cache_quant_mode")
+    _run_args(r)
+    m = sub.add_parser("matrix", help="every TP size, each as its own job, then the summary")
+    m.add_argument("--result-dir", required=True)
+    m.add_argument("--tps", default="1,2,4")
+    _run_args(m)
     s = sub.add_parser("summary", help="compare the sizes written so far")
     s.add_argument("--result-dir", required=True)
     s.add_argument("--tps", default="1,2,4")
     a = ap.parse_args(argv)
     if a.cmd == "run":
         rec = run_case(a.result_dir, a.model, a.max_tokens, device=a.device, dtype=a.dtype,
-                       max_model_len=a.max_model_len, block_size=a.block_size, kv_cache_quant_mode=a.kv)
+                       max_model_len=a.max_model_len, block_size=a.block_size, num_blocks=a.num_blocks,
+                       kv_cache_quant_mode=a.kv, comm_backend="nccl" if a.device == "cpu" else "fused")
         if rec is not None:
-            print(json.dumps({k: v for k, v in rec.items() if k != "rank_memory"}))
+            print(json.dumps({k: v for k, v in rec.items() if k != "rank_memory"}), flush=True)
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            os._exit(0)  # the group is not torn down at exit: gloo's destructor can race its own threads
+        return
+    if a.cmd == "matrix":
+        run_argv = []
+        for k in RUN_OPTS:
+            run_argv += [f"--{k.replace('_', '-')}", str(getattr(a, k))]
+        res = run_matrix(a.result_dir, [int(x) for x in a.tps.split(",")], run_argv)
+        _print_summary(res)
+        if not res["all_match"]:
+            raise SystemExit(1)
+        return
     else:
         res = summarize(a.result_dir, tuple(int(x) for x in a.tps.split(",")))
-        print(json.dumps({tp: {k: c[k] for k in ("matches_tp1", "weight_shard_ratio", "kv_block_shard_ratio",
-                                                  "max_memory_allocated_mb_per_rank")}
-                          for tp, c in res["cases"].items()}))
+        _print_summary(res)
         if not res["all_match"]:
             raise SystemExit(1)
 

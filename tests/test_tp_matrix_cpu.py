@@ -46,3 +46,13 @@ def test_tp_matrix_tokens_and_shards(tmp_path, capsys):
         assert abs(c["kv_block_shard_ratio"] - 1.0) < 1e-9
         assert len(set(c["weight_mb_per_rank"])) == 1  # every rank holds the same share
         assert [m["rank"] for m in c["rank_memory"]] == list(range(int(tp)))
+
+
+def test_matrix_command_runs_each_size_as_its_own_job(tmp_path, capsys):
+    """The one-command form: TP 1 in-process and TP 2 under torch.distributed.run (gloo on CPU)."""
+    tp_matrix.main(["matrix", "--result-dir", str(tmp_path), "--tps", "1,2", "--model", "tiny-tp8", "--device",
+                    "cpu", "--dtype", "fp32", "--max-tokens", "6", "--max-model-len", "256", "--block-size", "16",
+                    "--num-blocks", "32"])
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert out["1"]["matches_tp1"] and out["2"]["matches_tp1"]
+    assert abs(out["2"]["kv_block_shard_ratio"] - 1.0) < 1e-9
