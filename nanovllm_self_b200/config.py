@@ -129,6 +129,9 @@ class EngineConfig:
     # Timeout of the tensor-parallel process group: a collective whose peer never joins (a rank
     # that died or stalls between steps) ends with an error after this long instead of waiting.
     dist_timeout_s: float = 600.0
+    # Append every generate call's metrics (the ``return_metrics`` dict without the block-usage
+    # snapshot, plus a timestamp) as one JSON line to this file; rank 0 only.
+    metrics_path: str | None = None
     extra: dict = field(default_factory=dict)
 
     def __post_init__(self):

@@ -176,7 +176,7 @@ class LLMEngine:
         if self.enable_profile:
             self.tracer.print_summary()
         outputs = [s.token_ids for s in seqs]
-        if not return_metrics:
+        if not return_metrics and not self.config.metrics_path:
             return outputs
         gen = sum(s.num_completion_tokens for s in seqs)
         total_s = dev_ms_total / 1e3 if self.model_runner.is_cuda else wall
@@ -204,6 +204,14 @@ class LLMEngine:
         }
         if self.enable_profile:
             metrics["profile"] = self.tracer.summary()
+        if self.config.metrics_path and self.tp.rank == 0:
+            import json
+            row = {k: v for k, v in metrics.items() if k != "block_usage"}
+            row["decode_steps"] = {str(b): v for b, v in row["decode_steps"].items()}
+            with open(self.config.metrics_path, "a") as f:
+                f.write(json.dumps(dict(row, time=time.time()), default=str) + "\n")
+        if not return_metrics:
+            return outputs
         return {"outputs": outputs, "metrics": metrics}
 
     def shutdown(self):

@@ -118,3 +118,16 @@ def test_profile_summary_and_nvtx_off(capsys):
     assert prof["steps"] == prof["prefill_steps"] + prof["decode_steps"] and prof["decode_steps"] >= 3
     assert prof["host_run_ms"] > 0
     assert "[PROFILE]" in capsys.readouterr().out
+
+
+def test_metrics_jsonl_appends_one_line_per_generate(prompts, tmp_path):
+    import json
+    path = tmp_path / "m.jsonl"
+    llm = _llm(metrics_path=str(path))
+    sp = SamplingParams(temperature=0, max_tokens=4, ignore_eos=True)
+    out = llm.generate(prompts[:2], sp)
+    assert isinstance(out, list) and len(out) == 2  # return type unchanged without return_metrics
+    res = llm.generate(prompts[:1], sp, return_metrics=True)
+    rows = [json.loads(x) for x in path.read_text().splitlines()]
+    assert [r["num_seqs"] for r in rows] == [2, 1] and [r["generated_tokens"] for r in rows] == [8, 4]
+    assert rows[1]["throughput_tok_s"] == res["metrics"]["throughput_tok_s"] and "time" in rows[1]
