@@ -60,7 +60,13 @@ def main(argv=None) -> list:
         from .llm import HFLLM
         if not os.path.isdir(a.model):
             raise SystemExit("--hf needs a checkpoint directory")
-        hf = HFLLM(a.model, device=a.device)
+        import glob
+        has_tok = bool(glob.glob(os.path.join(a.model, "tokenizer*")))
+        if a.prompt and not has_tok:
+            raise SystemExit("text prompts need a tokenizer in the checkpoint directory; give --prompt-ids")
+        dt = {"fp32": torch.float32, "fp16": torch.float16}.get(a.dtype, torch.bfloat16)
+        # without a tokenizer there is no EOS id: -1 never stops
+        hf = HFLLM(a.model, device=a.device, dtype=dt, eos_token_id=None if has_tok else -1)
         prompts = ids + [list(hf.tokenizer(p)["input_ids"]) for p in a.prompt]
         for p in prompts:
             out = hf.generate(torch.tensor([p], device=a.device), max_token=a.max_tokens,

@@ -37,3 +37,15 @@ def test_module_entry_point_runs():
     bad = subprocess.run([sys.executable, "-m", "nanovllm_self_b200", *BASE], cwd=ROOT, capture_output=True,
                          text=True, timeout=300)
     assert bad.returncode != 0 and "--prompt" in bad.stderr
+
+
+def test_hf_loop_on_a_checkpoint_without_tokenizer(tmp_path):
+    import torch
+
+    from nanovllm_self_b200.models.configs import PRESETS
+    from nanovllm_self_b200.models.loader import save_hf_checkpoint
+    path = str(tmp_path / "ckpt")
+    save_hf_checkpoint(PRESETS["tiny"], path, seed=0, dtype=torch.float32)
+    res = main(["--model", path, "--device", "cpu", "--dtype", "fp32", "--max-tokens", "4", "--hf",
+                "--prompt-ids", "5,17,300,9,44"])
+    assert len(res) == 1 and len(res[0]["output_ids"]) == 4 and all(0 <= t < 1024 for t in res[0]["output_ids"])
